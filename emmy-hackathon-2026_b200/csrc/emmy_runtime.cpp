@@ -1,0 +1,516 @@
+// emmy_runtime.cpp -- native runtime behind include/emmy_b200.h.
+//
+// Replaces the reference's runners (hosted `POST /compile` + `POST /run`,
+// reference docs/API.md:12-53, and the ctypes driver-API script
+// reference tools/harness/gpu_run.py:46-103) with one C-ABI library:
+//   * PTX -> cubin in-process through nvPTXCompiler (the ptxas of the toolkit);
+//   * the CUDA driver API through dlopen("libcuda.so.1"), resolved lazily so
+//     the library loads and assembles on machines without a GPU;
+//   * launches under meta.json geometry, optional cluster dims, tensor maps,
+//     event timing with L2 eviction between launches.
+#include "../../include/emmy_b200.h"
+
+#include <cuda.h>
+#include <dlfcn.h>
+#include <nvPTXCompiler.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+// ---------------------------------------------------------------------------
+// driver API table
+// ---------------------------------------------------------------------------
+struct Driver {
+  void *lib = nullptr;
+  bool inited = false;
+  CUresult (*Init)(unsigned);
+  CUresult (*GetErrorString)(CUresult, const char **);
+  CUresult (*DeviceGetCount)(int *);
+  CUresult (*DeviceGet)(CUdevice *, int);
+  CUresult (*DevicePrimaryCtxRetain)(CUcontext *, CUdevice);
+  CUresult (*CtxSetCurrent)(CUcontext);
+  CUresult (*CtxGetCurrent)(CUcontext *);
+  CUresult (*ModuleLoadData)(CUmodule *, const void *);
+  CUresult (*ModuleUnload)(CUmodule);
+  CUresult (*ModuleGetFunction)(CUfunction *, CUmodule, const char *);
+  CUresult (*ModuleGetGlobal)(CUdeviceptr *, size_t *, CUmodule, const char *);
+  CUresult (*FuncGetAttribute)(int *, CUfunction_attribute, CUfunction);
+  CUresult (*FuncSetAttribute)(CUfunction, CUfunction_attribute, int);
+  CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned,
+                           unsigned, unsigned, CUstream, void **, void **);
+  CUresult (*LaunchKernelEx)(const CUlaunchConfig *, CUfunction, void **, void **);
+  CUresult (*TensorMapEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  CUresult (*MemAlloc)(CUdeviceptr *, size_t);
+  CUresult (*MemFree)(CUdeviceptr);
+  CUresult (*MemsetD8Async)(CUdeviceptr, unsigned char, size_t, CUstream);
+  CUresult (*MemcpyHtoDAsync)(CUdeviceptr, const void *, size_t, CUstream);
+  CUresult (*MemcpyDtoHAsync)(void *, CUdeviceptr, size_t, CUstream);
+  CUresult (*StreamSynchronize)(CUstream);
+  CUresult (*EventCreate)(CUevent *, unsigned);
+  CUresult (*EventDestroy)(CUevent);
+  CUresult (*EventRecord)(CUevent, CUstream);
+  CUresult (*EventSynchronize)(CUevent);
+  CUresult (*EventElapsedTime)(float *, CUevent, CUevent);
+};
+
+Driver g_drv;
+std::mutex g_drv_mu;
+
+template <class F>
+bool sym(void *lib, F &fp, const char *name) {
+  fp = reinterpret_cast<F>(dlsym(lib, name));
+  return fp != nullptr;
+}
+
+int cuerr(CUresult r, const char *what) {
+  const char *s = nullptr;
+  if (g_drv.GetErrorString) g_drv.GetErrorString(r, &s);
+  return fail(static_cast<int>(r), "%s: CUresult %d (%s)", what, static_cast<int>(r),
+              s ? s : "?");
+}
+
+#define CU(call, what)                              \
+  do {                                              \
+    CUresult _r = (call);                           \
+    if (_r != CUDA_SUCCESS) return cuerr(_r, what); \
+  } while (0)
+
+int driver() {
+  std::lock_guard<std::mutex> lk(g_drv_mu);
+  if (g_drv.inited) return 0;
+  if (!g_drv.lib) {
+    g_drv.lib = dlopen("libcuda.so.1", RTLD_NOW | RTLD_GLOBAL);
+    if (!g_drv.lib) return fail(EMMY_ENODRIVER, "libcuda.so.1 not loadable: %s", dlerror());
+  }
+  void *l = g_drv.lib;
+  bool ok = sym(l, g_drv.Init, "cuInit") && sym(l, g_drv.GetErrorString, "cuGetErrorString") &&
+            sym(l, g_drv.DeviceGetCount, "cuDeviceGetCount") &&
+            sym(l, g_drv.DeviceGet, "cuDeviceGet") &&
+            sym(l, g_drv.DevicePrimaryCtxRetain, "cuDevicePrimaryCtxRetain") &&
+            sym(l, g_drv.CtxSetCurrent, "cuCtxSetCurrent") &&
+            sym(l, g_drv.CtxGetCurrent, "cuCtxGetCurrent") &&
+            sym(l, g_drv.ModuleLoadData, "cuModuleLoadData") &&
+            sym(l, g_drv.ModuleUnload, "cuModuleUnload") &&
+            sym(l, g_drv.ModuleGetFunction, "cuModuleGetFunction") &&
+            sym(l, g_drv.ModuleGetGlobal, "cuModuleGetGlobal_v2") &&
+            sym(l, g_drv.FuncGetAttribute, "cuFuncGetAttribute") &&
+            sym(l, g_drv.FuncSetAttribute, "cuFuncSetAttribute") &&
+            sym(l, g_drv.LaunchKernel, "cuLaunchKernel") &&
+            sym(l, g_drv.LaunchKernelEx, "cuLaunchKernelEx") &&
+            sym(l, g_drv.TensorMapEncodeTiled, "cuTensorMapEncodeTiled") &&
+            sym(l, g_drv.MemAlloc, "cuMemAlloc_v2") && sym(l, g_drv.MemFree, "cuMemFree_v2") &&
+            sym(l, g_drv.MemsetD8Async, "cuMemsetD8Async") &&
+            sym(l, g_drv.MemcpyHtoDAsync, "cuMemcpyHtoDAsync_v2") &&
+            sym(l, g_drv.MemcpyDtoHAsync, "cuMemcpyDtoHAsync_v2") &&
+            sym(l, g_drv.StreamSynchronize, "cuStreamSynchronize") &&
+            sym(l, g_drv.EventCreate, "cuEventCreate") &&
+            sym(l, g_drv.EventDestroy, "cuEventDestroy_v2") &&
+            sym(l, g_drv.EventRecord, "cuEventRecord") &&
+            sym(l, g_drv.EventSynchronize, "cuEventSynchronize") &&
+            sym(l, g_drv.EventElapsedTime, "cuEventElapsedTime");
+  if (!ok) return fail(EMMY_ENODRIVER, "libcuda.so.1 lacks a required symbol: %s", dlerror());
+  CUresult r = g_drv.Init(0);
+  if (r != CUDA_SUCCESS) return cuerr(r, "cuInit");
+  g_drv.inited = true;
+  return 0;
+}
+
+// Make sure some context is current on this thread; if none, use device 0's
+// primary context (the one the CUDA runtime and frameworks share).
+int ensure_ctx() {
+  if (int e = driver()) return e;
+  CUcontext cur = nullptr;
+  CU(g_drv.CtxGetCurrent(&cur), "cuCtxGetCurrent");
+  if (cur) return 0;
+  return emmy_device_init(0);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// handles
+// ---------------------------------------------------------------------------
+struct emmy_image_s {
+  std::vector<char> data;
+  std::string log;
+};
+struct emmy_module_s {
+  CUmodule mod;
+};
+struct emmy_kernel_s {
+  CUfunction fn;
+  int max_dyn_smem_set;
+};
+
+extern "C" {
+
+int emmy_abi_version(void) { return EMMY_ABI_VERSION; }
+const char *emmy_last_error(void) { return g_err.c_str(); }
+
+// ---------------------------------------------------------------------------
+// assemble
+// ---------------------------------------------------------------------------
+int emmy_ptx_assemble(const char *ptx, size_t ptx_len, const char *arch,
+                      const char *const *opts, int n_opts, emmy_image_t *out) {
+  if (!ptx || !out || n_opts < 0) return fail(EMMY_EINVAL, "emmy_ptx_assemble: bad argument");
+  *out = nullptr;
+  nvPTXCompilerHandle h = nullptr;
+  nvPTXCompileResult cr = nvPTXCompilerCreate(&h, ptx_len, ptx);
+  if (cr != NVPTXCOMPILE_SUCCESS)
+    return fail(EMMY_EPTXAS, "nvPTXCompilerCreate failed (%d)", static_cast<int>(cr));
+  std::string gpu = std::string("--gpu-name=") + (arch && *arch ? arch : "sm_100a");
+  std::vector<const char *> o;
+  o.push_back(gpu.c_str());
+  o.push_back("--verbose");
+  for (int i = 0; i < n_opts; ++i) o.push_back(opts[i]);
+  nvPTXCompileResult r = nvPTXCompilerCompile(h, static_cast<int>(o.size()), o.data());
+  std::string log;
+  size_t n = 0;
+  if (nvPTXCompilerGetErrorLogSize(h, &n) == NVPTXCOMPILE_SUCCESS && n > 1) {
+    std::string e(n, '\0');
+    nvPTXCompilerGetErrorLog(h, &e[0]);
+    log += e.c_str();
+  }
+  if (r != NVPTXCOMPILE_SUCCESS) {
+    nvPTXCompilerDestroy(&h);
+    return fail(EMMY_EPTXAS, "ptxas (%s) failed: %s", gpu.c_str() + 11, log.c_str());
+  }
+  auto *img = new (std::nothrow) emmy_image_s();
+  if (!img) {
+    nvPTXCompilerDestroy(&h);
+    return fail(EMMY_ENOMEM, "out of host memory");
+  }
+  if (nvPTXCompilerGetInfoLogSize(h, &n) == NVPTXCOMPILE_SUCCESS && n > 1) {
+    std::string e(n, '\0');
+    nvPTXCompilerGetInfoLog(h, &e[0]);
+    log += e.c_str();
+  }
+  img->log = log;
+  if (nvPTXCompilerGetCompiledProgramSize(h, &n) != NVPTXCOMPILE_SUCCESS) {
+    delete img;
+    nvPTXCompilerDestroy(&h);
+    return fail(EMMY_EPTXAS, "cannot size the compiled program");
+  }
+  img->data.resize(n);
+  nvPTXCompilerGetCompiledProgram(h, img->data.data());
+  nvPTXCompilerDestroy(&h);
+  *out = img;
+  return 0;
+}
+
+int emmy_image_data(emmy_image_t img, const void **data, size_t *len) {
+  if (!img || !data || !len) return fail(EMMY_EINVAL, "emmy_image_data: bad argument");
+  *data = img->data.data();
+  *len = img->data.size();
+  return 0;
+}
+
+const char *emmy_image_log(emmy_image_t img) { return img ? img->log.c_str() : ""; }
+
+void emmy_image_free(emmy_image_t img) { delete img; }
+
+// ---------------------------------------------------------------------------
+// device, modules
+// ---------------------------------------------------------------------------
+int emmy_device_count(int *count) {
+  if (!count) return fail(EMMY_EINVAL, "emmy_device_count: null");
+  *count = 0;
+  if (int e = driver()) return e;
+  CU(g_drv.DeviceGetCount(count), "cuDeviceGetCount");
+  return 0;
+}
+
+int emmy_device_init(int device) {
+  if (int e = driver()) return e;
+  CUdevice dev;
+  CU(g_drv.DeviceGet(&dev, device), "cuDeviceGet");
+  CUcontext ctx;
+  CU(g_drv.DevicePrimaryCtxRetain(&ctx, dev), "cuDevicePrimaryCtxRetain");
+  CU(g_drv.CtxSetCurrent(ctx), "cuCtxSetCurrent");
+  return 0;
+}
+
+int emmy_module_load(const void *image, size_t len, emmy_module_t *out) {
+  if (!image || !out || len == 0) return fail(EMMY_EINVAL, "emmy_module_load: bad argument");
+  if (int e = ensure_ctx()) return e;
+  CUmodule m;
+  CU(g_drv.ModuleLoadData(&m, image), "cuModuleLoadData");
+  *out = new emmy_module_s{m};
+  return 0;
+}
+
+int emmy_module_unload(emmy_module_t mod) {
+  if (!mod) return 0;
+  if (int e = driver()) return e;
+  CUresult r = g_drv.ModuleUnload(mod->mod);
+  delete mod;
+  if (r != CUDA_SUCCESS) return cuerr(r, "cuModuleUnload");
+  return 0;
+}
+
+int emmy_kernel_get(emmy_module_t mod, const char *entry, emmy_kernel_t *out) {
+  if (!mod || !entry || !out) return fail(EMMY_EINVAL, "emmy_kernel_get: bad argument");
+  CUfunction f;
+  CUresult r = g_drv.ModuleGetFunction(&f, mod->mod, entry);
+  if (r == CUDA_ERROR_NOT_FOUND) return fail(EMMY_ENOENT, "entry %s not in module", entry);
+  if (r != CUDA_SUCCESS) return cuerr(r, "cuModuleGetFunction");
+  *out = new emmy_kernel_s{f, 0};
+  return 0;
+}
+
+int emmy_kernel_attrs(emmy_kernel_t k, int *regs, int *static_smem, int *max_threads) {
+  if (!k) return fail(EMMY_EINVAL, "emmy_kernel_attrs: null kernel");
+  if (regs) CU(g_drv.FuncGetAttribute(regs, CU_FUNC_ATTRIBUTE_NUM_REGS, k->fn), "attr regs");
+  if (static_smem)
+    CU(g_drv.FuncGetAttribute(static_smem, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, k->fn),
+       "attr smem");
+  if (max_threads)
+    CU(g_drv.FuncGetAttribute(max_threads, CU_FUNC_ATTRIBUTE_MAX_THREADS_PER_BLOCK, k->fn),
+       "attr threads");
+  return 0;
+}
+
+int emmy_module_global(emmy_module_t mod, const char *name, uint64_t *dptr, size_t *bytes) {
+  if (!mod || !name || !dptr) return fail(EMMY_EINVAL, "emmy_module_global: bad argument");
+  CUdeviceptr p;
+  size_t n = 0;
+  CUresult r = g_drv.ModuleGetGlobal(&p, &n, mod->mod, name);
+  if (r == CUDA_ERROR_NOT_FOUND) return fail(EMMY_ENOENT, "global %s not in module", name);
+  if (r != CUDA_SUCCESS) return cuerr(r, "cuModuleGetGlobal");
+  *dptr = static_cast<uint64_t>(p);
+  if (bytes) *bytes = n;
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// tensor maps
+// ---------------------------------------------------------------------------
+int emmy_tensormap_encode(void *tmap, int dtype, int rank, uint64_t gaddr,
+                          const uint64_t *dims, const uint64_t *strides,
+                          const uint32_t *box, int swizzle) {
+  if (!tmap || rank < 1 || rank > 5 || !dims || !box || (rank > 1 && !strides))
+    return fail(EMMY_EINVAL, "emmy_tensormap_encode: bad argument");
+  if (dtype < 0 || dtype > 10 || swizzle < 0 || swizzle > 3)
+    return fail(EMMY_EINVAL, "emmy_tensormap_encode: dtype %d / swizzle %d", dtype, swizzle);
+  if (gaddr % 16 != 0) return fail(EMMY_EINVAL, "tensor map base %#llx not 16-byte aligned",
+                                   static_cast<unsigned long long>(gaddr));
+  for (int i = 0; i + 1 < rank; ++i)
+    if (strides[i] % 16 != 0)
+      return fail(EMMY_EINVAL, "tensor map stride %d (%llu) not a multiple of 16", i,
+                  static_cast<unsigned long long>(strides[i]));
+  if (int e = driver()) return e;
+  cuuint64_t d[5], s[5];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) s[i] = strides[i];
+  }
+  static const CUtensorMapSwizzle sw[4] = {CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                                          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_SWIZZLE_128B};
+  CU(g_drv.TensorMapEncodeTiled(reinterpret_cast<CUtensorMap *>(tmap),
+                                static_cast<CUtensorMapDataType>(dtype), rank,
+                                reinterpret_cast<void *>(gaddr), d, s, b, es,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, sw[swizzle],
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+     "cuTensorMapEncodeTiled");
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// launch
+// ---------------------------------------------------------------------------
+static int launch(emmy_kernel_t k, const uint32_t grid[3], const uint32_t block[3],
+                  uint32_t smem, const uint32_t *cluster, void **params, CUstream s) {
+  if (smem > 48 * 1024 && static_cast<int>(smem) > k->max_dyn_smem_set) {
+    CU(g_drv.FuncSetAttribute(k->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                              static_cast<int>(smem)),
+       "cuFuncSetAttribute(max dynamic smem)");
+    k->max_dyn_smem_set = static_cast<int>(smem);
+  }
+  if (cluster && cluster[0] * cluster[1] * cluster[2] > 1) {
+    CUlaunchConfig cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDimX = grid[0];
+    cfg.gridDimY = grid[1];
+    cfg.gridDimZ = grid[2];
+    cfg.blockDimX = block[0];
+    cfg.blockDimY = block[1];
+    cfg.blockDimZ = block[2];
+    cfg.sharedMemBytes = smem;
+    cfg.hStream = s;
+    CUlaunchAttribute attr;
+    memset(&attr, 0, sizeof attr);
+    attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attr.value.clusterDim.x = cluster[0];
+    attr.value.clusterDim.y = cluster[1];
+    attr.value.clusterDim.z = cluster[2];
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    CU(g_drv.LaunchKernelEx(&cfg, k->fn, params, nullptr), "cuLaunchKernelEx");
+    return 0;
+  }
+  CU(g_drv.LaunchKernel(k->fn, grid[0], grid[1], grid[2], block[0], block[1], block[2], smem, s,
+                        params, nullptr),
+     "cuLaunchKernel");
+  return 0;
+}
+
+int emmy_launch(emmy_kernel_t k, const uint32_t grid[3], const uint32_t block[3],
+                uint32_t smem_bytes, const uint32_t *cluster, void **params, void *stream) {
+  if (!k || !grid || !block) return fail(EMMY_EINVAL, "emmy_launch: bad argument");
+  return launch(k, grid, block, smem_bytes, cluster, params, static_cast<CUstream>(stream));
+}
+
+int emmy_memset_async(uint64_t dptr, int v, size_t bytes, void *stream) {
+  if (int e = ensure_ctx()) return e;
+  CU(g_drv.MemsetD8Async(dptr, static_cast<unsigned char>(v), bytes,
+                         static_cast<CUstream>(stream)),
+     "cuMemsetD8Async");
+  return 0;
+}
+
+int emmy_memcpy_htod_async(uint64_t dst, const void *src, size_t bytes, void *stream) {
+  if (int e = ensure_ctx()) return e;
+  CU(g_drv.MemcpyHtoDAsync(dst, src, bytes, static_cast<CUstream>(stream)), "cuMemcpyHtoDAsync");
+  return 0;
+}
+
+int emmy_memcpy_dtoh_async(void *dst, uint64_t src, size_t bytes, void *stream) {
+  if (int e = ensure_ctx()) return e;
+  CU(g_drv.MemcpyDtoHAsync(dst, src, bytes, static_cast<CUstream>(stream)), "cuMemcpyDtoHAsync");
+  return 0;
+}
+
+int emmy_stream_sync(void *stream) {
+  if (int e = ensure_ctx()) return e;
+  CU(g_drv.StreamSynchronize(static_cast<CUstream>(stream)), "cuStreamSynchronize");
+  return 0;
+}
+
+int emmy_mem_alloc(uint64_t *dptr, size_t bytes) {
+  if (!dptr) return fail(EMMY_EINVAL, "emmy_mem_alloc: null");
+  if (int e = ensure_ctx()) return e;
+  CUdeviceptr p;
+  CU(g_drv.MemAlloc(&p, bytes ? bytes : 1), "cuMemAlloc");
+  *dptr = p;
+  return 0;
+}
+
+int emmy_mem_free(uint64_t dptr) {
+  if (!dptr) return 0;
+  if (int e = ensure_ctx()) return e;
+  CU(g_drv.MemFree(dptr), "cuMemFree");
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// timing
+// ---------------------------------------------------------------------------
+int emmy_time_launches(emmy_kernel_t k, const uint32_t grid[3], const uint32_t block[3],
+                       uint32_t smem, const uint32_t *cluster, void **params, void *stream,
+                       int warmup, int iters, uint64_t flush_dptr, size_t flush_bytes,
+                       const uint64_t *zero_dptrs, const size_t *zero_bytes, int n_zero,
+                       float *ms_out) {
+  if (!k || !grid || !block || iters < 1 || warmup < 0 || !ms_out || n_zero < 0 ||
+      (n_zero > 0 && (!zero_dptrs || !zero_bytes)))
+    return fail(EMMY_EINVAL, "emmy_time_launches: bad argument");
+  CUstream s = static_cast<CUstream>(stream);
+  auto prep = [&](int it) -> int {
+    if (flush_dptr && flush_bytes)
+      CU(g_drv.MemsetD8Async(flush_dptr, static_cast<unsigned char>(it & 0xff), flush_bytes, s),
+         "L2 flush");
+    for (int z = 0; z < n_zero; ++z)
+      CU(g_drv.MemsetD8Async(zero_dptrs[z], 0, zero_bytes[z], s), "zero output");
+    return 0;
+  };
+  for (int i = 0; i < warmup; ++i) {
+    if (int e = prep(i)) return e;
+    if (int e = launch(k, grid, block, smem, cluster, params, s)) return e;
+  }
+  std::vector<CUevent> ev(2 * static_cast<size_t>(iters));
+  for (auto &e : ev) CU(g_drv.EventCreate(&e, CU_EVENT_DEFAULT), "cuEventCreate");
+  int rc = 0;
+  for (int i = 0; i < iters && rc == 0; ++i) {
+    rc = prep(i);
+    if (rc) break;
+    CUresult r = g_drv.EventRecord(ev[2 * i], s);
+    if (r != CUDA_SUCCESS) {
+      rc = cuerr(r, "cuEventRecord");
+      break;
+    }
+    rc = launch(k, grid, block, smem, cluster, params, s);
+    if (rc) break;
+    r = g_drv.EventRecord(ev[2 * i + 1], s);
+    if (r != CUDA_SUCCESS) rc = cuerr(r, "cuEventRecord");
+  }
+  if (rc == 0) {
+    CUresult r = g_drv.EventSynchronize(ev.back());
+    if (r != CUDA_SUCCESS) rc = cuerr(r, "cuEventSynchronize");
+  }
+  for (int i = 0; i < iters && rc == 0; ++i) {
+    CUresult r = g_drv.EventElapsedTime(&ms_out[i], ev[2 * i], ev[2 * i + 1]);
+    if (r != CUDA_SUCCESS) rc = cuerr(r, "cuEventElapsedTime");
+  }
+  for (auto &e : ev) g_drv.EventDestroy(e);
+  return rc;
+}
+
+// ---------------------------------------------------------------------------
+// host-buffer run
+// ---------------------------------------------------------------------------
+int emmy_run_host(emmy_kernel_t k, const uint32_t grid[3], const uint32_t block[3],
+                  uint32_t smem, const uint32_t *cluster, int n_args, void *const *host,
+                  const uint64_t *dev, const size_t *bytes, const int *is_output, int n_extra,
+                  void **extra_params, void *stream) {
+  if (!k || !grid || !block || n_args < 0 || n_extra < 0 || (n_args && (!host || !dev || !bytes ||
+                                                                       !is_output)) ||
+      (n_extra && !extra_params))
+    return fail(EMMY_EINVAL, "emmy_run_host: bad argument");
+  CUstream s = static_cast<CUstream>(stream);
+  std::vector<CUdeviceptr> vals(static_cast<size_t>(n_args));
+  std::vector<void *> params(static_cast<size_t>(n_args + n_extra));
+  for (int i = 0; i < n_args; ++i) {
+    vals[i] = dev[i];
+    params[i] = &vals[i];
+    if (is_output[i]) {
+      CU(g_drv.MemsetD8Async(dev[i], 0, bytes[i], s), "zero output");
+    } else if (bytes[i]) {
+      if (!host[i]) return fail(EMMY_EINVAL, "emmy_run_host: input %d has no host buffer", i);
+      CU(g_drv.MemcpyHtoDAsync(dev[i], host[i], bytes[i], s), "cuMemcpyHtoDAsync");
+    }
+  }
+  for (int j = 0; j < n_extra; ++j) params[n_args + j] = extra_params[j];
+  if (int e = launch(k, grid, block, smem, cluster, params.data(), s)) return e;
+  for (int i = 0; i < n_args; ++i)
+    if (is_output[i] && host[i] && bytes[i])
+      CU(g_drv.MemcpyDtoHAsync(host[i], dev[i], bytes[i], s), "cuMemcpyDtoHAsync");
+  CU(g_drv.StreamSynchronize(s), "cuStreamSynchronize");
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,397 @@
+"""IR synthesiser: Kernel IR graphs + meta.json for the benchmark shapes.
+
+Emmy traces PyTorch expressions into IR (reference ``tools/generate.py:57-205``),
+which needs emmy-ml and torch tracing; neither runs offline.  This module
+writes the same artefacts directly, in the schedule forms Emmy itself emits
+for each category, scaled to the benchmark shapes:
+
+* pointwise -- the strided-loop form ``Tile[a0_co] { for a0 in a0_co..N:T }``;
+* full sum  -- the split form of reference ``tests/hsx/sum_big`` (``_ksplit`` CTAs,
+  one atomic add per CTA, output in ``zero_outputs``);
+* row sum / row mean -- reference ``problems/r04_row_sum`` / ``r03_mean``;
+* RMSNorm / softmax / L2 norm -- reference ``problems/f01..f03`` (softmax with the
+  input scaled by a constant, L2 norm with ``maximum(norm, eps)``).
+
+The output is the JSON graph format of the problems (``inputs``, ``outputs``,
+``nodes`` with ``op_fields.body`` as ``repr`` strings) plus a ``meta.json``
+dict with the reference's launch fields, the reference's argument forms
+(``seed``/``data``/``output``), this build's ``dist`` form for the benchmark
+distributions (:mod:`emmy_b200.data`), and an ``oracle`` entry naming the
+expression family the tests evaluate on the CPU.  Seeds follow the
+reference's convention: an input's seed is its index in ``graph.inputs``
+(reference ``tools/generate.py:135``).
+"""
+from __future__ import annotations
+
+import math
+
+from . import ir as I
+
+F32 = I.data_type("f32")
+BF16 = I.data_type("bf16")
+
+
+# --------------------------------------------------------------------------
+# repr serialiser (the inverse of ir.parse_repr)
+# --------------------------------------------------------------------------
+
+def to_repr(x) -> str:
+    k = type(x).__name__
+    if x is None or isinstance(x, bool):
+        return repr(x)
+    if isinstance(x, (int, float)) and not isinstance(x, bool):
+        return repr(x)
+    if isinstance(x, I.NpDtype):
+        return f"dtype({str.__repr__(str(x))})"
+    if isinstance(x, str):
+        return repr(str(x))
+    if isinstance(x, tuple):
+        if len(x) == 1:
+            return "(" + to_repr(x[0]) + ",)"
+        return "(" + ", ".join(to_repr(e) for e in x) + ")"
+    if k == "Dim":
+        return f"Dim({x.value})"
+    if k == "ElementwiseImpl":
+        return f"ElementwiseImpl({x.name!r})"
+    if k in I.NODE_CLASSES:
+        import dataclasses
+        parts = [f"{f.name}={to_repr(getattr(x, f.name))}" for f in dataclasses.fields(x)]
+        return f"{k}(" + ", ".join(parts) + ")"
+    raise TypeError(f"cannot serialise {k}")
+
+
+# --------------------------------------------------------------------------
+# builders
+# --------------------------------------------------------------------------
+
+def V(name):
+    return I.Var(name)
+
+
+def Lit(v):
+    return I.Literal(v, "int" if isinstance(v, int) else "float")
+
+
+def add(a, b):
+    return I.BinaryExpr("+", a, b)
+
+
+def mul(a, b):
+    return I.BinaryExpr("*", a, b)
+
+
+def eq(a, b):
+    return I.BinaryExpr("==", a, b)
+
+
+def axis(name, extent, parent=None):
+    w = None
+    if parent is not None:
+        w = I.Window(I.Axis(parent[0], I.Dim(parent[1]), None), None, None, True)
+    return I.Axis(name, I.Dim(extent), w)
+
+
+def load(name, buf, *index, dtype=F32):
+    return I.Load((name,), buf, tuple(index), dtype)
+
+
+def assign(name, op, *args, dtype=F32):
+    return I.Assign(name, I.ElementwiseImpl(op), tuple(args), dtype)
+
+
+def accum(name, value, op="add", base=None, axes=()):
+    return I.Accum(name, value, I.ElementwiseImpl(op), F32, tuple(axes), base)
+
+
+def write(out, index, values, atomic=False, dtype=F32):
+    return I.Write(out, tuple(index), tuple(values), dtype, atomic, "NONE")
+
+
+def tile(axes, body, block_threads=None):
+    return I.Tile(tuple(axes), tuple(body), block_threads, 0, None, None, "m")
+
+
+def strided(ax, start, step, body):
+    return I.StridedLoop(ax, start, Lit(step), tuple(body), False, None, True)
+
+
+def combine_block(states, B, combine):
+    """WarpShuffle + per-warp smem + lane-0 store + Sync + TreeHalve, as Emmy
+    emits it for a cooperative reduction over B threads (reference
+    ``problems/r01_array_sum/*.ir.txt:6-12``)."""
+    sb = tuple(f"{s}__o" for s in states)
+    out = [I.WarpShuffle(tuple(states), sb, tuple(combine), 32, F32)]
+    nw = B // 32
+    for s in states:
+        out.append(I.Smem(f"{s}_smem", (nw,), "float", 0))
+    out.append(I.Cond(eq(V("lane"), Lit(0)),
+                      tuple(write(f"{s}_smem", (V("warp"),), (s,)) for s in states), ()))
+    out.append(I.Sync(0, None, False))
+    out.append(I.TreeHalve(tuple(f"{s}_smem" for s in states), tuple(states), sb,
+                           tuple(combine), nw, "warp", F32, 0, None, None))
+    return out
+
+
+def add_combine(s="acc0"):
+    return [assign(s, "add", s, f"{s}__o", dtype=None)]
+
+
+def softmax_combine():
+    """The online-softmax merge of (max, sum) pairs (reference f02's combine)."""
+    return [assign("acc0__o__gn", "maximum", "acc0", "acc0__o", dtype=None),
+            assign("acc0__o__dg", "subtract", "acc0", "acc0__o__gn", dtype=None),
+            assign("acc0__o__alpha", "exp", "acc0__o__dg", dtype=None),
+            assign("acc0__o__dg_o", "subtract", "acc0__o", "acc0__o__gn", dtype=None),
+            assign("acc0__o__beta", "exp", "acc0__o__dg_o", dtype=None),
+            assign("acc0__o__acc1_sa", "multiply", "acc0__o__alpha", "acc1", dtype=None),
+            assign("acc0__o__acc1_sb", "multiply", "acc0__o__beta", "acc1__o", dtype=None),
+            assign("acc1", "add", "acc0__o__acc1_sa", "acc0__o__acc1_sb", dtype=None),
+            assign("acc0", "copy", "acc0__o__gn", dtype=None)]
+
+
+# --------------------------------------------------------------------------
+# graph + meta assembly
+# --------------------------------------------------------------------------
+
+class Problem:
+    def __init__(self, pid: str, code: str, entry: str, node: str):
+        self.pid, self.code, self.entry, self.node = pid, code, entry, node
+        self.inputs = []       # (name, shape, dtype, argspec)
+        self.consts = []       # (name, value)
+        self.out = None        # (name, shape, dtype)
+        self.body = None
+        self.grid = self.block = None
+        self.smem = 0
+        self.zero = []
+        self.oracle = None
+        self.rtol = self.atol = None
+
+    def add_input(self, name, shape, dtype="f32", dist=None):
+        self.inputs.append((name, tuple(shape), dtype, dist))
+
+    def add_const(self, name, value):
+        self.consts.append((name, float(value)))
+
+    def graph(self) -> dict:
+        nodes = {}
+        names = []
+        for name, shape, dt, _ in self.inputs:
+            nodes[name] = {"op": "InputOp", "op_fields": {}, "inputs": [],
+                           "outputs": [{"name": name, "shape": list(shape), "dtype": dt}]}
+            names.append(name)
+        for name, value in self.consts:
+            nodes[name] = {"op": "ConstantOp", "op_fields": {"name": name, "value": value},
+                           "inputs": [],
+                           "outputs": [{"name": name, "shape": [1], "dtype": "f32"}]}
+        oname, oshape, odt = self.out
+        nodes[self.node] = {
+            "op": "KernelOp",
+            "op_fields": {"body": [to_repr(self.body)], "name": self.entry,
+                          "zero_delegated": [], "serial": []},
+            "inputs": [c for c, _ in self.consts] + names,
+            "outputs": [{"name": oname, "shape": list(oshape), "dtype": odt}]}
+        return {"inputs": names, "outputs": [oname], "nodes": nodes}
+
+    def meta(self) -> dict:
+        args = []
+        arg_order = []
+        for name, value in self.consts:
+            args.append({"name": name, "dtype": "f32", "shape": [1], "data": [value]})
+            arg_order.append(name)
+        for i, (name, shape, dt, dist) in enumerate(self.inputs):
+            a = {"name": name, "dtype": dt, "shape": list(shape), "seed": i}
+            if dist:
+                a["dist"] = dist
+            args.append(a)
+            arg_order.append(name)
+        oname, oshape, odt = self.out
+        args.append({"name": oname, "dtype": odt, "shape": list(oshape), "output": True})
+        arg_order.append(oname)
+        return {"id": self.pid, "code": self.code, "rtol": self.rtol, "atol": self.atol,
+                "graph_inputs": [n for n, *_ in self.inputs], "graph_outputs": [oname],
+                "kernels": [{"node": self.node, "entry": self.entry, "arg_order": arg_order,
+                             "grid": list(self.grid), "block": list(self.block),
+                             "smem_bytes": self.smem, "zero_outputs": list(self.zero),
+                             "args": args, "final": True}],
+                "oracle": self.oracle}
+
+    def build(self) -> tuple[dict, dict]:
+        return self.graph(), self.meta()
+
+
+# --------------------------------------------------------------------------
+# the benchmark configurations
+# --------------------------------------------------------------------------
+
+UNIF01 = {"kind": "uniform", "lo": 0.0, "hi": 1.0}
+UNIF11 = {"kind": "uniform", "lo": -1.0, "hi": 1.0}
+
+
+def vector_add(n: int = 1_048_576, threads: int | None = None, block: int = 256) -> Problem:
+    """``c = a + b`` over ``n`` f32 elements, strided-loop form."""
+    T = threads or min(n, 148 * block)
+    T = -(-T // block) * block
+    p = Problem(f"add_{n}", "a + b", "k_add_pointwise", "add")
+    p.add_input("x0", (n,), dist=UNIF11)
+    p.add_input("x1", (n,), dist=UNIF11)
+    p.out = ("add", (n,), "f32")
+    loop = strided(axis("a0", n), V("a0_co"), T,
+                   [load("in0", "x0", V("a0")), load("in1", "x1", V("a0")),
+                    assign("v0", "add", "in0", "in1"), write("add", (V("a0"),), ("v0",))])
+    p.body = tile([axis("a0_co", T)], [loop])
+    p.grid, p.block = (T // block, 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 0, 0
+    p.oracle = {"family": "add", "args": {"a": "x0", "b": "x1"}, "output": "add"}
+    return p
+
+
+def full_sum(n: int = 268_435_456, ctas: int = 2048, block: int = 256) -> Problem:
+    """``s = sum(x)``, x ~ U(0,1): split form, one atomic add per CTA."""
+    assert n % ctas == 0
+    C = n // ctas
+    p = Problem(f"sum_{n}", "x.sum()", "k_sum_1_reduce", "sum_1")
+    p.add_input("x", (n,), dist=UNIF01)
+    p.out = ("sum_1", (), "f32")
+    loop = strided(axis("a0", C, parent=("a0", n)), V("a0_co"), block,
+                   [load("in0", "x", add(V("a0"), mul(V("_ksplit"), Lit(C)))),
+                    accum("acc0", "in0", axes=("a0",))])
+    body = [loop] + combine_block(["acc0"], block, add_combine()) + [
+        I.Cond(eq(V("a0_co"), Lit(0)), (write("sum_1", (), ("acc0",), atomic=True),), ())]
+    p.body = tile([axis("_ksplit", ctas), axis("a0_co", block)], body, block)
+    p.grid, p.block = (ctas, 1, 1), (block, 1, 1)
+    p.zero = ["sum_1"]
+    p.rtol, p.atol = 1e-4, None
+    p.oracle = {"family": "sum", "args": {"x": "x"}, "output": "sum_1"}
+    return p
+
+
+def row_reduce(rows: int = 32768, cols: int = 8192, block: int = 256, mean: bool = False) -> Problem:
+    """``y[r] = sum_c x[r, c]`` (or the mean, ``/ cols``), x ~ N(0,1)."""
+    name = "mean" if mean else "sum_1"
+    p = Problem(f"row_{'mean' if mean else 'sum'}_{rows}x{cols}",
+                f"x.{'mean' if mean else 'sum'}(-1)", f"k_{name}_reduce", name)
+    if mean:
+        p.add_const("mean_count", cols)
+    p.add_input("x", (rows, cols))
+    p.out = (name, (rows,), "f32")
+    loop = strided(axis("a1", cols), V("a1_co"), block,
+                   [load("in0", "x", V("a0"), V("a1")), accum("acc0", "in0", axes=("a1",))])
+    tail = [write(name, (V("a0"),), ("acc0",))]
+    if mean:
+        tail = [load("in1", "mean_count", Lit(0)), assign("v0", "divide", "acc0", "in1"),
+                write(name, (V("a0"),), ("v0",))]
+    body = [loop] + combine_block(["acc0"], block, add_combine()) + [
+        I.Cond(eq(V("a1_co"), Lit(0)), tuple(tail), ())]
+    p.body = tile([axis("a0", rows), axis("a1_co", block)], body)
+    p.grid, p.block = (rows, 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 1e-4, None
+    p.oracle = {"family": "row_mean" if mean else "row_sum", "args": {"x": "x"}, "output": name}
+    return p
+
+
+def rmsnorm(rows: int = 65536, cols: int = 4096, block: int = 128, eps: float = 1e-6) -> Problem:
+    """``y = x * rsqrt(mean(x^2) + eps) * w`` (reference f01's IR with eps)."""
+    p = Problem(f"rmsnorm_{rows}x{cols}", "x * rsqrt(mean(x^2)+eps) * w", "k_rmsnorm", "mul_1")
+    p.add_const("mean_count", cols)
+    p.add_const("add_c1", eps)
+    p.add_input("x", (rows, cols))
+    p.add_input("w", (cols,), dist={"kind": "uniform", "lo": 0.5, "hi": 1.5})
+    p.out = ("mul_1", (rows, cols), "f32")
+    loop1 = strided(axis("a1", cols), V("a1_co"), block,
+                    [load("in2", "x", V("a0"), V("a1")), assign("v1", "multiply", "in2", "in2"),
+                     accum("acc0", "v1", axes=("a1",))])
+    post = [load("in1", "mean_count", Lit(0)), assign("v0", "reciprocal", "in1"),
+            assign("v2", "multiply", "acc0", "v0"), load("in0", "add_c1", Lit(0)),
+            assign("v3", "add", "in0", "v2"), assign("v4", "sqrt", "v3"),
+            assign("v5", "reciprocal", "v4")]
+    loop2 = strided(axis("a2", cols), V("a1_co"), block,
+                    [load("in3", "x", V("a0"), V("a2")), assign("v6", "multiply", "in3", "v5"),
+                     load("in4", "w", V("a2")), assign("v7", "multiply", "in4", "v6"),
+                     write("mul_1", (V("a0"), V("a2")), ("v7",))])
+    p.body = tile([axis("a0", rows), axis("a1_co", block)],
+                  [loop1] + combine_block(["acc0"], block, add_combine()) + post + [loop2])
+    p.grid, p.block = (rows, 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 1e-5, None
+    p.oracle = {"family": "rmsnorm", "args": {"x": "x", "w": "w"}, "output": "mul_1", "eps": eps}
+    return p
+
+
+def softmax(rows: int = 65536, cols: int = 4096, block: int = 128, scale: float = 4.0) -> Problem:
+    """Row softmax of ``scale * x`` (reference f02's online-softmax IR)."""
+    p = Problem(f"softmax_{rows}x{cols}", f"softmax({scale} * x, -1)", "k_softmax", "softmax")
+    p.add_const("mul_c1", scale)
+    p.add_input("x", (rows, cols))
+    p.out = ("softmax", (rows, cols), "f32")
+    loop1 = strided(axis("a1", cols), V("a1_co"), block, [
+        I.Let("one", Lit(1.0), F32),
+        load("in0r", "x", V("a0"), V("a1")), load("c0", "mul_c1", Lit(0)),
+        assign("in0", "multiply", "in0r", "c0"),
+        assign("in0__gn", "maximum", "acc0", "in0"),
+        assign("in0__dg", "subtract", "acc0", "in0__gn"),
+        assign("in0__alpha", "exp", "in0__dg"),
+        assign("in0__dg_o", "subtract", "in0", "in0__gn"),
+        assign("in0__beta", "exp", "in0__dg_o"),
+        assign("in0__acc1_sa", "multiply", "acc1", "in0__alpha"),
+        assign("in0__acc1_sb", "multiply", "in0__beta", "one"),
+        accum("acc1", "in0__acc1_sb", base="in0__acc1_sa", axes=("a1",)),
+        accum("acc0", "in0", op="maximum", axes=("a1",))])
+    post = [assign("v2", "reciprocal", "acc1")]
+    loop2 = strided(axis("a3", cols), V("a1_co"), block, [
+        load("in2r", "x", V("a0"), V("a3")), load("c1", "mul_c1", Lit(0)),
+        assign("in2", "multiply", "in2r", "c1"),
+        assign("v3", "subtract", "in2", "acc0"), assign("v4", "exp", "v3"),
+        assign("v5", "multiply", "v2", "v4"), write("softmax", (V("a0"), V("a3")), ("v5",))])
+    p.body = tile([axis("a0", rows), axis("a1_co", block)],
+                  [loop1] + combine_block(["acc0", "acc1"], block, softmax_combine()) + post
+                  + [loop2])
+    p.grid, p.block = (rows, 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 1e-5, None
+    p.oracle = {"family": "softmax", "args": {"x": "x"}, "output": "softmax", "scale": scale}
+    return p
+
+
+def l2norm(rows: int = 65536, cols: int = 4096, block: int = 128, eps: float = 1e-12) -> Problem:
+    """``y = x / max(||x||_2, eps)`` (reference f03's IR with F.normalize's eps)."""
+    p = Problem(f"l2norm_{rows}x{cols}", "x / max(norm(x, -1), eps)", "k_l2norm", "div")
+    p.add_const("eps_c1", eps)
+    p.add_input("x", (rows, cols))
+    p.out = ("div", (rows, cols), "f32")
+    loop1 = strided(axis("a1", cols), V("a1_co"), block,
+                    [load("in0", "x", V("a0"), V("a1")), assign("v0", "multiply", "in0", "in0"),
+                     accum("acc0", "v0", axes=("a1",))])
+    post = [assign("v1", "sqrt", "acc0"), load("e0", "eps_c1", Lit(0)),
+            assign("v1m", "maximum", "v1", "e0"), assign("v2", "reciprocal", "v1m")]
+    loop2 = strided(axis("a2", cols), V("a1_co"), block,
+                    [load("in1", "x", V("a0"), V("a2")), assign("v3", "multiply", "in1", "v2"),
+                     write("div", (V("a0"), V("a2")), ("v3",))])
+    p.body = tile([axis("a0", rows), axis("a1_co", block)],
+                  [loop1] + combine_block(["acc0"], block, add_combine()) + post + [loop2])
+    p.grid, p.block = (rows, 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 1e-5, None
+    p.oracle = {"family": "l2norm", "args": {"x": "x"}, "output": "div", "eps": eps}
+    return p
+
+
+# the BASELINE.json configurations by name (full sizes)
+def config(name: str, **kw) -> Problem:
+    table = {
+        "vector_add": vector_add,
+        "full_sum": full_sum,
+        "row_sum": lambda **k: row_reduce(mean=False, **k),
+        "row_mean": lambda **k: row_reduce(mean=True, **k),
+        "rmsnorm": rmsnorm,
+        "softmax": softmax,
+        "l2norm": l2norm,
+    }
+    return table[name](**kw)
+
+
+def algorithmic_bytes(p: Problem) -> int:
+    """Bytes a kernel must move at minimum: every input read once, every
+    output written once (the roofline numerator for HBM-bound kernels)."""
+    n = 0
+    for _, shape, dt, _ in p.inputs:
+        n += math.prod(shape) * (2 if dt == "bf16" else 4)
+    n += 4 * len(p.consts)
+    n += math.prod(p.out[1]) * 4 if p.out[1] else 4
+    return n

@@ -1,0 +1,187 @@
+"""CPU oracle for the five kernel categories -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU legs of ``bench.py``
+may import this module; the product (``compile.py`` and the ``emmy_b200``
+package) never does.
+
+The reference checks every kernel against a numpy/torch evaluation of the
+kernel's PyTorch expression on the seeded inputs: Emmy's generator evaluates
+it and stores ``expected.npz`` (reference ``tools/generate.py:142-151``), the
+open-set expression table pairs each expression with a float64 numpy
+reference cast to float32 (``tools/expressions_open.py:52-104``), and the
+corpus oracles are numpy lambdas (``tools/harness/refs.py:22-124``).  This
+module restates those evaluations:
+
+* float64 arithmetic on the inputs, cast to float32 at the end, for
+  reductions, fused row ops, matmul and attention;
+* float32 arithmetic in the IR's operation order for pointwise kernels, which
+  is what "bit-exact vs numpy" means for ``a + b`` and ``x * c + d``.
+
+Pinned by ``tests/test_oracle.py``: every open problem's ``expected.npz``
+(all five categories) is reproduced within the problem's own rtol/atol.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+f32, f64 = np.float32, np.float64
+
+
+def _d(x):
+    return np.asarray(x, dtype=f64)
+
+
+# --------------------------------------------------------------------------
+# expression families (float64 unless noted)
+# --------------------------------------------------------------------------
+
+def add_f32(a, b):
+    """``a + b`` in float32 (one ``add.rn.f32`` per element)."""
+    return np.add(np.asarray(a, f32), np.asarray(b, f32), dtype=f32)
+
+
+def scale_shift_f32(x, m, c):
+    """``x * m + c`` in float32, two roundings (reference p02, ops multiply then add)."""
+    return np.add(np.multiply(np.asarray(x, f32), f32(m), dtype=f32), f32(c), dtype=f32)
+
+
+def relu_mul_f32(x, y):
+    return np.multiply(np.asarray(y, f32), np.maximum(np.asarray(x, f32), f32(0)), dtype=f32)
+
+
+def full_sum(x):
+    return np.asarray(_d(x).sum(), dtype=f32)
+
+
+def full_mean(x):
+    return np.asarray(_d(x).mean(), dtype=f32)
+
+
+def row_sum(x):
+    return _d(x).sum(-1).astype(f32)
+
+
+def row_mean(x):
+    return _d(x).mean(-1).astype(f32)
+
+
+def rmsnorm(x, w, eps):
+    """``x * rsqrt(mean(x^2) + eps) * w`` (reference f01 with its eps)."""
+    x = _d(x)
+    r = 1.0 / np.sqrt((x * x).mean(-1, keepdims=True) + eps)
+    return (x * r * _d(w)).astype(f32)
+
+
+def softmax_rows(x, scale=1.0):
+    """Row softmax of ``scale * x`` (reference f02; the benchmark scales by 4)."""
+    z = _d(x) * scale
+    z = z - z.max(-1, keepdims=True)
+    e = np.exp(z)
+    return (e / e.sum(-1, keepdims=True)).astype(f32)
+
+
+def l2norm(x, eps=None):
+    """``x / ||x||_2`` per row; with ``eps``, ``x / max(||x||_2, eps)`` (F.normalize)."""
+    x = _d(x)
+    n = np.sqrt((x * x).sum(-1, keepdims=True))
+    if eps is not None:
+        n = np.maximum(n, eps)
+    return (x / n).astype(f32)
+
+
+def matmul(a, b):
+    return (_d(a) @ _d(b)).astype(f32)
+
+
+def attention(q, k, v, scale, k_transposed=False):
+    """``softmax(q k^T * scale) v`` per leading (batch, head) index, float64.
+    ``k_transposed``: ``k`` is given as ``k^T`` (the reference's open problems
+    pre-transpose it, ``tools/expressions_open.py:91-92``)."""
+    q, k, v = _d(q), _d(k), _d(v)
+    kt = k if k_transposed else np.swapaxes(k, -1, -2)
+    s = (q @ kt) * scale
+    s = s - s.max(-1, keepdims=True)
+    e = np.exp(s)
+    p = e / e.sum(-1, keepdims=True)
+    return (p @ v).astype(f32)
+
+
+# --------------------------------------------------------------------------
+# the reference's open problems (problems/*/meta.json "code")
+# --------------------------------------------------------------------------
+
+def _const(v, name):
+    return float(np.asarray(v[name]).reshape(-1)[0])
+
+
+PROBLEMS = {
+    "p00_scalar_add": lambda v: {"add": add_f32(v["x0"], v["x1"])},
+    "p01_vector_add": lambda v: {"add": add_f32(v["x0"], v["x1"])},
+    "p02_scale_shift": lambda v: {"add": scale_shift_f32(v["x"], _const(v, "mul_c1"),
+                                                         _const(v, "add_c1"))},
+    "p03_relu_mul": lambda v: {"mul": relu_mul_f32(v["x"], v["y"])},
+    "r01_array_sum": lambda v: {"sum_1": full_sum(v["x"])},
+    "r02_big_sum": lambda v: {"sum_1": full_sum(v["x"])},
+    "r03_mean": lambda v: {"mean": full_mean(v["x"])},
+    "r04_row_sum": lambda v: {"sum_1": row_sum(v["x"])},
+    "f01_rmsnorm": lambda v: {"mul_1": rmsnorm(v["x"], v["w"], _const(v, "add_c1"))},
+    "f02_row_softmax": lambda v: {"softmax": softmax_rows(v["x"])},
+    "f03_l2norm": lambda v: {"div": l2norm(v["x"])},
+    "m01_matmul_512": lambda v: {"matmul": matmul(v["x0"], v["x1"])},
+    "m02_matmul_rect": lambda v: {"matmul": matmul(v["x0"], v["x1"])},
+    "a01_attention": lambda v: {"matmul_1": attention(v["q"], v["kt"], v["v"],
+                                                      1.0 / _const(v, "div_c1"), True)},
+    "a02_attention_128": lambda v: {"matmul_1": attention(v["q"], v["kt"], v["v"],
+                                                          1.0 / _const(v, "div_c1"), True)},
+}
+
+
+def evaluate_problem(problem_id: str, inputs: dict) -> dict:
+    return PROBLEMS[problem_id](inputs)
+
+
+# --------------------------------------------------------------------------
+# synthesised configurations: the IR synthesiser records {"family", params}
+# in meta["oracle"]; inputs are keyed by buffer name
+# --------------------------------------------------------------------------
+
+def bf16_to_f32(bits):
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def evaluate_family(spec: dict, inputs: dict) -> dict:
+    fam = spec["family"]
+    a = spec.get("args", {})
+    v = {k: (bf16_to_f32(x) if spec.get("bf16", {}).get(k) else x) for k, x in inputs.items()}
+    out = spec["output"]
+    if fam == "add":
+        r = add_f32(v[a["a"]], v[a["b"]])
+    elif fam == "sum":
+        r = full_sum(v[a["x"]])
+    elif fam == "row_sum":
+        r = row_sum(v[a["x"]])
+    elif fam == "row_mean":
+        r = row_mean(v[a["x"]])
+    elif fam == "rmsnorm":
+        r = rmsnorm(v[a["x"]], v[a["w"]], spec["eps"])
+    elif fam == "softmax":
+        r = softmax_rows(v[a["x"]], spec.get("scale", 1.0))
+    elif fam == "l2norm":
+        r = l2norm(v[a["x"]], spec.get("eps"))
+    elif fam == "matmul":
+        r = matmul(v[a["a"]], v[a["b"]])
+    elif fam == "attention":
+        r = attention(v[a["q"]], v[a["k"]], v[a["v"]], spec["scale"])
+    else:
+        raise KeyError(fam)
+    return {out: r}
+
+
+def tolerance(spec_or_meta: dict, ref: np.ndarray) -> tuple[float, float]:
+    """(rtol, atol): the problem's own pair, with atol = rtol * max|ref| when the
+    problem gives none (the survey's recommendation for non-pointwise checks)."""
+    rtol = float(spec_or_meta.get("rtol", 0.0))
+    atol = spec_or_meta.get("atol")
+    if atol is None:
+        atol = rtol * float(np.max(np.abs(ref))) if ref.size else 0.0
+    return rtol, float(atol)

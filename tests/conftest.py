@@ -1,0 +1,34 @@
+"""Shared test setup: import paths, the ``gpu`` marker, fixture locations."""
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(REPO / "emmy-hackathon-2026_b200"))
+sys.path.insert(0, str(REPO))
+
+GOLDEN = REPO / "tests" / "golden"
+PROBLEMS = sorted(p for p in (GOLDEN / "problems").iterdir() if p.is_dir())
+FIXTURES = sorted(p for p in (GOLDEN / "fixtures").iterdir() if p.is_dir())
+REFERENCE = Path(os.environ.get("EMMY_REFERENCE_ROOT", "/root/reference"))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def native_lib():
+    from emmy_b200 import native
+    native.build()
+    return native.lib()
+
+
+def gpu_available() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:
+        return False
