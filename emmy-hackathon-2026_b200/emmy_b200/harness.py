@@ -202,6 +202,37 @@ class Buffers:
                 host = inputs[name] if name in inputs else materialize(a, folder)
                 self.t[name] = to_device(np.asarray(host).reshape(-1), dt, device)
 
+    @classmethod
+    def random(cls, kern: CompiledKernel, seed: int = 0, device="cuda") -> "Buffers":
+        """Buffers filled on the device by torch's generator with each input's
+        distribution (``dist``; standard normal otherwise) -- for timing runs,
+        where values only need the right distribution, not the seed
+        convention.  ``data`` arguments keep their exact values."""
+        import torch
+        self = cls.__new__(cls)
+        self.kern = kern
+        self.t = {}
+        self.args = {a["name"]: a for a in kern.info["args"]}
+        g = torch.Generator(device=device).manual_seed(seed)
+        for i, (name, a) in enumerate(self.args.items()):
+            if a.get("scalar"):
+                continue
+            n = max(1, int(np.prod(a["shape"])) if a["shape"] else 1)
+            dt = torch_dtype(a["dtype"])
+            if a.get("output"):
+                self.t[name] = torch.zeros(n, dtype=dt, device=device)
+            elif "data" in a:
+                self.t[name] = to_device(materialize(a).reshape(-1), a["dtype"], device)
+            else:
+                d = a.get("dist") or {}
+                x = torch.empty(n, dtype=torch.float32, device=device)
+                if d.get("kind") == "uniform":
+                    x.uniform_(float(d.get("lo", 0.0)), float(d.get("hi", 1.0)), generator=g)
+                else:
+                    x.normal_(0.0, float(d.get("scale", 1.0)), generator=g)
+                self.t[name] = x.to(dt)
+        return self
+
     def ptrs(self) -> dict:
         p = {n: t.data_ptr() for n, t in self.t.items()}
         for name, a in self.args.items():

@@ -269,7 +269,8 @@ def row_reduce(rows: int = 32768, cols: int = 8192, block: int = 256, mean: bool
     """``y[r] = sum_c x[r, c]`` (or the mean, ``/ cols``), x ~ N(0,1)."""
     name = "mean" if mean else "sum_1"
     p = Problem(f"row_{'mean' if mean else 'sum'}_{rows}x{cols}",
-                f"x.{'mean' if mean else 'sum'}(-1)", f"k_{name}_reduce", name)
+                f"x.{'mean' if mean else 'sum'}(-1)",
+                "k_mean_rows_reduce" if mean else "k_sum_rows_reduce", name)
     if mean:
         p.add_const("mean_count", cols)
     p.add_input("x", (rows, cols))
@@ -384,6 +385,12 @@ def config(name: str, **kw) -> Problem:
         "l2norm": l2norm,
     }
     return table[name](**kw)
+
+
+def algorithmic_flops(p: Problem) -> int:
+    """FLOPs of a contraction (``2MNK`` for matmul, ``4 B H S^2 D`` for
+    attention); 0 for memory-bound kernels."""
+    return int((p.oracle or {}).get("flops", 0))
 
 
 def algorithmic_bytes(p: Problem) -> int:

@@ -450,6 +450,15 @@ class RowsTemplate:
             width *= 2
         self._butterfly(chain, env, list(tree.state), list(tree.state_b), tree.combine_states,
                         width)
+        # the butterfly leaves the row total in lanes [0, width); every lane
+        # needs it (pass 2 runs in all threads), so broadcast lane 0's
+        for st in tree.state:
+            b = k.reg("r")
+            k(f"mov.b32 {b}, {chain.value(st)};")
+            k(f"shfl.sync.idx.b32 {b}, {b}, 0, 0x1f, 0xffffffff;")
+            r = k.reg("f")
+            k(f"mov.b32 {r}, {b};")
+            env[st] = r
 
     def _butterfly(self, chain, env, states, states_b, combine, width):
         k = self.k
