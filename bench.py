@@ -52,18 +52,17 @@ def peaks() -> tuple[float, str]:
     return FALLBACK_HBM, "fallback"
 
 
-def profile_traffic(kernel: str):
-    """DRAM bytes per launch from a committed ncu summary
-    (``profiles/<kernel>.md``, line ``traffic_bytes_per_launch: N``)."""
-    f = REPO / "profiles" / f"{kernel}.md"
-    if not f.exists():
-        return None
-    for ln in f.read_text().splitlines():
-        if ln.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return int(ln.split(":", 1)[1].strip())
-            except ValueError:
-                return None
+def profile_traffic(config: str):
+    """DRAM bytes per launch from the committed ncu summary of that
+    configuration's kernel (``profiles/<config>__<entry>.md``, line
+    ``traffic_bytes_per_launch: N``); None when no capture exists."""
+    for f in sorted((REPO / "profiles").glob(f"{config}__*.md")):
+        for ln in f.read_text().splitlines():
+            if ln.strip().startswith("traffic_bytes_per_launch:"):
+                try:
+                    return int(ln.split(":", 1)[1].strip())
+                except ValueError:
+                    return None
     return None
 
 
@@ -333,7 +332,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             continue
         img = native.Image(f.read_text())
         mod = native.Module(img.data)
-        kh = mod.kernel(kerns[n].entry)
+        kh = mod.kernel("ref_" + kerns[n].entry)
         k = kerns[n]
         arr, keep = k.params(ptrs[n])
         zero = [(out_sum.data_ptr(), 4)] if n == "full_sum" else []
@@ -448,7 +447,7 @@ def run_case(args) -> None:
     if f.exists() and not kw:
         img = native.Image(f.read_text())
         mod = native.Module(img.data)
-        kh = mod.kernel(kern.entry)
+        kh = mod.kernel("ref_" + kern.entry)
         ref = harness.CompiledKernel.__new__(harness.CompiledKernel)
         ref.__dict__.update(kern.__dict__)
         ref._module, ref._kernel = mod, kh

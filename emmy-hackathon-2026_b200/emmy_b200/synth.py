@@ -373,6 +373,100 @@ def l2norm(rows: int = 65536, cols: int = 4096, block: int = 128, eps: float = 1
     return p
 
 
+def _div(a, b):
+    return I.BinaryExpr("/", a, b)
+
+
+def _mod(a, b):
+    return I.BinaryExpr("%", a, b)
+
+
+def _lt(a, b):
+    return I.BinaryExpr("<", a, b)
+
+
+_SMEM_CTYPE = {"f32": "float", "bf16": "__nv_bfloat16"}
+
+
+def matmul(M: int = 16384, N: int = 8192, K: int = 4096, dtype: str = "bf16", BM: int = 128,
+           BN: int = 256, BK: int = 64, stages: int = 4, U0: int = 4, U1: int = 64,
+           seeds=(0, 1)) -> Problem:
+    """``C = A @ B`` with A [M,K], B [K,N] ~ U(-1,1) of ``dtype``, C f32, in the
+    schedule form of the reference's ``problems/m01_matmul_512`` IR: a CTA per
+    BM x BN output tile, U0 x U1 threads each owning an (BM/U0) x (BN/U1)
+    register micro-tile, a ``stages``-deep cp.async ring of A/B k-slices in
+    shared memory, and a fully unrolled inner k loop of multiply + Accum."""
+    assert M % BM == 0 and N % BN == 0 and K % BK == 0 and BM % U0 == 0 and BN % U1 == 0
+    mu, nu = BM // U0, BN // U1
+    T = U0 * U1
+    es = 2 if dtype == "bf16" else 4
+    E = 16 // es                            # elements per 16-byte cp.async
+    dt = BF16 if dtype == "bf16" else F32
+    p = Problem(f"matmul_{dtype}_{M}x{N}x{K}", "x0 @ x1", f"k_matmul_{dtype}", "matmul")
+    p.add_input("x0", (M, K), dtype=dtype, dist=UNIF11)
+    p.add_input("x1", (K, N), dtype=dtype, dist=UNIF11)
+    p.out = ("matmul", (M, N), "f32")
+    tid = add(mul(V("a0_u"), Lit(U1)), V("a1_u"))
+
+    def copies(slot, koff):
+        ca, cb = BM * BK // E, BK * BN // E
+        fa = mul(V("_fa"), Lit(E))
+        fb = mul(V("_fb"), Lit(E))
+        la = strided(axis("_fa", ca), tid, T, [I.CpAsyncCopy(
+            "_a_smem", (add(mul(slot, Lit(BM)), _div(fa, Lit(BK))), _mod(fa, Lit(BK))), "x0",
+            (add(mul(V("a0_b"), Lit(BM)), _div(fa, Lit(BK))), add(koff, _mod(fa, Lit(BK)))),
+            16, "NONE", None, None)])
+        lb = strided(axis("_fb", cb), tid, T, [I.CpAsyncCopy(
+            "_b_smem", (add(mul(slot, Lit(BK)), _div(fb, Lit(BN))), _mod(fb, Lit(BN))), "x1",
+            (add(koff, _div(fb, Lit(BN))), add(mul(V("a1_b"), Lit(BN)), _mod(fb, Lit(BN)))),
+            16, "NONE", None, None)])
+        return [la, lb, I.CpAsyncCommit()]
+
+    body = [I.Init(f"acc0__c{i}_{j}", 0.0, F32) for i in range(mu) for j in range(nu)]
+    body += [I.Smem("_a_smem", (stages * BM, BK), _SMEM_CTYPE[dtype], 16),
+             I.Smem("_b_smem", (stages * BK, BN), _SMEM_CTYPE[dtype], 16)]
+    for s in range(stages - 1):
+        body += copies(Lit(s), Lit(s * BK))
+    ks = V("_ks")
+    cur = _mod(_div(ks, Lit(BK)), Lit(stages))
+    nxt = _mod(add(_div(ks, Lit(BK)), Lit(stages - 1)), Lit(stages))
+    ahead = add(ks, Lit((stages - 1) * BK))
+    kpre = I.TernaryExpr(_lt(ahead, Lit(K)), ahead, Lit(K - BK))
+    inner = []
+    for j in range(nu):
+        inner.append(I.Load((f"in1__c0_{j}",), "_b_smem",
+                            (add(mul(cur, Lit(BK)), V("_ki")),
+                             add(mul(V("a1_u"), Lit(nu)), Lit(j))), None))
+    for i in range(mu):
+        inner.append(I.Load((f"in0__c{i}_0",), "_a_smem",
+                            (add(mul(cur, Lit(BM)), add(mul(V("a0_u"), Lit(mu)), Lit(i))),
+                             V("_ki")), None))
+        for j in range(nu):
+            inner.append(assign(f"acc0__v__c{i}_{j}", "multiply", f"in1__c0_{j}", f"in0__c{i}_0"))
+            inner.append(accum(f"acc0__c{i}_{j}", f"acc0__v__c{i}_{j}", axes=("_ki",)))
+    kloop = I.Loop(axis("_ki", BK), tuple(inner), False, False)
+    main = copies(nxt, kpre) + [I.CpAsyncWait(stages - 1), I.Sync(0, None, False), kloop,
+                                I.Sync(0, None, False)]
+    body.append(I.StridedLoop(axis("_ks", K), Lit(0), Lit(BK), tuple(main), False, None, False))
+    for i in range(mu):
+        body.append(write("matmul", (add(add(mul(V("a0_b"), Lit(BM)), mul(V("a0_u"), Lit(mu))),
+                                         Lit(i)),
+                                     add(mul(V("a1_b"), Lit(BN)), mul(V("a1_u"), Lit(nu)))),
+                          tuple(f"acc0__c{i}_{j}" for j in range(nu))))
+    p.body = tile([axis("a0_b", M // BM, parent=("a0", M)), axis("a1_b", N // BN, parent=("a1", N)),
+                   axis("a0_u", U0), axis("a1_u", U1)], body)
+    p.grid, p.block = ((M // BM) * (N // BN), 1, 1), (T, 1, 1)
+    # the IR's ring, plus room for the tcgen05 template's barriers and alignment
+    p.smem = stages * (BM * BK + BK * BN) * es + 2048
+    if dtype == "bf16":
+        p.rtol, p.atol = 2e-2, None
+    else:
+        p.rtol, p.atol = 1e-4, None
+    p.oracle = {"family": "matmul", "args": {"a": "x0", "b": "x1"}, "output": "matmul",
+                "flops": 2 * M * N * K, "bf16": {"x0": dtype == "bf16", "x1": dtype == "bf16"}}
+    return p
+
+
 # the BASELINE.json configurations by name (full sizes)
 def config(name: str, **kw) -> Problem:
     table = {
@@ -383,6 +477,8 @@ def config(name: str, **kw) -> Problem:
         "rmsnorm": rmsnorm,
         "softmax": softmax,
         "l2norm": l2norm,
+        "matmul_bf16": lambda **k: matmul(dtype="bf16", **k),
+        "matmul_f32": lambda **k: matmul(**{"dtype": "f32", "BK": 32, **k}),
     }
     return table[name](**kw)
 

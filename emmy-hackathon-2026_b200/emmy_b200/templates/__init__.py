@@ -1,8 +1,9 @@
 """Hand-written sm_100a kernel templates, tried in order by the compiler."""
 from .common import TemplateMismatch
+from .gemm import GemmTemplate
 from .pointwise import PointwiseTemplate
 from .rows import RowsTemplate
 
-TEMPLATES = [PointwiseTemplate, RowsTemplate]
+TEMPLATES = [PointwiseTemplate, RowsTemplate, GemmTemplate]
 
-__all__ = ["TEMPLATES", "TemplateMismatch", "PointwiseTemplate", "RowsTemplate"]
+__all__ = ["TEMPLATES", "TemplateMismatch", "PointwiseTemplate", "RowsTemplate", "GemmTemplate"]

@@ -99,9 +99,24 @@ def reference_ptx_file(ir_path) -> bytes:
                          json.loads((p.parent / "meta.json").read_text())).encode()
 
 
+REF_PREFIX = "ref_"
+
+
 def emit_reference_ptx(name: str, graph_dict: dict, meta: dict) -> Path:
-    """Write the reference's PTX for a (synthesised) IR to ``oracle/_ref``."""
+    """Write the reference's PTX for a (synthesised) IR to ``oracle/_ref``.
+
+    The KernelOp is renamed ``ref_<entry>`` (in the IR handed to the reference
+    compiler, and in a copy of meta), so a profiler's launch list tells the
+    reference's kernel apart from this build's kernel for the same IR."""
+    import copy
+    g = copy.deepcopy(graph_dict)
+    m = copy.deepcopy(meta)
+    for nd in g["nodes"].values():
+        if nd["op"] == "KernelOp":
+            nd["op_fields"]["name"] = REF_PREFIX + nd["op_fields"]["name"]
+    for kinfo in m["kernels"]:
+        kinfo["entry"] = REF_PREFIX + kinfo["entry"]
     REF_OUT.mkdir(parents=True, exist_ok=True)
     out = REF_OUT / f"{name}.ptx"
-    out.write_bytes(reference_ptx(graph_dict, meta).encode())
+    out.write_bytes(reference_ptx(g, m).encode())
     return out

@@ -1,0 +1,58 @@
+"""Parity on the GPU for the tcgen05 matmul template (bf16 inputs, f32
+accumulate) against the float64 CPU oracle on the same bf16-rounded inputs,
+rel 2e-2 with atol = rtol * max|ref|: small and tile-edge shapes in full, the
+BASELINE shape (M=16384, N=8192, K=4096) on sampled rows.  The kernel's
+bounded waits must not have fired (module status word stays 0)."""
+import numpy as np
+import pytest
+
+from emmy_b200 import synth
+from emmy_b200.data import bf16_to_f32, materialize
+from oracle import expr
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    dict(M=128, N=256, K=64),                    # one tile, one k-step
+    dict(M=256, N=256, K=128),
+    dict(M=512, N=512, K=1024),                  # ring wraps (16 k-steps, 4 stages)
+    dict(M=256, N=256, K=256, BN=128, U0=8, U1=32),
+    dict(M=256, N=512, K=192, BN=64, U0=16, U1=16, BK=64),
+]
+
+
+def _run(p, rows=None):
+    from emmy_b200 import harness
+    g, m = p.build()
+    k = m["kernels"][0]
+    ins = {a["name"]: materialize(a) for a in k["args"] if not a.get("output")}
+    outs, kern = harness.run(g, m, ins)
+    assert kern.kind == "gemm"
+    addr, n = kern.module().global_addr("__emmy_status")
+    import ctypes
+    import torch
+    st = torch.zeros(1, dtype=torch.int32)
+    from emmy_b200 import native
+    native.check(native.lib().emmy_memcpy_dtoh_async(st.data_ptr(), addr, 4, None))
+    torch.cuda.synchronize()
+    assert int(st[0]) == 0, f"bounded wait fired, status {int(st[0])}"
+    a = ins["x0"] if rows is None else ins["x0"][rows]
+    ref = expr.evaluate_family(m["oracle"], {"x0": a, "x1": ins["x1"]})["matmul"]
+    got = outs["matmul"] if rows is None else outs["matmul"][rows]
+    rtol, atol = expr.tolerance(m, ref)
+    err = np.max(np.abs(got - ref))
+    assert np.allclose(got, ref, rtol=rtol, atol=atol), err
+    return got, ref
+
+
+@pytest.mark.parametrize("kw", CASES, ids=[f"{c['M']}x{c['N']}x{c['K']}" for c in CASES])
+def test_gemm_small(kw):
+    got, ref = _run(synth.matmul(**kw))
+    # bf16 products accumulate exactly enough in f32 that the error is tiny
+    assert np.max(np.abs(got - ref)) <= 1e-3 * max(1.0, float(np.max(np.abs(ref))))
+
+
+def test_gemm_baseline_rows():
+    p = synth.matmul()
+    rows = np.sort(np.random.default_rng(3).choice(16384, 48, replace=False))
+    _run(p, rows=rows)
