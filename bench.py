@@ -159,9 +159,10 @@ def cpu_reductions(x_sum, x_rows, threads: int = 1) -> float:
 
 def host_inputs(rank: int):
     import torch
-    g = torch.Generator().manual_seed(1000 * rank + 0)
+    from emmy_b200.dist import rank_seed
+    g = torch.Generator().manual_seed(rank_seed(0, rank))
     x_sum = torch.rand(268_435_456, generator=g, dtype=torch.float32)
-    g.manual_seed(1000 * rank + 1)
+    g.manual_seed(rank_seed(1, rank))
     x_rows = torch.randn(32768, 8192, generator=g, dtype=torch.float32)
     return x_sum, x_rows
 
@@ -200,8 +201,7 @@ def run_reference(args, rank: int, world: int) -> None:
 def run_ours(args, rank: int, world: int, local: int) -> None:
     import numpy as np
     import torch
-    import torch.distributed as dist
-
+    from emmy_b200 import dist as D
     from emmy_b200 import harness, native
 
     torch.cuda.set_device(local)
@@ -246,8 +246,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             launch(n)
         if evs is not None:
             evs[3].record(stream)
-        if world > 1:
-            dist.all_reduce(out_sum)
+        D.global_sum(out_sum)
 
     for _ in range(args.warmup):
         step()
@@ -261,8 +260,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
 
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
+    D.barrier()
     torch.cuda.synchronize()
     with Clocks(local) as clk:
         start.record(stream)
@@ -270,15 +268,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             step(evs[s])
         end.record(stream)
         torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    D.barrier()
     ms = start.elapsed_time(end)
     per = {n: [evs[s][i].elapsed_time(evs[s][i + 1]) for s in range(args.steps)]
            for i, n in enumerate(order)}
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t)
+    ms_max = D.max_over_ranks(ms, device=dev)
     value = step_bytes * world * args.steps / (ms_max / 1e3) / 1e9
 
     # e2e through the C ABI with host buffers: copies in, launch, result out
@@ -308,21 +302,17 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     for n in order:  # warm
         harness.run_host(kerns[n], host[n], devt[n], sh)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
+    D.barrier()
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(e2e_steps):
         for n in order:
             harness.run_host(kerns[n], host[n], devt[n], sh)
-        if world > 1:
-            dist.all_reduce(out_sum)
+        D.global_sum(out_sum)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_val = step_bytes * world * e2e_steps / (float(e2e_ms) / 1e3) / 1e9
+    e2e_ms = D.max_over_ranks(e0.elapsed_time(e1), device=dev)
+    e2e_val = step_bytes * world * e2e_steps / (e2e_ms / 1e3) / 1e9
 
     # reference compiler's PTX for the same IRs, JIT-run on this GPU
     ref_ptx = {}
@@ -480,20 +470,15 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    from emmy_b200 import dist as D
     if world > 1:
-        import datetime
-
         import torch
-        import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        D.init("nccl", D.from_env(), timeout_s=120, device=torch.device("cuda", local))
     try:
         run_ours(args, rank, world, local)
     finally:
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
+        D.finish()
 
 
 if __name__ == "__main__":

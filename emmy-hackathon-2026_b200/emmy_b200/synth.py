@@ -389,7 +389,7 @@ _SMEM_CTYPE = {"f32": "float", "bf16": "__nv_bfloat16"}
 
 
 def matmul(M: int = 16384, N: int = 8192, K: int = 4096, dtype: str = "bf16", BM: int = 128,
-           BN: int = 256, BK: int = 64, stages: int = 4, U0: int = 4, U1: int = 64,
+           BN: int = 256, BK: int = 64, stages: int = 2, U0: int = 4, U1: int = 64,
            seeds=(0, 1)) -> Problem:
     """``C = A @ B`` with A [M,K], B [K,N] ~ U(-1,1) of ``dtype``, C f32, in the
     schedule form of the reference's ``problems/m01_matmul_512`` IR: a CTA per

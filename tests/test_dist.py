@@ -1,0 +1,83 @@
+"""The multi-rank host logic on CPU: two gloo ranks, each reducing its own
+shard, finished by the all-reduce (the global-sum exchange of the path);
+max-over-ranks timing; shard ranges; and a rank that never joins makes the
+other's collective fail inside the process-group timeout instead of
+hanging."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from emmy_b200 import dist as D
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port),
+                       "RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank)})
+    import torch
+    r = D.from_env()
+    D.init("gloo", r, timeout_s=30)
+    n = 1 << 16
+    lo, hi = D.shard_range(n, r.rank, r.world)
+    x = np.random.default_rng(D.rank_seed(0, 0)).uniform(0, 1, n).astype(np.float32)
+    part = torch.tensor([x[lo:hi].astype(np.float64).sum()], dtype=torch.float64)
+    D.global_sum(part)
+    mx = D.max_over_ranks(float(rank + 1))
+    q.put((rank, float(part), mx, float(x.astype(np.float64).sum())))
+    D.barrier()
+    D.finish()
+
+
+def test_two_rank_global_sum():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, total, mx, ref in res:
+        assert abs(total - ref) <= 1e-9 * ref
+        assert mx == 2.0
+
+
+def _lonely(port, q):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port),
+                       "RANK": "0", "WORLD_SIZE": "2", "LOCAL_RANK": "0"})
+    try:
+        D.init("gloo", D.from_env(), timeout_s=3)
+        q.put("joined")
+    except Exception as e:  # the peer never joins: rendezvous times out
+        q.put(type(e).__name__)
+
+
+def test_missing_rank_times_out():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_lonely, args=(_port(), q))
+    p.start()
+    out = q.get(timeout=120)
+    p.join(timeout=60)
+    assert out != "joined"
+
+
+@pytest.mark.parametrize("n,world", [(10, 3), (32768, 8), (5, 8), (0, 2)])
+def test_shard_ranges_cover(n, world):
+    seen = []
+    for r in range(world):
+        a, b = D.shard_range(n, r, world)
+        seen.extend(range(a, b))
+    assert seen == list(range(n))
