@@ -312,7 +312,7 @@ int emmy_tensormap_encode(void *tmap, int dtype, int rank, uint64_t gaddr,
                           const uint32_t *box, int swizzle) {
   if (!tmap || rank < 1 || rank > 5 || !dims || !box || (rank > 1 && !strides))
     return fail(EMMY_EINVAL, "emmy_tensormap_encode: bad argument");
-  if (dtype < 0 || dtype > 10 || swizzle < 0 || swizzle > 3)
+  if (dtype < 0 || dtype > 10 || swizzle < 0 || swizzle > 6)
     return fail(EMMY_EINVAL, "emmy_tensormap_encode: dtype %d / swizzle %d", dtype, swizzle);
   if (gaddr % 16 != 0) return fail(EMMY_EINVAL, "tensor map base %#llx not 16-byte aligned",
                                    static_cast<unsigned long long>(gaddr));
@@ -329,8 +329,11 @@ int emmy_tensormap_encode(void *tmap, int dtype, int rank, uint64_t gaddr,
     es[i] = 1;
     if (i + 1 < rank) s[i] = strides[i];
   }
-  static const CUtensorMapSwizzle sw[4] = {CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
-                                          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_SWIZZLE_128B};
+  static const CUtensorMapSwizzle sw[7] = {
+      CU_TENSOR_MAP_SWIZZLE_NONE,          CU_TENSOR_MAP_SWIZZLE_32B,
+      CU_TENSOR_MAP_SWIZZLE_64B,           CU_TENSOR_MAP_SWIZZLE_128B,
+      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B_FLIP_8B,
+      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_64B};
   CU(g_drv.TensorMapEncodeTiled(reinterpret_cast<CUtensorMap *>(tmap),
                                 static_cast<CUtensorMapDataType>(dtype), rank,
                                 reinterpret_cast<void *>(gaddr), d, s, b, es,

@@ -478,7 +478,7 @@ def config(name: str, **kw) -> Problem:
         "softmax": softmax,
         "l2norm": l2norm,
         "matmul_bf16": lambda **k: matmul(dtype="bf16", **k),
-        "matmul_f32": lambda **k: matmul(**{"dtype": "f32", "BK": 32, **k}),
+        "matmul_f32": lambda **k: matmul(**{"dtype": "f32", "BK": 32, "stages": 4, **k}),
     }
     return table[name](**kw)
 

@@ -20,9 +20,16 @@ IR's CTA -> output-tile assignment and computes each tile with:
   32*(w%4)..+31, i.e. output rows) and writing 32-byte ``st.global.v8`` rows.
 
 A is K-major ([M,K] row-major) and B MN-major ([K,N] row-major), both with
-the 128-byte swizzle; the shared-memory matrix descriptors follow the UMMA
-canonical layouts (K-major: 8-row groups 1024 B apart; MN-major: 64-element
-N blocks ``BK*128`` B apart, 8-row K groups 1024 B apart).
+a 128-byte swizzle; the shared-memory matrix descriptors follow the UMMA
+canonical layouts (K-major: 8-row groups 1024 B apart; MN-major 16-bit:
+64-element N blocks ``BK*128`` B apart, 8-row K groups 1024 B apart;
+MN-major 32-bit (tf32): the 128-byte swizzle with 32-byte atoms, 32-element N
+blocks ``BK*128`` B apart, 4-row K groups 512 B apart).
+
+fp32 operands take the 3xTF32 route: four converter warps split each landed
+k-slice into tf32 high and low parts in shared memory and the MMA thread
+issues ``kind::tf32`` MMAs for lo*hi, hi*lo and hi*hi (the lo*lo term,
+below 2^-22 relative, is dropped).
 
 Every mbarrier wait is bounded by ``%globaltimer`` (2 s); on expiry the
 kernel records a code in the module-scope word ``__emmy_status`` (1 producer,
@@ -48,15 +55,18 @@ SMEM_LIMIT = 227 * 1024       # max dynamic shared memory per CTA on sm_100
 def _desc_hi(lbo: int, sbo: int, swizzle_code: int = 2) -> int:
     """Constant part of a UMMA shared-memory descriptor: leading/stride byte
     offsets (>>4), descriptor version 1 (bits 46-47), layout type at 61-63
-    (2 = 128-byte swizzle); the start address (>>4) is added at run time."""
+    (2 = 128-byte swizzle with 16-byte atoms, 1 = 128-byte swizzle with
+    32-byte atoms); the start address (>>4) is added at run time."""
     return ((lbo >> 4) << 16) | ((sbo >> 4) << 32) | (1 << 46) | (swizzle_code << 61)
 
 
-def idesc_f16(M: int, N: int, b_mn_major: bool) -> int:
-    """Instruction descriptor of ``tcgen05.mma .kind::f16``: f32 accumulator
-    (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12 = 1), A K-major, B major-ness
-    at bit 16, N>>3 at bits 17-22, M>>4 at bits 24-28."""
-    return (1 << 4) | (1 << 7) | (1 << 10) | (int(b_mn_major) << 16) | ((N >> 3) << 17) \
+def idesc_mma(M: int, N: int, b_mn_major: bool, tf32: bool = False) -> int:
+    """Instruction descriptor of ``tcgen05.mma`` (kind::f16 / kind::tf32): f32
+    accumulator (bits 4-5 = 1), A and B format at bits 7-9 / 10-12 (1 = bf16,
+    2 = tf32), A K-major, B major-ness at bit 16, N>>3 at bits 17-22, M>>4 at
+    bits 24-28."""
+    fmt = 2 if tf32 else 1
+    return (1 << 4) | (fmt << 7) | (fmt << 10) | (int(b_mn_major) << 16) | ((N >> 3) << 17) \
         | ((M >> 4) << 24)
 
 
@@ -160,37 +170,53 @@ class GemmTemplate:
         if (BM, BN) == (None, None) or ext["a0_b"] * BM != M or ext["a1_b"] * BN != N:
             raise TemplateMismatch("tile does not cover the output")
         dts = {bufs.dtypes[A], bufs.dtypes[B]}
-        if dts != {"bf16"}:
-            raise TemplateMismatch(f"operand dtype {dts} (bf16 path)")
+        if dts == {"bf16"}:
+            mode = "bf16"
+        elif dts == {"f32"}:
+            mode = "tf32x3"
+        else:
+            raise TemplateMismatch(f"operand dtypes {dts}")
         threads = ctx.threads
         if ctx.block != (threads, 1, 1) or threads != 256:
             raise TemplateMismatch("tcgen05 template runs 256-thread CTAs")
         if ctx.grid[0] * ctx.grid[1] * ctx.grid[2] != ext["a0_b"] * ext["a1_b"]:
             raise TemplateMismatch("grid is not one CTA per output tile")
-        if BM != 128 or BN % 64 or not 64 <= BN <= 256 or K % 64:
-            raise TemplateMismatch(f"tile {BM}x{BN}, K={K} outside the tcgen05 shapes")
         self = cls()
+        self.mode = mode
+        self.esize = 2 if mode == "bf16" else 4
+        self.BK = 128 // self.esize          # one 128-byte swizzle row of K per stage
+        self.box_n = 128 // self.esize       # B loaded as 128-byte-wide column boxes
+        if BM != 128 or BN % self.box_n or not 64 <= BN <= 256 or BN % 16 or K % self.BK:
+            raise TemplateMismatch(f"tile {BM}x{BN}, K={K} outside the tcgen05 shapes")
         self.ctx, self.A, self.B, self.C = ctx, A, B, C
         self.M, self.N, self.K, self.BM, self.BN = M, N, K, BM, BN
-        self.BK = 64
-        self.esize = 2
-        stage = (BM * self.BK + self.BK * BN) * self.esize
+        raw = (BM * self.BK + self.BK * BN) * self.esize
+        # 3xTF32 keeps a low-part copy of each operand slice next to it
+        stage = raw * (2 if mode == "tf32x3" else 1)
         self.stage_bytes = stage
         avail = min(ctx.smem_bytes, SMEM_LIMIT) - 1024 - 256
         self.S = min(6, avail // stage)
         if self.S < 2:
             raise TemplateMismatch("meta smem_bytes too small for a 2-stage ring")
         self.NB = ext["a1_b"]
+        self.hw_trunc = False
         return self
 
     # ------------------------------------------------------------------- emit
     def emit(self) -> str:
         ctx = self.ctx
         BM, BN, BK, S, K = self.BM, self.BN, self.BK, self.S, self.K
+        es = self.esize
+        tf32 = self.mode == "tf32x3"
         KT = K // BK
-        SA = BM * BK * 2                 # A stage bytes (16 KB)
-        SB = BK * BN * 2                 # B stage bytes
-        NBOX = BN // 64                  # B loaded as 64-column boxes
+        SA = BM * BK * es                # A slice bytes (16 KiB)
+        SB = BK * BN * es                # B slice bytes
+        RAW = SA + SB
+        STG = self.stage_bytes           # raw (+ low parts) per stage
+        BOXN = self.box_n
+        NBOX = BN // BOXN
+        KMMA = 32 // es                  # K per tcgen05.mma (32 bytes of K)
+        tm_dtype = 9 if not tf32 else 7  # CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 / FLOAT32
         params = ctx.params() + [("tmapA", ".align 64 .b8", "[128]"),
                                  ("tmapB", ".align 64 .b8", "[128]")]
         k = Kernel(ctx.entry, params)
@@ -198,11 +224,14 @@ class GemmTemplate:
         k.decl(".extern .shared .align 1024 .b8 __emmy_smem[];")
         k.decl(".global .align 4 .u32 __emmy_status;")
         # host-built tensor maps (innermost dimension first)
-        k.directive(f"tmap tmapA buf={self.A} dtype=9 dims={K},{self.M} strides={K * 2} "
-                    f"box={BK},{BM} swizzle=3")
-        k.directive(f"tmap tmapB buf={self.B} dtype=9 dims={self.N},{K} strides={self.N * 2} "
-                    f"box=64,{BK} swizzle=3")
-        k.comment(f"emmy-b200 template: tcgen05 gemm bf16 M={self.M} N={self.N} K={K} "
+        k.directive(f"tmap tmapA buf={self.A} dtype={tm_dtype} dims={K},{self.M} "
+                    f"strides={K * es} box={BK},{BM} swizzle=3")
+        # MN-major 32-bit operands need the 128-byte swizzle with 32-byte atoms
+        # (4-row K groups); 16-bit ones use the plain 128-byte swizzle
+        b_swz = 4 if tf32 else 3
+        k.directive(f"tmap tmapB buf={self.B} dtype={tm_dtype} dims={self.N},{K} "
+                    f"strides={self.N * es} box={BOXN},{BK} swizzle={b_swz}")
+        k.comment(f"emmy-b200 template: tcgen05 gemm {self.mode} M={self.M} N={self.N} K={K} "
                   f"tile {BM}x{BN}x{BK} stages={S}")
         cbase = k.param_ptr(self.C)
         ta = k.reg("rd")
@@ -225,31 +254,31 @@ class GemmTemplate:
         k(f"mul.lo.u32 {m0}, {mblk}, {BM};")
         n0 = k.reg("r")
         k(f"mul.lo.u32 {n0}, {nblk}, {BN};")
-        # shared memory layout (1024-aligned base): A ring, B ring, barriers
+        # shared memory (1024-aligned base): S stages of [A | B (| A_lo | B_lo)],
+        # then mbarriers: full[S], empty[S], conv[S] (3xTF32), accum, tmem slot
         raw = k.reg("r")
         k(f"mov.u32 {raw}, __emmy_smem;")
-        base = k.reg("r")
-        k(f"add.u32 {base}, {raw}, 1023;")
-        k(f"and.b32 {base}, {base}, -1024;")
-        a_ring = base
-        b_ring = k.reg("r")
-        k(f"add.u32 {b_ring}, {base}, {S * SA};")
+        ring = k.reg("r")
+        k(f"add.u32 {ring}, {raw}, 1023;")
+        k(f"and.b32 {ring}, {ring}, -1024;")
         bars = k.reg("r")
-        k(f"add.u32 {bars}, {b_ring}, {S * SB};")
-        # full[s] at bars + 8s, empty[s] at bars + 8(S+s), accum at bars + 16S,
-        # tmem address slot at bars + 16S + 8
+        k(f"add.u32 {bars}, {ring}, {S * STG};")
+        nb = 3 * S if tf32 else 2 * S
         accb = k.reg("r")
-        k(f"add.u32 {accb}, {bars}, {16 * S};")
+        k(f"add.u32 {accb}, {bars}, {8 * nb};")
         tslot = k.reg("r")
-        k(f"add.u32 {tslot}, {bars}, {16 * S + 8};")
+        k(f"add.u32 {tslot}, {accb}, 8;")
         status = k.reg("rd")
         k(f"mov.u64 {status}, __emmy_status;")
         p0 = k.reg("p")
         k(f"setp.eq.u32 {p0}, {tid}, 0;")
         skip_init = k.label("SKIP_INIT")
         k(f"@!{p0} bra {skip_init};")
-        for s in range(2 * S + 1):
+        for s in range(2 * S):
             k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 1;")
+        for s in range(2 * S, nb):       # conv[s]: the 128 converter threads arrive
+            k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 128;")
+        k(f"mbarrier.init.shared::cta.b64 [{accb}], 1;")
         k("fence.mbarrier_init.release.cluster;")
         k(f"prefetch.tensormap [{ta}];")
         k(f"prefetch.tensormap [{tb}];")
@@ -258,7 +287,8 @@ class GemmTemplate:
         k(f"setp.eq.u32 {pw1}, {warp}, 1;")
         skip_alloc = k.label("SKIP_ALLOC")
         k(f"@!{pw1} bra {skip_alloc};")
-        k(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{tslot}], {max(32, BN)};")
+        ncols = max(32, 1 << (BN - 1).bit_length())
+        k(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{tslot}], {ncols};")
         k("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;")
         k.mark(skip_alloc)
         k("tcgen05.fence::before_thread_sync;")
@@ -267,53 +297,68 @@ class GemmTemplate:
         tmem = k.reg("r")
         k(f"ld.shared.u32 {tmem}, [{tslot}];")
         teardown = k.label("TEARDOWN")
-
-        # ---------------- producer: warp 0, lane 0 ----------------
         pl0 = k.reg("p")
         k(f"setp.eq.u32 {pl0}, {lane}, 0;")
+        kt, st, ph = k.reg("r"), k.reg("r"), k.reg("r")
+
+        def bar_addr(group, stage_reg):
+            r = k.reg("r")
+            k(f"mad.lo.u32 {r}, {stage_reg}, 8, {bars};")
+            if group:
+                k(f"add.u32 {r}, {r}, {8 * S * group};")
+            return r
+
+        def stage_base(stage_reg):
+            r = k.reg("r")
+            k(f"mad.lo.u32 {r}, {stage_reg}, {STG}, {ring};")
+            return r
+
+        def loop_head(label):
+            k(f"mov.u32 {kt}, 0;")
+            k(f"mov.u32 {st}, 0;")
+            k(f"mov.u32 {ph}, 0;")
+            top = k.label(label)
+            k.mark(top)
+            return top
+
+        def loop_tail(top):
+            self._advance(k, st, ph, S)
+            k(f"add.u32 {kt}, {kt}, 1;")
+            pl = k.reg("p")
+            k(f"setp.lt.u32 {pl}, {kt}, {KT};")
+            k(f"@{pl} bra {top};")
+
+        # ---------------- producer: warp 0, lane 0 ----------------
         pprod = k.reg("p")
         k(f"setp.eq.u32 {pprod}, {warp}, 0;")
         k(f"and.pred {pprod}, {pprod}, {pl0};")
         end_prod = k.label("END_PROD")
         k(f"@!{pprod} bra {end_prod};")
-        kt = k.reg("r")
-        st = k.reg("r")
-        ph = k.reg("r")
-        k(f"mov.u32 {kt}, 0;")
-        k(f"mov.u32 {st}, 0;")
-        k(f"mov.u32 {ph}, 0;")
-        top = k.label("PROD")
-        k.mark(top)
-        eb = k.reg("r")
-        k(f"mad.lo.u32 {eb}, {st}, 8, {bars};")
-        k(f"add.u32 {eb}, {eb}, {8 * S};")
+        top = loop_head("PROD")
         par = k.reg("r")
         k(f"xor.b32 {par}, {ph}, 1;")
-        self._wait(k, eb, par, status, 1, end_prod)
-        fb = k.reg("r")
-        k(f"mad.lo.u32 {fb}, {st}, 8, {bars};")
-        k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {SA + SB};")
+        self._wait(k, bar_addr(1, st), par, status, 1, end_prod)
+        fb = bar_addr(0, st)
+        k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {RAW};")
         kc = k.reg("r")
         k(f"mul.lo.u32 {kc}, {kt}, {BK};")
-        da = k.reg("r")
-        k(f"mad.lo.u32 {da}, {st}, {SA}, {a_ring};")
+        da = stage_base(st)
         k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
           f"[{da}], [{ta}, {{{kc}, {m0}}}], [{fb}];")
-        dbb = k.reg("r")
-        k(f"mad.lo.u32 {dbb}, {st}, {SB}, {b_ring};")
         for i in range(NBOX):
             nx = k.reg("r")
-            k(f"add.u32 {nx}, {n0}, {64 * i};")
+            k(f"add.u32 {nx}, {n0}, {BOXN * i};")
             db = k.reg("r")
-            k(f"add.u32 {db}, {dbb}, {i * BK * 128};")
+            k(f"add.u32 {db}, {da}, {SA + i * BK * 128};")
             k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
               f"[{db}], [{tb}, {{{nx}, {kc}}}], [{fb}];")
-        self._advance(k, st, ph, S)
-        k(f"add.u32 {kt}, {kt}, 1;")
-        pl = k.reg("p")
-        k(f"setp.lt.u32 {pl}, {kt}, {KT};")
-        k(f"@{pl} bra {top};")
+        loop_tail(top)
         k.mark(end_prod)
+
+        # ---------------- 3xTF32 converters: warps 4-7 ----------------
+        if tf32:
+            self._converters(k, warp, tid, bar_addr, stage_base, loop_head, loop_tail, status,
+                             RAW, st, ph)
 
         # ---------------- MMA issuer: warp 1, lane 0 ----------------
         pmma = k.reg("p")
@@ -322,47 +367,46 @@ class GemmTemplate:
         end_mma = k.label("END_MMA")
         k(f"@!{pmma} bra {end_mma};")
         idesc = k.reg("r")
-        k(f"mov.u32 {idesc}, {idesc_f16(BM, BN, True)};")
+        k(f"mov.u32 {idesc}, {idesc_mma(BM, BN, True, tf32)};")
         hiA = _desc_hi(16, 1024)
-        hiB = _desc_hi(BK * 128, 1024)
-        k(f"mov.u32 {kt}, 0;")
-        k(f"mov.u32 {st}, 0;")
-        k(f"mov.u32 {ph}, 0;")
-        top2 = k.label("MMA")
-        k.mark(top2)
-        fb2 = k.reg("r")
-        k(f"mad.lo.u32 {fb2}, {st}, 8, {bars};")
-        self._wait(k, fb2, ph, status, 2, end_mma)
+        hiB = _desc_hi(BK * 128, 512, 1) if tf32 else _desc_hi(BK * 128, 1024)
+        top2 = loop_head("MMA")
+        self._wait(k, bar_addr(2 if tf32 else 0, st), ph, status, 2, end_mma)
         k("tcgen05.fence::after_thread_sync;")
-        aad = k.reg("r")
-        k(f"mad.lo.u32 {aad}, {st}, {SA}, {a_ring};")
+        sb = stage_base(st)
         bad = k.reg("r")
-        k(f"mad.lo.u32 {bad}, {st}, {SB}, {b_ring};")
-        adesc = self._desc(k, aad, hiA)
+        k(f"add.u32 {bad}, {sb}, {SA};")
+        adesc = self._desc(k, sb, hiA)
         bdesc = self._desc(k, bad, hiB)
+        if tf32:
+            lad = k.reg("r")
+            k(f"add.u32 {lad}, {sb}, {RAW};")
+            lbd = k.reg("r")
+            k(f"add.u32 {lbd}, {sb}, {RAW + SA};")
+            ldesc_a = self._desc(k, lad, hiA)
+            ldesc_b = self._desc(k, lbd, hiB)
         pacc = k.reg("p")
         k(f"setp.ne.u32 {pacc}, {kt}, 0;")
-        for kk in range(BK // 16):
-            ad = k.reg("rd")
-            k(f"add.s64 {ad}, {adesc}, {kk * 2};")          # +32 bytes along K
-            bd = k.reg("rd")
-            k(f"add.s64 {bd}, {bdesc}, {kk * 128};")        # +16 rows * 128 bytes
-            pa = pacc if kk == 0 else "1"
-            if kk == 0:
-                k(f"tcgen05.mma.cta_group::1.kind::f16 [{tmem}], {ad}, {bd}, {idesc}, {pa};")
-            else:
-                pt = k.reg("p")
-                k(f"setp.eq.u32 {pt}, 0, 0;")
-                k(f"tcgen05.mma.cta_group::1.kind::f16 [{tmem}], {ad}, {bd}, {idesc}, {pt};")
-        eb2 = k.reg("r")
-        k(f"mad.lo.u32 {eb2}, {st}, 8, {bars};")
-        k(f"add.u32 {eb2}, {eb2}, {8 * S};")
-        k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{eb2}];")
-        self._advance(k, st, ph, S)
-        k(f"add.u32 {kt}, {kt}, 1;")
-        pl2 = k.reg("p")
-        k(f"setp.lt.u32 {pl2}, {kt}, {KT};")
-        k(f"@{pl2} bra {top2};")
+        ptrue = k.reg("p")
+        k(f"setp.eq.u32 {ptrue}, 0, 0;")
+        kind_ = "tf32" if tf32 else "f16"
+        first = True
+        for kk in range(BK // KMMA):
+            ao, bo = kk * 2, kk * KMMA * 8   # +32 B along K (A); +KMMA rows of 128 B (B)
+            pairs = [(adesc, bdesc)]
+            if tf32:   # small terms first: lo*hi + hi*lo, then hi*hi
+                pairs = [(ldesc_a, bdesc), (adesc, ldesc_b), (adesc, bdesc)]
+            for da_, db_ in pairs:
+                ad = k.reg("rd")
+                k(f"add.s64 {ad}, {da_}, {ao};")
+                bd = k.reg("rd")
+                k(f"add.s64 {bd}, {db_}, {bo};")
+                pa = pacc if first else ptrue
+                first = False
+                k(f"tcgen05.mma.cta_group::1.kind::{kind_} [{tmem}], {ad}, {bd}, {idesc}, {pa};")
+        k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+          f"[{bar_addr(1, st)}];")
+        loop_tail(top2)
         k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{accb}];")
         k.mark(end_mma)
 
@@ -383,7 +427,7 @@ class GemmTemplate:
         col = k.reg("r")
         k(f"mad.lo.u32 {col}, {h}, {half}, {n0};")
         taddr = k.reg("r")
-        k(f"shl.b32 {taddr}, {q}, 21;")              # (32*q) << 16
+        k(f"shl.b32 {taddr}, {q}, 21;")              # (32*q) << 16: TMEM lane field
         hc = k.reg("r")
         k(f"mul.lo.u32 {hc}, {h}, {half};")
         k(f"add.u32 {taddr}, {taddr}, {hc};")
@@ -395,14 +439,15 @@ class GemmTemplate:
         k(f"add.s64 {off}, {off}, {c2};")
         cptr = k.reg("rd")
         k(f"add.s64 {cptr}, {cbase}, {off};")
-        for c in range(half // 32):
-            regs = k.regs("r", 32)
+        chunk = 32 if half % 32 == 0 else 16 if half % 16 == 0 else 8
+        for c in range(half // chunk):
+            regs = k.regs("r", chunk)
             ta2 = k.reg("r")
-            k(f"add.u32 {ta2}, {taddr}, {32 * c};")
-            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{ta2}];")
+            k(f"add.u32 {ta2}, {taddr}, {chunk * c};")
+            k(f"tcgen05.ld.sync.aligned.32x32b.x{chunk}.b32 {{{', '.join(regs)}}}, [{ta2}];")
             k("tcgen05.wait::ld.sync.aligned;")
-            for v in range(4):
-                k(f"st.global.v8.b32 [{cptr}+{128 * c + 32 * v}], "
+            for v in range(chunk // 8):
+                k(f"st.global.v8.b32 [{cptr}+{4 * chunk * c + 32 * v}], "
                   f"{{{', '.join(regs[8 * v:8 * v + 8])}}};")
         # ---------------- teardown ----------------
         # reached converged, or (after a timed-out wait) diverged: the
@@ -415,10 +460,51 @@ class GemmTemplate:
         k(f"@!{pw1} bra {end};")
         k("bar.warp.sync 0xffffffff;")
         k("tcgen05.fence::after_thread_sync;")
-        k(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tmem}, {max(32, BN)};")
+        k(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tmem}, {ncols};")
         k.mark(end)
         k("ret;")
         return k.render()
+
+    def _converters(self, k, warp, tid, bar_addr, stage_base, loop_head, loop_tail, status,
+                    RAW, st, ph):
+        """Warps 4-7 split every landed stage for 3xTF32: for each f32 x of the
+        A and B slices, hi = cvt.rna.tf32(x) is written back in place and
+        lo = cvt.rna.tf32(x - hi) into the stage's low-part area (the same
+        swizzled layout, so the same descriptors apply).  x - hi is exact in
+        f32; the dropped lo*lo term is below 2^-22 relative.  Then
+        ``fence.proxy.async`` makes the generic-proxy stores visible to the
+        tensor core's async-proxy reads before the conv[s] arrive."""
+        pc = k.reg("p")
+        k(f"setp.ge.u32 {pc}, {warp}, 4;")
+        end_conv = k.label("END_CONV")
+        k(f"@!{pc} bra {end_conv};")
+        ct = k.reg("r")
+        k(f"sub.u32 {ct}, {tid}, 128;")               # converter thread 0..127
+        off0 = k.reg("r")
+        k(f"shl.b32 {off0}, {ct}, 4;")                # 16 bytes per thread per pass
+        top = loop_head("CONV")
+        self._wait(k, bar_addr(0, st), ph, status, 4, end_conv)
+        sb = stage_base(st)
+        a0 = k.reg("r")
+        k(f"add.u32 {a0}, {sb}, {off0};")
+        per = RAW // (16 * 128)
+        for i in range(per):
+            x = k.regs("r", 4)
+            ad = f"{a0}+{i * 2048}" if i else a0
+            k(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{ad}];")
+            hi = k.regs("r", 4)
+            lo = k.regs("r", 4)
+            for j in range(4):
+                k(f"cvt.rna.tf32.f32 {hi[j]}, {x[j]};")
+                d = k.reg("f")
+                k(f"sub.rn.f32 {d}, {x[j]}, {hi[j]};")
+                k(f"cvt.rna.tf32.f32 {lo[j]}, {d};")
+            k(f"st.shared.v4.b32 [{ad}], {{{', '.join(hi)}}};")
+            k(f"st.shared.v4.b32 [{a0}+{RAW + i * 2048}], {{{', '.join(lo)}}};")
+        k("fence.proxy.async.shared::cta;")
+        k(f"mbarrier.arrive.shared::cta.b64 _, [{bar_addr(2, st)}];")
+        loop_tail(top)
+        k.mark(end_conv)
 
     @staticmethod
     def _advance(k, st, ph, S):

@@ -95,7 +95,9 @@ EMMY_API int emmy_module_global(emmy_module_t mod, const char *name, uint64_t *d
 /* (128 bytes, written to `tmap`).  dtype: 0=u8 1=u16 2=u32 3=i32 4=u64       */
 /* 5=i64 6=f16 7=f32 8=f64 9=bf16 10=tf32 (CUtensorMapDataType numbering).    */
 /* dims/strides are innermost-first; strides[i] is the byte stride of        */
-/* dimension i+1 (rank-1 values).  swizzle: 0 none, 1 32B, 2 64B, 3 128B.    */
+/* dimension i+1 (rank-1 values).  swizzle (CUtensorMapSwizzle numbering):  */
+/* 0 none, 1 32B, 2 64B, 3 128B, 4 128B with 32B atoms, 5 the same with the */
+/* 8-byte flip, 6 128B with 64B atoms.                                       */
 /* ------------------------------------------------------------------------ */
 EMMY_API int emmy_tensormap_encode(void *tmap, int dtype, int rank, uint64_t gaddr,
                           const uint64_t *dims, const uint64_t *strides,

@@ -56,3 +56,21 @@ def test_gemm_baseline_rows():
     p = synth.matmul()
     rows = np.sort(np.random.default_rng(3).choice(16384, 48, replace=False))
     _run(p, rows=rows)
+
+
+F32_CASES = [dict(M=128, N=256, K=32), dict(M=256, N=256, K=128), dict(M=512, N=512, K=1024),
+             dict(M=256, N=256, K=256, BN=128, U0=8, U1=32)]
+
+
+@pytest.mark.parametrize("kw", F32_CASES, ids=[f"{c['M']}x{c['N']}x{c['K']}" for c in F32_CASES])
+def test_gemm_f32_3xtf32(kw):
+    """fp32 inputs through the 3xTF32 split: rel 1e-4 (BASELINE), and in
+    practice close to fp32 accuracy (checked at 2e-5 of max|C|)."""
+    got, ref = _run(synth.config("matmul_f32", **kw))
+    assert np.max(np.abs(got - ref)) <= 2e-5 * max(1.0, float(np.max(np.abs(ref))))
+
+
+def test_gemm_f32_baseline_rows():
+    p = synth.config("matmul_f32")
+    rows = np.sort(np.random.default_rng(4).choice(16384, 32, replace=False))
+    _run(p, rows=rows)
