@@ -58,6 +58,7 @@ class Kernel:
         self.directives: list[str] = []
         self.label_n = 0
         self.maxntid = None
+        self.maxnreg = None
         self.minnctapersm = None
         self.reqnctapercluster = None
 
@@ -131,6 +132,8 @@ class Kernel:
         perf = []
         if self.maxntid:
             perf.append(".maxntid " + ", ".join(str(x) for x in self.maxntid))
+        if self.maxnreg:
+            perf.append(f".maxnreg {self.maxnreg}")
         if self.minnctapersm:
             perf.append(f".minnctapersm {self.minnctapersm}")
         if self.reqnctapercluster:

@@ -467,6 +467,85 @@ def matmul(M: int = 16384, N: int = 8192, K: int = 4096, dtype: str = "bf16", BM
     return p
 
 
+def attention(B: int = 8, H: int = 32, S: int = 4096, D: int = 128, BM: int = 128,
+              U0: int = 8, U1: int = 32, dtype: str = "bf16") -> Problem:
+    """``O = softmax(Q K^T / sqrt(D)) V`` per (batch, head), non-causal, Q/K/V
+    [B,H,S,D] ~ N(0,1) of ``dtype``, O f32, in the schedule form of the
+    reference's ``problems/a01_attention`` / ``a02_attention_128`` IRs (a CTA per
+    BM query rows x all D output columns, U0 x U1 threads each owning a
+    (BM/U0) x (D/U1) micro-tile; per key: the q.k dot product loop, the online
+    softmax chain with the ``acc1`` max / ``acc3`` sum / ``acc5`` weighted-sum
+    accumulators, then ``reciprocal`` + ``multiply``), extended with leading
+    batch and head axes and indexing K[b,h,s,d] directly (the reference's open
+    problems pre-transpose K)."""
+    assert S % BM == 0 and BM % U0 == 0 and D % U1 == 0
+    mu, nu = BM // U0, D // U1
+    dt = BF16 if dtype == "bf16" else F32
+    p = Problem(f"attention_{dtype}_{B}x{H}x{S}x{D}", "softmax(q @ k^T / sqrt(d)) @ v",
+                f"k_attention_{dtype}_d{D}", "matmul_1")
+    p.add_const("div_c1", math.sqrt(D))
+    for i, n in enumerate(("q", "k", "v")):
+        p.add_input(n, (B, H, S, D), dtype=dtype)
+    p.out = ("matmul_1", (B, H, S, D), "f32")
+    bh = (V("ab"), V("ah"))
+
+    def row(i):
+        return add(add(mul(V("a0_b"), Lit(BM)), mul(V("a0_u"), Lit(mu))), Lit(i))
+
+    def col(j):
+        return add(add(mul(V("a5_b"), Lit(D)), mul(V("a5_u"), Lit(nu))), Lit(j))
+
+    key_body = []
+    for i in range(mu):
+        key_body.append(I.Loop(axis("a2", D), (
+            I.Load((f"in2__ar{i}",), "q", bh + (row(i), V("a2")), dt),
+            I.Load((f"in1__ar{i}",), "k", bh + (V("a1"), V("a2")), dt),
+            assign(f"v3__ar{i}", "multiply", f"in1__ar{i}", f"in2__ar{i}"),
+            accum(f"acc0__ar{i}", f"v3__ar{i}", axes=("a2",))), False, True))
+    for j in range(nu):
+        key_body.append(I.Load((f"in7__bc{j}",), "v", bh + (V("a1"), col(j)), dt))
+    for i in range(mu):
+        for j in range(nu):
+            c = f"__c{i}_{j}"
+            key_body += [
+                assign(f"v4{c}", "multiply", f"acc0__ar{i}", "v1"),
+                I.Let(f"one{c}", Lit(1.0), F32),
+                assign(f"v4__gn{c}", "maximum", f"acc1{c}", f"v4{c}"),
+                assign(f"v4__dg{c}", "subtract", f"acc1{c}", f"v4__gn{c}"),
+                assign(f"v4__alpha{c}", "exp", f"v4__dg{c}"),
+                assign(f"v4__dg_o{c}", "subtract", f"v4{c}", f"v4__gn{c}"),
+                assign(f"v4__beta{c}", "exp", f"v4__dg_o{c}"),
+                assign(f"v4__acc3_sa{c}", "multiply", f"acc3{c}", f"v4__alpha{c}"),
+                assign(f"v4__acc3_sb{c}", "multiply", f"one{c}", f"v4__beta{c}"),
+                accum(f"acc3{c}", f"v4__acc3_sb{c}", base=f"v4__acc3_sa{c}", axes=("a1",)),
+                assign(f"v4__acc5__sum_sa{c}", "multiply", f"acc5__sum{c}", f"v4__alpha{c}"),
+                assign(f"v4__acc5__sum_sb{c}", "multiply", f"in7__bc{j}", f"v4__beta{c}"),
+                accum(f"acc5__sum{c}", f"v4__acc5__sum_sb{c}", base=f"v4__acc5__sum_sa{c}",
+                      axes=("a1",)),
+                accum(f"acc1{c}", f"v4{c}", op="maximum", axes=("a1",))]
+    body = [load("in0", "div_c1", Lit(0)), assign("v1", "reciprocal", "in0"),
+            I.Loop(axis("a1", S), tuple(key_body), False, True)]
+    for i in range(mu):
+        for j in range(nu):
+            c = f"__c{i}_{j}"
+            body += [assign(f"v9{c}", "reciprocal", f"acc3{c}"),
+                     assign(f"acc5{c}", "multiply", f"acc5__sum{c}", f"v9{c}")]
+    for i in range(mu):
+        body.append(write("matmul_1", bh + (row(i), col(0)),
+                          tuple(f"acc5__c{i}_{j}" for j in range(nu))))
+    p.body = tile([axis("ab", B), axis("ah", H), axis("a0_b", S // BM, parent=("a0", S)),
+                   axis("a5_b", 1, parent=("a5", D)), axis("a0_u", U0), axis("a5_u", U1)], body)
+    p.grid, p.block = (B * H * (S // BM), 1, 1), (U0 * U1, 1, 1)
+    # the template's shared memory: Q tile + a 2-stage ring of K/V tiles (+ slack)
+    p.smem = BM * D * 2 + 2 * (2 * BM * D * 2) + 2048
+    p.rtol, p.atol = 2e-2, None
+    p.oracle = {"family": "attention", "args": {"q": "q", "k": "k", "v": "v"},
+                "output": "matmul_1", "scale": 1.0 / math.sqrt(D),
+                "flops": 4 * B * H * S * S * D,
+                "bf16": {n: dtype == "bf16" for n in ("q", "k", "v")}}
+    return p
+
+
 # the BASELINE.json configurations by name (full sizes)
 def config(name: str, **kw) -> Problem:
     table = {
@@ -479,6 +558,8 @@ def config(name: str, **kw) -> Problem:
         "l2norm": l2norm,
         "matmul_bf16": lambda **k: matmul(dtype="bf16", **k),
         "matmul_f32": lambda **k: matmul(**{"dtype": "f32", "BK": 32, "stages": 4, **k}),
+        "attention": attention,
+        "attention_d64": lambda **k: attention(**{"D": 64, **k}),
     }
     return table[name](**kw)
 
