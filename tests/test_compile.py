@@ -96,3 +96,17 @@ def test_in_process_api():
     c = mod.Compiler(g, json.loads((folder / "meta.json").read_text()), mod.find_kernel(g))
     c.compile()
     assert c.render() == mod.compile_ir(folder / "kernel.ir.json")
+
+
+def test_generic_lowering_assembles_all_goldens(native_lib, monkeypatch):
+    """Every golden IR (15 problems, 8 bug fixtures) also compiles through the
+    statement-by-statement lowering and assembles for sm_100a."""
+    from conftest import FIXTURES, PROBLEMS
+    from emmy_b200 import native
+    monkeypatch.setenv("EMMY_TEMPLATE", "generic")
+    for folder in PROBLEMS + FIXTURES:
+        g = json.loads((folder / "kernel.ir.json").read_text())
+        m = json.loads((folder / "meta.json").read_text())
+        c = compile_graph(g, m)
+        assert c.kind == "generic"
+        native.Image(c.render())
