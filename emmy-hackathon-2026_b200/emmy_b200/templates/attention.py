@@ -11,17 +11,24 @@ micro-tile to scalar FFMAs that recompute the scores per output column
 (``compile.py:1882-1928``).  This template keeps the IR's CTA -> (batch,
 head, 128 query rows) assignment and computes the tile as:
 
-* TMA loads the CTA's Q tile once and a 2-stage ring of K/V tiles of 128 keys
-  (128-byte swizzle; no multicast);
+* TMA loads the CTA's Q tile once and K and V tiles of 128 keys into two
+  separate rings (3 + 2 stages at D=128, 4 + 4 at D=64; 128-byte swizzle;
+  no multicast), each fed by its own producer thread, so a K tile is reused
+  as soon as its Q.K^T has run and the loads stay ahead of the MMAs;
 * one thread issues ``S_j = Q K_j^T`` (``tcgen05.mma kind::f16``, M=N=128)
   into one of two TMEM score buffers, and ``O += P_{j-1} V_{j-1}`` with P read
   from TMEM (the ``[a-tmem]`` form) and V as an MN-major shared operand, so
   the scores of block j+1 overlap the softmax of block j;
-* four softmax warps own one query row per thread (= its TMEM lane): row max,
-  ``p = 2^(s*c - m)`` (c = s*log2 e), row sum, the ``2^(m_old - m_new)``
-  rescale of the running O row in TMEM, and P written back over S as packed
-  bf16 pairs;
-* after the last block each thread scales its O row by 1/l and stores it.
+* eight softmax warps, two threads per query row (the row is the thread's
+  TMEM lane; each thread owns half of the 128 score columns and half of the
+  D output columns): half-row maxima exchanged through shared memory under a
+  64-arrival mbarrier, ``p = 2^(s*c - m)`` (c = s*log2 e), P written back
+  over S as packed bf16 pairs, partial row sums; the exponent base m moves
+  only when the row max grows by more than 2^8, and only then is the running
+  O row rescaled in TMEM by ``2^(m_old - m_new)`` (the same base is used for
+  the final 1/l, so this is exact);
+* after the last block the two half sums are added and each thread scales
+  its half of the O row by 1/l and stores it.
 
 The arithmetic is the IR's: the same online-softmax recurrence (max, the
 exp rescale factor of the previous state, sum, weighted sum), evaluated per
@@ -117,15 +124,18 @@ class AttentionTemplate:
         if BM != 128 or ext["a0_b"] * 128 != S or ext["a5_b"] != 1 or D not in (64, 128) or \
                 S % 128 or ext["ab"] != B or ext["ah"] != H:
             raise TemplateMismatch("tile geometry")
-        if ctx.block != (256, 1, 1) or ctx.grid[0] * ctx.grid[1] * ctx.grid[2] != B * H * S // 128:
+        if ctx.block != (512, 1, 1) or ctx.grid[0] * ctx.grid[1] * ctx.grid[2] != B * H * S // 128:
             raise TemplateMismatch("launch geometry")
         self = cls()
         self.ctx, self.q, self.k, self.v, self.out, self.scale_buf = ctx, q, k_, v, out, scale_buf
         self.B, self.H, self.S, self.D = B, H, S, D
-        self.tile_bytes = 128 * D * 2
-        need = 1024 + self.tile_bytes * 5 + 256
-        if min(ctx.smem_bytes, 227 * 1024) < need:
-            raise TemplateMismatch("meta smem_bytes too small")
+        self.tile_bytes = TB = 128 * D * 2
+        # Q tile + K ring + V ring, sized from the launch's shared memory
+        avail = min(ctx.smem_bytes, 227 * 1024) - 1024 - 512 - 3072 - TB
+        n = min(8, avail // TB)
+        if n < 4:
+            raise TemplateMismatch("meta smem_bytes too small for 2+2 K/V stages")
+        self.SK, self.SV = (n + 1) // 2, n // 2
         return self
 
     # ------------------------------------------------------------------- emit
@@ -140,8 +150,7 @@ class AttentionTemplate:
                                  ("tmapK", ".align 64 .b8", "[128]"),
                                  ("tmapV", ".align 64 .b8", "[128]")]
         k = Kernel(ctx.entry, params)
-        k.maxntid = (256, 1, 1)
-        k.maxnreg = 168           # one CTA per SM (TMEM, shared memory): room for the rows
+        k.maxntid = (512, 1, 1)
         k.decl(".extern .shared .align 1024 .b8 __emmy_smem[];")
         k.decl(".global .align 4 .u32 __emmy_status;")
         rows = self.B * self.H * S
@@ -169,28 +178,44 @@ class AttentionTemplate:
         k(f"mul.lo.u32 {krow0}, {bh}, {S};")
         qrow0 = k.reg("r")
         k(f"mad.lo.u32 {qrow0}, {qb}, 128, {krow0};")
-        # shared memory: Q | K0 V0 | K1 V1 | barriers | tmem slot
+        SK, SV = self.SK, self.SV
+        # shared memory: Q | K ring (SK tiles) | V ring (SV tiles) | barriers |
+        # tmem slot | row exchange
         raw = k.reg("r")
         k(f"mov.u32 {raw}, __emmy_smem;")
         qs = k.reg("r")
         k(f"add.u32 {qs}, {raw}, 1023;")
         k(f"and.b32 {qs}, {qs}, -1024;")
-        ring = k.reg("r")
-        k(f"add.u32 {ring}, {qs}, {TB};")
+        kring = k.reg("r")
+        k(f"add.u32 {kring}, {qs}, {TB};")
+        vring = k.reg("r")
+        k(f"add.u32 {vring}, {kring}, {SK * TB};")
         bars = k.reg("r")
-        k(f"add.u32 {bars}, {ring}, {4 * TB};")
+        k(f"add.u32 {bars}, {vring}, {SV * TB};")
         # barrier slots
-        Q_FULL, K_FULL, V_FULL, KV_EMPTY, S_FULL, P_READY, O_DONE, FINAL = 0, 1, 3, 5, 7, 9, 11, 12
+        Q_FULL = 0
+        K_FULL, K_EMPTY = 1, 1 + SK
+        V_FULL, V_EMPTY = 1 + 2 * SK, 1 + 2 * SK + SV
+        S_FULL = 1 + 2 * SK + 2 * SV
+        P_READY = S_FULL + 2
+        O_DONE = P_READY + 2
+        FINAL = O_DONE + 1
+        XBAR = FINAL + 1          # xbar[q]: the two warps of row quarter q (64 arrivals)
+        NSLOT = XBAR + 4
         tslot = k.reg("r")
-        k(f"add.u32 {tslot}, {bars}, {13 * 8};")
+        k(f"add.u32 {tslot}, {bars}, {NSLOT * 8};")
+        # row-max / row-sum exchange between the two threads of a row:
+        # xch[parity][half][row] f32 at bars + 512, the final sums at +2048
+        xch = k.reg("r")
+        k(f"add.u32 {xch}, {bars}, 512;")
         status = k.reg("rd")
         k(f"mov.u64 {status}, __emmy_status;")
         p0 = k.reg("p")
         k(f"setp.eq.u32 {p0}, {tid}, 0;")
         skip = k.label("SKIP_INIT")
         k(f"@!{p0} bra {skip};")
-        for slot in range(13):
-            cnt = 128 if slot in (P_READY, P_READY + 1) else 1
+        for slot in range(NSLOT):
+            cnt = 256 if slot in (P_READY, P_READY + 1) else 64 if slot >= XBAR else 1
             k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * slot}], {cnt};")
         k("fence.mbarrier_init.release.cluster;")
         for r in (tq, tk, tv):
@@ -232,43 +257,52 @@ class AttentionTemplate:
             k(f"shr.u32 {ph}, {jreg}, 1;")
             k(f"and.b32 {ph}, {ph}, 1;")
 
-        # ---------------- producer: warp 0 lane 0 ----------------
-        pp = k.reg("p")
-        k(f"setp.eq.u32 {pp}, {warp}, 0;")
-        k(f"and.pred {pp}, {pp}, {pl0};")
-        end_prod = k.label("END_PROD")
-        k(f"@!{pp} bra {end_prod};")
-        qf = bar(Q_FULL)
-        k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qf}], {TB};")
-        for i in range(NBX):
-            k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-              f"[{qs}+{i * 16384}], [{tq}, {{{64 * i}, {qrow0}}}], [{qf}];")
-        k(f"mov.u32 {j}, 0;")
-        top = k.label("PROD")
-        k.mark(top)
-        split(j)
-        par = k.reg("r")
-        k(f"xor.b32 {par}, {ph}, 1;")
-        wait(k, bar(KV_EMPTY, b), par, status, 1, end_prod)
-        kr = k.reg("r")
-        k(f"mad.lo.u32 {kr}, {j}, 128, {krow0};")
-        st0 = k.reg("r")
-        k(f"mad.lo.u32 {st0}, {b}, {2 * TB}, {ring};")
-        kfb = bar(K_FULL, b)
-        k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{kfb}], {TB};")
-        for i in range(NBX):
-            k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-              f"[{st0}+{i * 16384}], [{tk}, {{{64 * i}, {kr}}}], [{kfb}];")
-        vfb = bar(V_FULL, b)
-        k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{vfb}], {TB};")
-        for i in range(NBX):
-            k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-              f"[{st0}+{TB + i * 16384}], [{tv}, {{{64 * i}, {kr}}}], [{vfb}];")
-        k(f"add.u32 {j}, {j}, 1;")
-        pl = k.reg("p")
-        k(f"setp.lt.u32 {pl}, {j}, {NB};")
-        k(f"@{pl} bra {top};")
-        k.mark(end_prod)
+        def ring_slot(jreg, depth):
+            """(stage, phase) of block j in a ring of ``depth`` stages."""
+            st_ = k.reg("r")
+            k(f"rem.u32 {st_}, {jreg}, {depth};")
+            ph_ = k.reg("r")
+            k(f"div.u32 {ph_}, {jreg}, {depth};")
+            k(f"and.b32 {ph_}, {ph_}, 1;")
+            return st_, ph_
+
+        def producer(which, warp_id, tmap, ring, depth, full, empty, load_q):
+            pp = k.reg("p")
+            k(f"setp.eq.u32 {pp}, {warp}, {warp_id};")
+            k(f"and.pred {pp}, {pp}, {pl0};")
+            end_p = k.label(f"END_{which}")
+            k(f"@!{pp} bra {end_p};")
+            if load_q:
+                qf = bar(Q_FULL)
+                k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qf}], {TB};")
+                for i in range(NBX):
+                    k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+                      f"[{qs}+{i * 16384}], [{tq}, {{{64 * i}, {qrow0}}}], [{qf}];")
+            k(f"mov.u32 {j}, 0;")
+            top = k.label(f"PROD_{which}")
+            k.mark(top)
+            st_, ph_ = ring_slot(j, depth)
+            par = k.reg("r")
+            k(f"xor.b32 {par}, {ph_}, 1;")
+            wait(k, bar(empty, st_), par, status, 1, end_p)
+            kr = k.reg("r")
+            k(f"mad.lo.u32 {kr}, {j}, 128, {krow0};")
+            dst = k.reg("r")
+            k(f"mad.lo.u32 {dst}, {st_}, {TB}, {ring};")
+            fb = bar(full, st_)
+            k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {TB};")
+            for i in range(NBX):
+                k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+                  f"[{dst}+{i * 16384}], [{tmap}, {{{64 * i}, {kr}}}], [{fb}];")
+            k(f"add.u32 {j}, {j}, 1;")
+            pl = k.reg("p")
+            k(f"setp.lt.u32 {pl}, {j}, {NB};")
+            k(f"@{pl} bra {top};")
+            k.mark(end_p)
+
+        # ---------------- producers: K (and Q) on warp 0, V on warp 2 ----------------
+        producer("K", 0, tk, kring, SK, K_FULL, K_EMPTY, True)
+        producer("V", 2, tv, vring, SV, V_FULL, V_EMPTY, False)
 
         # ---------------- MMA issuer: warp 1 lane 0 ----------------
         pm = k.reg("p")
@@ -292,16 +326,18 @@ class AttentionTemplate:
         k(f"add.u32 {o_tm}, {tmem}, 256;")
 
         def issue_qk(jreg):
-            split(jreg)
-            wait(k, bar(K_FULL, b), ph, status, 2, end_mma)
+            kst, kph = ring_slot(jreg, SK)
+            wait(k, bar(K_FULL, kst), kph, status, 2, end_mma)
             k("tcgen05.fence::after_thread_sync;")
-            kst = k.reg("r")
-            k(f"mad.lo.u32 {kst}, {b}, {2 * TB}, {ring};")
-            dk = GemmTemplate._desc(k, kst, hiK)
+            kad = k.reg("r")
+            k(f"mad.lo.u32 {kad}, {kst}, {TB}, {kring};")
+            dk = GemmTemplate._desc(k, kad, hiK)
+            sb = k.reg("r")
+            k(f"and.b32 {sb}, {jreg}, 1;")
             s_tm = k.reg("r")
-            k(f"mad.lo.u32 {s_tm}, {b}, 128, {tmem};")
+            k(f"mad.lo.u32 {s_tm}, {sb}, 128, {tmem};")
             pfirst = k.reg("p")
-            k("setp.ne.u32 {}, 0, 0;".format(pfirst))      # first MMA overwrites S
+            k(f"setp.ne.u32 {pfirst}, 0, 0;")       # the first MMA overwrites S
             for kk in range(D // 16):
                 off = (kk % 4) * 2 + (kk // 4) * 1024
                 a = k.reg("rd")
@@ -311,17 +347,19 @@ class AttentionTemplate:
                 k(f"tcgen05.mma.cta_group::1.kind::f16 [{s_tm}], {a}, {bd}, {iqk}, "
                   f"{pfirst if kk == 0 else ptrue};")
             k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-              f"[{bar(S_FULL, b)}];")
+              f"[{bar(S_FULL, sb)}];")
+            k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+              f"[{bar(K_EMPTY, kst)}];")
 
         def issue_pv(ireg, first_pred):
             split(ireg)
             wait(k, bar(P_READY, b), ph, status, 2, end_mma)
             k("tcgen05.fence::after_thread_sync;")
-            wait(k, bar(V_FULL, b), ph, status, 2, end_mma)
-            vst = k.reg("r")
-            k(f"mad.lo.u32 {vst}, {b}, {2 * TB}, {ring};")
-            k(f"add.u32 {vst}, {vst}, {TB};")
-            dv = GemmTemplate._desc(k, vst, hiV)
+            vst, vph = ring_slot(ireg, SV)
+            wait(k, bar(V_FULL, vst), vph, status, 2, end_mma)
+            vad = k.reg("r")
+            k(f"mad.lo.u32 {vad}, {vst}, {TB}, {vring};")
+            dv = GemmTemplate._desc(k, vad, hiV)
             p_tm = k.reg("r")
             k(f"mad.lo.u32 {p_tm}, {b}, 128, {tmem};")
             for kk in range(8):                     # 128 keys, K=16 per MMA
@@ -334,7 +372,7 @@ class AttentionTemplate:
             k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
               f"[{bar(O_DONE)}];")
             k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-              f"[{bar(KV_EMPTY, b)}];")
+              f"[{bar(V_EMPTY, vst)}];")
 
         k(f"mov.u32 {j}, 0;")
         issue_qk(j)
@@ -359,21 +397,50 @@ class AttentionTemplate:
           f"[{bar(FINAL)}];")
         k.mark(end_mma)
 
-        # ---------------- softmax warps 4-7: one query row per thread ----------------
+        # ------------- softmax warps 4-11: two threads per query row -------------
+        # warp w: rows 32*(w%4) + lane (its TMEM lanes), half h = (w-4)/4 of the
+        # 128 score columns and of the D output columns
         psm = k.reg("p")
         k(f"setp.ge.u32 {psm}, {warp}, 4;")
+        psm2 = k.reg("p")
+        k(f"setp.lt.u32 {psm2}, {warp}, 12;")
+        k(f"and.pred {psm}, {psm}, {psm2};")
         end_sm = k.label("END_SM")
         k(f"@!{psm} bra {end_sm};")
         q4 = k.reg("r")
         k(f"and.b32 {q4}, {warp}, 3;")
+        hh = k.reg("r")
+        k(f"sub.u32 {hh}, {warp}, 4;")
+        k(f"shr.u32 {hh}, {hh}, 2;")
+        row = k.reg("r")
+        k(f"mad.lo.u32 {row}, {q4}, 32, {lane};")
         trow = k.reg("r")
         k(f"shl.b32 {trow}, {q4}, 21;")            # TMEM lane field (32*q4) << 16
         k(f"add.u32 {trow}, {trow}, {tmem};")
+        scol = k.reg("r")
+        k(f"shl.b32 {scol}, {hh}, 6;")             # 64*h score columns
+        pcol = k.reg("r")
+        k(f"shl.b32 {pcol}, {hh}, 5;")             # 32*h packed P columns
+        ocol = k.reg("r")
+        k(f"mul.lo.u32 {ocol}, {hh}, {D // 2};")
+        k(f"add.u32 {ocol}, {ocol}, 256;")
+        otm = k.reg("r")
+        k(f"add.u32 {otm}, {trow}, {ocol};")
+        xb = k.reg("r")                            # exchange mbarrier of this row pair
+        k(f"mad.lo.u32 {xb}, {q4}, 8, {bars};")
+        k(f"add.u32 {xb}, {xb}, {8 * XBAR};")
+        mine = k.reg("r")                          # &xch[0][h][row]
+        k(f"mad.lo.u32 {mine}, {hh}, 512, {xch};")
+        k(f"mad.lo.u32 {mine}, {row}, 4, {mine};")
+        other = k.reg("r")                         # &xch[0][1-h][row]
+        k(f"xor.b32 {other}, {hh}, 1;")
+        k(f"mad.lo.u32 {other}, {other}, 512, {xch};")
+        k(f"mad.lo.u32 {other}, {row}, 4, {other};")
         sc = k.reg("f")
         k(f"ld.global.nc.f32 {sc}, [{sbuf}];")
         k(f"rcp.rn.f32 {sc}, {sc};")
         k(f"mul.rn.f32 {sc}, {sc}, 0f{_f32hex(LOG2E)};")     # c = s * log2(e)
-        m = k.reg("f")
+        m = k.reg("f")                             # max used for the exponents
         k(f"mov.f32 {m}, 0fFF800000;")
         lsum = k.reg("f")
         k(f"mov.f32 {lsum}, 0f00000000;")
@@ -385,96 +452,132 @@ class AttentionTemplate:
         k("tcgen05.fence::after_thread_sync;")
         srow = k.reg("r")
         k(f"mad.lo.u32 {srow}, {b}, 128, {trow};")
-        # pass A: row max of the raw scores
-        mx = [k.reg("f") for _ in range(4)]
-        for r in mx:
-            k(f"mov.f32 {r}, 0fFF800000;")
-        for c4 in range(4):
-            regs = k.regs("r", 32)
-            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{srow}+{32 * c4}];")
-            k("tcgen05.wait::ld.sync.aligned;")
-            for i, r in enumerate(regs):
-                k(f"max.f32 {mx[i % 4]}, {mx[i % 4]}, {r};")
-        k(f"max.f32 {mx[0]}, {mx[0]}, {mx[1]};")
-        k(f"max.f32 {mx[2]}, {mx[2]}, {mx[3]};")
-        k(f"max.f32 {mx[0]}, {mx[0]}, {mx[2]};")
-        mnew = k.reg("f")
-        k(f"mul.rn.f32 {mnew}, {mx[0]}, {sc};")
-        k(f"max.f32 {mnew}, {mnew}, {m};")
+        sa = k.reg("r")
+        k(f"add.u32 {sa}, {srow}, {scol};")
+        sv = k.regs("r", 64)
+        for c2 in range(2):
+            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv[32 * c2:32 * c2 + 32])}}}, "
+              f"[{sa}+{32 * c2}];")
+        k("tcgen05.wait::ld.sync.aligned;")
+        mx = [k.reg("f") for _ in range(8)]
+        for i in range(8):
+            k(f"max.f32 {mx[i]}, {sv[i]}, {sv[i + 8]};")
+        for i in range(16, 64):
+            k(f"max.f32 {mx[i % 8]}, {mx[i % 8]}, {sv[i]};")
+        for w in (4, 2, 1):
+            for i in range(w):
+                k(f"max.f32 {mx[i]}, {mx[i]}, {mx[i + w]};")
+        # exchange the half-row maxima (buffer by iteration parity)
+        par2 = k.reg("r")
+        k(f"and.b32 {par2}, {j}, 1;")
+        po = k.reg("r")
+        k(f"shl.b32 {po}, {par2}, 10;")
+        wa = k.reg("r")
+        k(f"add.u32 {wa}, {mine}, {po};")
+        k(f"st.shared.f32 [{wa}], {mx[0]};")
+        k(f"mbarrier.arrive.shared::cta.b64 _, [{xb}];")
+        wait(k, xb, par2, status, 5, teardown)
+        ra = k.reg("r")
+        k(f"add.u32 {ra}, {other}, {po};")
+        om = k.reg("f")
+        k(f"ld.shared.f32 {om}, [{ra}];")
+        k(f"max.f32 {mx[0]}, {mx[0]}, {om};")
+        # lazy rescaling: move the exponent base only when the row max grew by
+        # more than 2^8 (p stays <= 256); the final 1/l uses the same base
+        cand = k.reg("f")
+        k(f"mul.rn.f32 {cand}, {mx[0]}, {sc};")
+        thr = k.reg("f")
+        k(f"add.rn.f32 {thr}, {m}, 0f41000000;")         # m + 8
+        need = k.reg("p")
+        k(f"setp.gt.f32 {need}, {cand}, {thr};")
+        meff = k.reg("f")
+        k(f"selp.f32 {meff}, {cand}, {m}, {need};")
         alpha = k.reg("f")
         dlt = k.reg("f")
-        k(f"sub.rn.f32 {dlt}, {m}, {mnew};")
+        k(f"sub.rn.f32 {dlt}, {m}, {meff};")
         k(f"ex2.approx.ftz.f32 {alpha}, {dlt};")
+        k(f"@!{need} mov.f32 {alpha}, 0f3F800000;")
         negm = k.reg("f")
-        k(f"neg.f32 {negm}, {mnew};")
-        # pass B: p = 2^(s*c - m), row sum, P as bf16 pairs over the scores
-        ps = [k.reg("f") for _ in range(4)]
-        for r in ps:
-            k(f"mov.f32 {r}, 0f00000000;")
-        for c4 in range(4):
-            regs = k.regs("r", 32)
-            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{srow}+{32 * c4}];")
-            k("tcgen05.wait::ld.sync.aligned;")
-            pv = []
-            for i, r in enumerate(regs):
+        k(f"neg.f32 {negm}, {meff};")
+        ps = [k.reg("f") for _ in range(8)]
+        packed = k.regs("r", 32)
+        for i in range(0, 64, 2):
+            e2 = []
+            for ii in (i, i + 1):
                 t = k.reg("f")
-                k(f"fma.rn.f32 {t}, {r}, {sc}, {negm};")
+                k(f"fma.rn.f32 {t}, {sv[ii]}, {sc}, {negm};")
                 e = k.reg("f")
                 k(f"ex2.approx.ftz.f32 {e}, {t};")
-                k(f"add.rn.f32 {ps[i % 4]}, {ps[i % 4]}, {e};")
-                pv.append(e)
-            packed = k.regs("r", 16)
-            for i in range(16):
-                k(f"cvt.rn.bf16x2.f32 {packed[i]}, {pv[2 * i + 1]}, {pv[2 * i]};")
-            k(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{srow}+{16 * c4}], "
-              f"{{{', '.join(packed)}}};")
-        k(f"add.rn.f32 {ps[0]}, {ps[0]}, {ps[1]};")
-        k(f"add.rn.f32 {ps[2]}, {ps[2]}, {ps[3]};")
-        k(f"add.rn.f32 {ps[0]}, {ps[0]}, {ps[2]};")
+                if ii < 8:
+                    k(f"mov.f32 {ps[ii]}, {e};")
+                else:
+                    k(f"add.rn.f32 {ps[ii % 8]}, {ps[ii % 8]}, {e};")
+                e2.append(e)
+            k(f"cvt.rn.bf16x2.f32 {packed[i // 2]}, {e2[1]}, {e2[0]};")
+        pa = k.reg("r")
+        k(f"add.u32 {pa}, {srow}, {pcol};")
+        k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{pa}], {{{', '.join(packed)}}};")
+        for w in (4, 2, 1):
+            for i in range(w):
+                k(f"add.rn.f32 {ps[i]}, {ps[i]}, {ps[i + w]};")
         k(f"fma.rn.f32 {lsum}, {lsum}, {alpha}, {ps[0]};")
-        # rescale the running O row once the previous P.V has landed
+        # rescale this warp's half of the running O rows if any of its rows
+        # moved (warp-uniform), after the previous P.V has landed
         skip_rs = k.label("NO_RESCALE")
         pj0 = k.reg("p")
         k(f"setp.eq.u32 {pj0}, {j}, 0;")
         k(f"@{pj0} bra {skip_rs};")
+        anyw = k.reg("p")
+        k(f"vote.sync.any.pred {anyw}, {need}, 0xffffffff;")
+        k(f"@!{anyw} bra {skip_rs};")
         jp = k.reg("r")
         k(f"sub.u32 {jp}, {j}, 1;")
         k(f"and.b32 {jp}, {jp}, 1;")
         wait(k, bar(O_DONE), jp, status, 3, teardown)
         k("tcgen05.fence::after_thread_sync;")
-        for c in range(D // 32):
-            regs = k.regs("r", 32)
-            addr = f"{trow}+{256 + 32 * c}"
-            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{addr}];")
-            k("tcgen05.wait::ld.sync.aligned;")
-            for r in regs:
-                k(f"mul.rn.f32 {r}, {r}, {alpha};")
-            k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{addr}], {{{', '.join(regs)}}};")
+        half = D // 2
+        ov = k.regs("r", half)
+        for c in range(half // 32):
+            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov[32 * c:32 * c + 32])}}}, "
+              f"[{otm}+{32 * c}];")
+        k("tcgen05.wait::ld.sync.aligned;")
+        for r in ov:
+            k(f"mul.rn.f32 {r}, {r}, {alpha};")
+        for c in range(half // 32):
+            k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{otm}+{32 * c}], "
+              f"{{{', '.join(ov[32 * c:32 * c + 32])}}};")
         k.mark(skip_rs)
         k("tcgen05.wait::st.sync.aligned;")
         k("tcgen05.fence::before_thread_sync;")
         k(f"mbarrier.arrive.shared::cta.b64 _, [{bar(P_READY, b)}];")
-        k(f"mov.f32 {m}, {mnew};")
+        k(f"mov.f32 {m}, {meff};")
         k(f"add.u32 {j}, {j}, 1;")
         pl3 = k.reg("p")
         k(f"setp.lt.u32 {pl3}, {j}, {NB};")
         k(f"@{pl3} bra {top3};")
-        # epilogue: O row * (1 / l) -> global
+        # epilogue: row sum of both halves, O half-row * (1 / l) -> global
+        k(f"st.shared.f32 [{mine}+2048], {lsum};")
+        k(f"mbarrier.arrive.shared::cta.b64 _, [{xb}];")
+        k(f"mov.u32 {par2}, {NB & 1};")
+        wait(k, xb, par2, status, 5, teardown)
+        ol = k.reg("f")
+        k(f"ld.shared.f32 {ol}, [{other}+2048];")
+        k(f"add.rn.f32 {lsum}, {lsum}, {ol};")
         wait(k, bar(FINAL), self._zero(k), status, 3, teardown)
         k("tcgen05.fence::after_thread_sync;")
         inv = k.reg("f")
         k(f"rcp.rn.f32 {inv}, {lsum};")
-        ct = k.reg("r")
-        k(f"sub.u32 {ct}, {tid}, 128;")
         orow = k.reg("r")
-        k(f"add.u32 {orow}, {qrow0}, {ct};")
+        k(f"add.u32 {orow}, {qrow0}, {row};")
         oa = k.reg("rd")
         k(f"mul.wide.u32 {oa}, {orow}, {D * 4};")
         k(f"add.s64 {oa}, {oa}, {obase};")
-        for c in range(D // 32):
+        hoff = k.reg("rd")
+        k(f"mul.wide.u32 {hoff}, {hh}, {half * 4};")
+        k(f"add.s64 {oa}, {oa}, {hoff};")
+        for c in range(half // 32):
             regs = k.regs("r", 32)
-            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, "
-              f"[{trow}+{256 + 32 * c}];")
+            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{otm}+{32 * c}];")
             k("tcgen05.wait::ld.sync.aligned;")
             for r in regs:
                 k(f"mul.rn.f32 {r}, {r}, {inv};")

@@ -34,7 +34,7 @@ def _run(p, heads=None):
     rtol, atol = expr.tolerance(m, ref)
     err = float(np.max(np.abs(got - ref)))
     assert np.allclose(got, ref, rtol=rtol, atol=atol), err
-    assert err <= 2e-3 * float(np.max(np.abs(ref))), err
+    assert err <= 4e-3 * float(np.max(np.abs(ref))), err
 
 
 CASES = [dict(B=1, H=1, S=128, D=128), dict(B=1, H=2, S=256, D=128), dict(B=2, H=2, S=512, D=64),
