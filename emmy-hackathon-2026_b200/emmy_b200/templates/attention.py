@@ -348,12 +348,14 @@ class AttentionTemplate:
                   f"{pfirst if kk == 0 else ptrue};")
             k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
               f"[{bar(S_FULL, sb)}];")
+            k.comment(f"@trace 0 {jreg}")
             k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
               f"[{bar(K_EMPTY, kst)}];")
 
         def issue_pv(ireg, first_pred):
             split(ireg)
             wait(k, bar(P_READY, b), ph, status, 2, end_mma)
+            k.comment(f"@trace 1 {ireg}")
             k("tcgen05.fence::after_thread_sync;")
             vst, vph = ring_slot(ireg, SV)
             wait(k, bar(V_FULL, vst), vph, status, 2, end_mma)
@@ -369,6 +371,7 @@ class AttentionTemplate:
                 k(f"add.s64 {bd}, {dv}, {kk * 128};")  # +16 key rows * 128 B
                 k(f"tcgen05.mma.cta_group::1.kind::f16 [{o_tm}], [{a}], {bd}, {ipv}, "
                   f"{first_pred if kk == 0 else ptrue};")
+            k.comment(f"@trace 2 {ireg}")
             k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
               f"[{bar(O_DONE)}];")
             k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
@@ -449,6 +452,7 @@ class AttentionTemplate:
         k.mark(top3)
         split(j)
         wait(k, bar(S_FULL, b), ph, status, 3, teardown)
+        k.comment(f"@trace 3 {j}")
         k("tcgen05.fence::after_thread_sync;")
         srow = k.reg("r")
         k(f"mad.lo.u32 {srow}, {b}, 128, {trow};")
@@ -517,6 +521,7 @@ class AttentionTemplate:
         pa = k.reg("r")
         k(f"add.u32 {pa}, {srow}, {pcol};")
         k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{pa}], {{{', '.join(packed)}}};")
+        k.comment(f"@trace 4 {j}")
         for w in (4, 2, 1):
             for i in range(w):
                 k(f"add.rn.f32 {ps[i]}, {ps[i]}, {ps[i + w]};")
@@ -550,6 +555,7 @@ class AttentionTemplate:
         k("tcgen05.wait::st.sync.aligned;")
         k("tcgen05.fence::before_thread_sync;")
         k(f"mbarrier.arrive.shared::cta.b64 _, [{bar(P_READY, b)}];")
+        k.comment(f"@trace 5 {j}")
         k(f"mov.f32 {m}, {meff};")
         k(f"add.u32 {j}, {j}, 1;")
         pl3 = k.reg("p")
