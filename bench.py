@@ -362,6 +362,23 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                "kind": "port",
                "sample": "full workload once per run (median of 3), numpy float32 reductions "
                          "as the reference's refs.py, single thread"}
+    categories = None
+    if world == 1 and not args.no_categories:
+        # every other category's kernel at its BASELINE size (own buffers;
+        # the reductions inputs are released first)
+        del x_sum, x_rows, devt, host, ptrs, params
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        categories = {}
+        for nm in CATEGORY_CASES:
+            try:
+                r = measure_case(nm, {}, 10, 3)
+            except Exception as e:  # report, keep the headline line
+                categories[nm] = {"error": f"{type(e).__name__}: {e}"[:200]}
+                continue
+            categories[nm] = {kk: r[kk] for kk in ("template", "ms_median", "GB/s", "TFLOP/s",
+                                                   "frac", "reference_ptx_ms",
+                                                   "speedup_vs_reference_ptx") if kk in r}
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
@@ -383,57 +400,58 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                     "path": "emmy_run_host (C ABI) from pinned host memory"},
             "gpu_launches": 3 * args.steps,
             "clocks": clk.summary(),
+            "categories": categories,
         }
         print(json.dumps(line), flush=True)
 
 
-def run_case(args) -> None:
-    """One synthesised configuration (``--case``, sizes from ``--size k=v,..``):
-    ``--steps`` launches timed one by one with CUDA events on the launching
-    stream; L2 is flushed between launches when the inputs would fit in it.
-    Prints one JSON line (not the contract line; used for per-category
-    numbers and for small ncu captures)."""
+def measure_case(name: str, kw: dict, steps: int, warmup: int) -> dict:
+    """Time one synthesised configuration: ``steps`` launches through the C ABI,
+    each bracketed by CUDA events on the launching stream; L2 flushed between
+    launches when the inputs would fit in it.  Includes the reference
+    compiler's PTX for the same IR (``oracle/_ref``) when it exists."""
+    import numpy as np
     import torch
 
     from emmy_b200 import harness, native, synth
 
-    torch.cuda.set_device(0)
-    native.check(native.lib().emmy_device_init(0))
-    kw = {}
-    for item in filter(None, (args.size or "").split(",")):
-        key, val = item.split("=")
-        kw[key] = float(val) if "." in val or "e-" in val else int(val)
-    p = synth.config(args.case, **kw)
+    p = synth.config(name, **kw)
     g, m = p.build()
     kern = harness.CompiledKernel(g, m)
     bufs = harness.Buffers.random(kern, seed=0)
     stream = torch.cuda.current_stream().cuda_stream
     in_bytes = sum(t.numel() * t.element_size() for n, t in bufs.t.items()
                    if not bufs.args[n].get("output"))
-    flush = None
+    flush = fb = None
     if in_bytes < 2 * 126 * 2 ** 20:
         fb = torch.empty(512 * 2 ** 20, dtype=torch.uint8, device="cuda")
         flush = (fb.data_ptr(), fb.numel())
-    ms = kern.time(bufs.ptrs(), warmup=args.warmup, iters=args.steps, stream=stream,
+    ms = kern.time(bufs.ptrs(), warmup=warmup, iters=steps, stream=stream,
                    flush=flush, zero=bufs.zero_list())
     med = float(np.median(ms))
     hbm, src = peaks()
     nb = synth.algorithmic_bytes(p)
     flops = synth.algorithmic_flops(p)
-    line = {"case": args.case, "size": kw, "template": kern.kind, "entry": kern.entry,
+    line = {"case": name, "size": kw, "template": kern.kind, "entry": kern.entry,
             "ms_median": round(med, 5), "ms_min": round(float(np.min(ms)), 5),
-            "launches": args.steps, "l2_flush": flush is not None,
+            "launches": steps, "l2_flush": flush is not None,
             "regs": kern.image.registers().get(kern.entry)}
     if flops:
         tf = flops / (med / 1e3) / 1e12
-        peak = float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]) \
-            if (REPO / "MEASURED_PEAKS.json").exists() else 1590.0
-        line.update({"TFLOP/s": round(tf, 1), "bf16_peak": peak, "frac": round(tf / peak, 3)})
+        mp = REPO / "MEASURED_PEAKS.json"
+        peak = float(json.loads(mp.read_text())["bf16_tflops"]) if mp.exists() else 1590.0
+        basis = "measured bf16 peak"
+        if kern.kind == "gemm" and getattr(kern.compiler.template, "mode", "") == "tf32x3":
+            # fp32 through 3xTF32: tf32 runs at half the bf16 rate and every
+            # product costs three tf32 MMAs
+            peak, basis = peak / 2 / 3, "3xTF32 effective = measured bf16 peak / 2 / 3"
+        line.update({"TFLOP/s": round(tf, 1), "peak": round(peak, 1), "peak_basis": basis,
+                     "frac": round(tf / peak, 3), "flops": flops})
     else:
         gbs = nb / (med / 1e3) / 1e9
         line.update({"GB/s": round(gbs, 1), "peak": hbm, "peak_source": src,
                      "frac": round(gbs / hbm, 3), "algorithmic_bytes": nb})
-    f = REPO / "oracle" / "_ref" / f"{args.case}.ptx"
+    f = REPO / "oracle" / "_ref" / f"{name}.ptx"
     if f.exists() and not kw:
         img = native.Image(f.read_text())
         mod = native.Module(img.data)
@@ -441,11 +459,35 @@ def run_case(args) -> None:
         ref = harness.CompiledKernel.__new__(harness.CompiledKernel)
         ref.__dict__.update(kern.__dict__)
         ref._module, ref._kernel = mod, kh
-        rms = ref.time(bufs.ptrs(), warmup=2, iters=min(args.steps, 10), stream=stream,
+        rms = ref.time(bufs.ptrs(), warmup=2, iters=min(steps, 10), stream=stream,
                        flush=flush, zero=bufs.zero_list())
         line["reference_ptx_ms"] = round(float(np.median(rms)), 5)
         line["speedup_vs_reference_ptx"] = round(float(np.median(rms)) / med, 2)
-    print(json.dumps(line), flush=True)
+        mod.unload()
+    del bufs, fb
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return line
+
+
+CATEGORY_CASES = ["vector_add", "rmsnorm", "softmax", "l2norm", "matmul_bf16", "matmul_f32",
+                  "attention", "attention_d64"]
+
+
+def run_case(args) -> None:
+    """``--case`` (sizes from ``--size k=v,..``): one JSON line for one
+    configuration (per-category numbers; small ncu captures)."""
+    import torch
+
+    from emmy_b200 import native
+
+    torch.cuda.set_device(0)
+    native.check(native.lib().emmy_device_init(0))
+    kw = {}
+    for item in filter(None, (args.size or "").split(",")):
+        key, val = item.split("=")
+        kw[key] = float(val) if "." in val or "e-" in val else int(val)
+    print(json.dumps(measure_case(args.case, kw, args.steps, args.warmup)), flush=True)
 
 
 def main():
@@ -456,6 +498,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default=None, help="time one synthesised configuration")
     ap.add_argument("--size", default=None, help="size overrides for --case, k=v,k=v")
+    ap.add_argument("--no-categories", action="store_true",
+                    help="skip the per-category kernels after the headline workload")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -463,8 +507,6 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.case:
-        import numpy as np  # noqa: F401
-        globals()["np"] = np
         run_case(args)
         return
     if args.impl == "reference":
