@@ -30,6 +30,28 @@ from .data import NP, materialize, nbytes
 
 _TMAP_RE = re.compile(r"^// @emmy tmap (\S+) (.*)$", re.M)
 _CLUSTER_RE = re.compile(r"^// @emmy cluster (\d+) (\d+) (\d+)$", re.M)
+_REGSPLIT_RE = re.compile(r"^// @emmy regsplit launch=(\d+) threads=(\d+) warpgroups=([\d,]+)$",
+                          re.M)
+
+
+def check_regsplit(ptx: str, launch_regs: int) -> None:
+    """A kernel that moves registers between warpgroups with setmaxnreg may
+    only run when the launch holds what the split was computed for: the
+    loaded function's register count equal to the declared one, and the
+    warpgroup shares adding up to no more than threads x that count
+    (otherwise setmaxnreg.inc would wait for registers that never come)."""
+    mo = _REGSPLIT_RE.search(ptx)
+    if mo is None:
+        if "setmaxnreg" in ptx:
+            raise RuntimeError("setmaxnreg without a '// @emmy regsplit' declaration")
+        return
+    want, threads = int(mo.group(1)), int(mo.group(2))
+    shares = [int(x) for x in mo.group(3).split(",")]
+    if launch_regs != want:
+        raise RuntimeError(f"register split expects {want} registers per thread at launch, "
+                           f"the loaded function has {launch_regs}")
+    if 128 * sum(shares) > threads * want or len(shares) * 128 != threads:
+        raise RuntimeError(f"register split {shares} exceeds {threads} x {want}")
 
 
 def parse_tmaps(ptx: str) -> list:
@@ -88,7 +110,9 @@ class CompiledKernel:
     def kernel(self) -> native.KernelHandle:
         if self._kernel is None:
             self._module = native.Module(self.image.data)
-            self._kernel = self._module.kernel(self.entry)
+            k = self._module.kernel(self.entry)
+            check_regsplit(self.ptx, k.attrs()["regs"])
+            self._kernel = k
         return self._kernel
 
     def module(self) -> native.Module:

@@ -467,7 +467,7 @@ def matmul(M: int = 16384, N: int = 8192, K: int = 4096, dtype: str = "bf16", BM
     return p
 
 
-def attention(B: int = 8, H: int = 32, S: int = 4096, D: int = 128, BM: int = 128,
+def attention(B: int = 8, H: int = 32, S: int = 4096, D: int = 128, BM: int = 256,
               U0: int = 16, U1: int = 32, dtype: str = "bf16") -> Problem:
     """``O = softmax(Q K^T / sqrt(D)) V`` per (batch, head), non-causal, Q/K/V
     [B,H,S,D] ~ N(0,1) of ``dtype``, O f32, in the schedule form of the
@@ -536,11 +536,11 @@ def attention(B: int = 8, H: int = 32, S: int = 4096, D: int = 128, BM: int = 12
     p.body = tile([axis("ab", B), axis("ah", H), axis("a0_b", S // BM, parent=("a0", S)),
                    axis("a5_b", 1, parent=("a5", D)), axis("a0_u", U0), axis("a5_u", U1)], body)
     p.grid, p.block = (B * H * (S // BM), 1, 1), (U0 * U1, 1, 1)
-    # the template's shared memory: Q tile + a 2-stage ring of K/V tiles (+ slack)
-    # the template's shared memory: the Q tile, a K ring and a V ring of
-    # 128 x D tiles (3 + 2 stages at D=128, 4 + 4 below), plus barriers
-    tb = BM * D * 2
-    p.smem = tb * (1 + (5 if D >= 128 else 8)) + 8192
+    # the template's shared memory: the BM/128 Q tiles, a K ring and a V ring
+    # of 128 x D tiles (3 + 2 stages at D=128, 4 + 4 below), barriers and the
+    # 1 KB alignment of the tiles
+    tb = 128 * D * 2
+    p.smem = tb * (BM // 128 + (5 if D >= 128 else 8)) + 2048
     p.rtol, p.atol = 2e-2, None
     p.oracle = {"family": "attention", "args": {"q": "q", "k": "k", "v": "v"},
                 "output": "matmul_1", "scale": 1.0 / math.sqrt(D),

@@ -9,33 +9,36 @@ then ``reciprocal`` + ``multiply``), here with leading batch/head axes, bf16
 Q/K/V [B,H,S,D] and an f32 output.  The reference lowers each thread's
 micro-tile to scalar FFMAs that recompute the scores per output column
 (``compile.py:1882-1928``).  This template keeps the IR's CTA -> (batch,
-head, 128 query rows) assignment and computes the tile as:
+head, BM query rows) assignment, BM = 128 * NT with NT = 1 or 2 query tiles
+of 128 rows, and computes the CTA's rows as:
 
-* TMA loads the CTA's Q tile once and K and V tiles of 128 keys into two
+* TMA loads the NT Q tiles once and K and V tiles of 128 keys into two
   separate rings (3 + 2 stages at D=128, 4 + 4 at D=64; 128-byte swizzle;
-  no multicast), each fed by its own producer thread, so a K tile is reused
-  as soon as its Q.K^T has run and the loads stay ahead of the MMAs;
-* one thread issues ``S_j = Q K_j^T`` (``tcgen05.mma kind::f16``, M=N=128)
-  into one of two TMEM score buffers, and ``O += P_{j-1} V_{j-1}`` with P read
-  from TMEM (the ``[a-tmem]`` form) and V as an MN-major shared operand, so
-  the scores of block j+1 overlap the softmax of block j;
-* eight softmax warps, two threads per query row (the row is the thread's
-  TMEM lane; each thread owns half of the 128 score columns and half of the
-  D output columns): half-row maxima exchanged through shared memory under a
-  64-arrival mbarrier, ``p = 2^(s*c - m)`` (c = s*log2 e), P written back
-  over S as packed bf16 pairs, partial row sums; the exponent base m moves
-  only when the row max grows by more than 2^8, and only then is the running
-  O row rescaled in TMEM by ``2^(m_old - m_new)`` (the same base is used for
-  the final 1/l, so this is exact);
-* after the last block the two half sums are added and each thread scales
-  its half of the O row by 1/l and stores it.
+  no multicast), each fed by its own producer thread;
+* one thread issues, per key block j and query tile t, ``O_t += P_t V_j``
+  (P read from TMEM, the ``[a-tmem]`` form; V an MN-major shared operand)
+  followed by ``S_t = Q_t K_{j+1}^T`` (M=N=128) into the tile's TMEM score
+  buffer.  With two tiles the tensor pipe works on one tile while the other
+  tile's softmax runs (ping-pong), so neither waits for the other;
+* four softmax warps per tile, one thread per query row (the row is the
+  thread's TMEM lane): the row max over the 128 scores (read in two halves),
+  ``p = 2^(s*c - m)`` (c = s*log2 e) written back over S as packed bf16
+  pairs, the row sum; the exponent base m moves only when the row max grows
+  by more than 2^8, and only then is the running O row rescaled in TMEM by
+  ``2^(m_old - m_new)`` (the same base is used for the final 1/l, so this is
+  exact).  O_t is idle at that point: the previous ``P V`` of the tile is
+  ordered before the ``Q K^T`` whose completion released the scores;
+* after the last block each thread scales its O row by 1/l and stores it.
 
-The arithmetic is the IR's: the same online-softmax recurrence (max, the
-exp rescale factor of the previous state, sum, weighted sum), evaluated per
+TMEM: S_t at columns 128 t, O_t at 256 + D t (512 columns allocated).  The
+arithmetic is the IR's: the same online-softmax recurrence (max, the exp
+rescale factor of the previous state, sum, weighted sum), evaluated per
 128-key block instead of per key.  Every mbarrier wait is bounded by
 ``%globaltimer`` (2 s) and reports through ``__emmy_status``.
 """
 from __future__ import annotations
+
+import struct
 
 from ..analysis import NotAffine, affine, kind, walk
 from ..ptx import Kernel
@@ -43,10 +46,24 @@ from .common import TemplateMismatch
 from .gemm import GemmTemplate, _desc_hi, idesc_mma
 
 LOG2E = 1.4426950408889634
+SMEM_MAX = 227 * 1024
+# 2^f on [-0.5, 0.5]: degree-3 polynomial minimising the maximum relative
+# error (linear-programming fit on 4001 points; 7.5e-5), f32 coefficients
+EXP2_POLY = (0.9999280571937561, 0.6932608485221863, 0.24261115491390228, 0.05517221987247467)
+
+# warp roles (512 threads): softmax warps 0..4*NT-1, then these
+MMA_WARP, PROD_K_WARP, PROD_V_WARP = 8, 9, 10
+# registers per thread: at launch, and after setmaxnreg for the softmax
+# warpgroups and for the rest (2 x 128 x 200 + 2 x 128 x 56 = 512 x 128)
+LAUNCH_REGS, SOFT_REGS, ROLE_REGS = 128, 200, 56
 
 
 class AttentionTemplate:
     name = "attention"
+    # column pairs per 16 whose exp2 runs on the FMA pipe instead of the
+    # MUFU, by head dim (measured: a polynomial pair costs more issue and
+    # FMA-pipe time than two MUFU ex2, so only the MUFU-bound D=64 gains)
+    POLY = {64: 4, 128: 0}
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -121,17 +138,18 @@ class AttentionTemplate:
         for w in writes:
             r = affine(w.index[2])
             BM = r.coef("a0_b")
-        if BM != 128 or ext["a0_b"] * 128 != S or ext["a5_b"] != 1 or D not in (64, 128) or \
-                S % 128 or ext["ab"] != B or ext["ah"] != H:
+        if BM not in (128, 256) or ext["a0_b"] * BM != S or ext["a5_b"] != 1 or \
+                D not in (64, 128) or S % 128 or ext["ab"] != B or ext["ah"] != H:
             raise TemplateMismatch("tile geometry")
-        if ctx.block != (512, 1, 1) or ctx.grid[0] * ctx.grid[1] * ctx.grid[2] != B * H * S // 128:
+        if ctx.block != (512, 1, 1) or ctx.grid[0] * ctx.grid[1] * ctx.grid[2] != B * H * S // BM:
             raise TemplateMismatch("launch geometry")
         self = cls()
         self.ctx, self.q, self.k, self.v, self.out, self.scale_buf = ctx, q, k_, v, out, scale_buf
         self.B, self.H, self.S, self.D = B, H, S, D
+        self.NT = BM // 128
         self.tile_bytes = TB = 128 * D * 2
-        # Q tile + K ring + V ring, sized from the launch's shared memory
-        avail = min(ctx.smem_bytes, 227 * 1024) - 1024 - 512 - 3072 - TB
+        # Q tiles + K ring + V ring, sized from the launch's shared memory
+        avail = min(ctx.smem_bytes, SMEM_MAX) - 1024 - 512 - self.NT * TB
         n = min(8, avail // TB)
         if n < 4:
             raise TemplateMismatch("meta smem_bytes too small for 2+2 K/V stages")
@@ -141,9 +159,9 @@ class AttentionTemplate:
     # ------------------------------------------------------------------- emit
     def emit(self) -> str:
         ctx = self.ctx
-        D, S = self.D, self.S
+        D, S, NT = self.D, self.S, self.NT
         NB = S // 128                      # key blocks
-        QB = S // 128                      # query blocks per head
+        QB = S // (128 * NT)               # CTAs per (batch, head)
         TB = self.tile_bytes               # one 128 x D bf16 tile
         NBX = D // 64                      # 64-column boxes per tile
         params = ctx.params() + [("tmapQ", ".align 64 .b8", "[128]"),
@@ -157,7 +175,8 @@ class AttentionTemplate:
         for nm, buf in (("tmapQ", self.q), ("tmapK", self.k), ("tmapV", self.v)):
             k.directive(f"tmap {nm} buf={buf} dtype=9 dims={D},{rows} strides={D * 2} "
                         f"box=64,128 swizzle=3")
-        k.comment(f"emmy-b200 template: tcgen05 flash attention B={self.B} H={self.H} S={S} D={D}")
+        k.comment(f"emmy-b200 template: tcgen05 flash attention B={self.B} H={self.H} S={S} "
+                  f"D={D}, {NT} query tile(s) per CTA")
         obase = k.param_ptr(self.out)
         sbuf = k.param_ptr(self.scale_buf)
         tq, tk, tv = (k.reg("rd") for _ in range(3))
@@ -177,17 +196,17 @@ class AttentionTemplate:
         krow0 = k.reg("r")
         k(f"mul.lo.u32 {krow0}, {bh}, {S};")
         qrow0 = k.reg("r")
-        k(f"mad.lo.u32 {qrow0}, {qb}, 128, {krow0};")
+        k(f"mad.lo.u32 {qrow0}, {qb}, {128 * NT}, {krow0};")
         SK, SV = self.SK, self.SV
-        # shared memory: Q | K ring (SK tiles) | V ring (SV tiles) | barriers |
-        # tmem slot | row exchange
+        # shared memory: Q tiles | K ring (SK tiles) | V ring (SV tiles) |
+        # barriers | tmem slot
         raw = k.reg("r")
         k(f"mov.u32 {raw}, __emmy_smem;")
         qs = k.reg("r")
         k(f"add.u32 {qs}, {raw}, 1023;")
         k(f"and.b32 {qs}, {qs}, -1024;")
         kring = k.reg("r")
-        k(f"add.u32 {kring}, {qs}, {TB};")
+        k(f"add.u32 {kring}, {qs}, {NT * TB};")
         vring = k.reg("r")
         k(f"add.u32 {vring}, {kring}, {SK * TB};")
         bars = k.reg("r")
@@ -196,18 +215,14 @@ class AttentionTemplate:
         Q_FULL = 0
         K_FULL, K_EMPTY = 1, 1 + SK
         V_FULL, V_EMPTY = 1 + 2 * SK, 1 + 2 * SK + SV
-        S_FULL = 1 + 2 * SK + 2 * SV
-        P_READY = S_FULL + 2
-        O_DONE = P_READY + 2
-        FINAL = O_DONE + 1
-        XBAR = FINAL + 1          # xbar[q]: the two warps of row quarter q (64 arrivals)
-        NSLOT = XBAR + 4
+        S_FULL = V_EMPTY + SV          # [NT]: scores of tile t ready (tcgen05.commit)
+        P_READY = S_FULL + NT          # [NT]: the 4 softmax warps wrote P of tile t
+        FINAL = P_READY + NT           # [NT]: last P V of tile t done
+        DRAIN = FINAL + NT             # the MMA thread's own ops in flight at exit
+        NSLOT = DRAIN + 1
+        assert NSLOT * 8 + 4 <= 512
         tslot = k.reg("r")
         k(f"add.u32 {tslot}, {bars}, {NSLOT * 8};")
-        # row-max / row-sum exchange between the two threads of a row:
-        # xch[parity][half][row] f32 at bars + 512, the final sums at +2048
-        xch = k.reg("r")
-        k(f"add.u32 {xch}, {bars}, 512;")
         status = k.reg("rd")
         k(f"mov.u64 {status}, __emmy_status;")
         p0 = k.reg("p")
@@ -215,16 +230,16 @@ class AttentionTemplate:
         skip = k.label("SKIP_INIT")
         k(f"@!{p0} bra {skip};")
         for slot in range(NSLOT):
-            cnt = 256 if slot in (P_READY, P_READY + 1) else 64 if slot >= XBAR else 1
+            cnt = 4 if P_READY <= slot < P_READY + NT else 1
             k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * slot}], {cnt};")
         k("fence.mbarrier_init.release.cluster;")
         for r in (tq, tk, tv):
             k(f"prefetch.tensormap [{r}];")
         k.mark(skip)
-        pw1 = k.reg("p")
-        k(f"setp.eq.u32 {pw1}, {warp}, 1;")
+        pwm = k.reg("p")
+        k(f"setp.eq.u32 {pwm}, {warp}, {MMA_WARP};")
         skip2 = k.label("SKIP_ALLOC")
-        k(f"@!{pw1} bra {skip2};")
+        k(f"@!{pwm} bra {skip2};")
         k(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{tslot}], 512;")
         k("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;")
         k.mark(skip2)
@@ -233,13 +248,33 @@ class AttentionTemplate:
         k("tcgen05.fence::after_thread_sync;")
         tmem = k.reg("r")
         k(f"ld.shared.u32 {tmem}, [{tslot}];")
-        teardown = k.label("TEARDOWN")
+        # register split: the softmax warpgroups (one row of scores each in
+        # registers) take SOFT_REGS, the others give theirs up; the launch
+        # holds exactly 512 x LAUNCH_REGS (.maxnreg with setmaxnreg makes
+        # ptxas allocate exactly that), and the shares add up to no more
+        shares = [SOFT_REGS if g_ < NT else ROLE_REGS for g_ in range(4)]
+        assert sum(128 * r for r in shares) <= 512 * LAUNCH_REGS
+        k.maxnreg = LAUNCH_REGS
+        k.directive(f"regsplit launch={LAUNCH_REGS} threads=512 "
+                    f"warpgroups={','.join(str(r) for r in shares)}")
         pl0 = k.reg("p")
         k(f"setp.eq.u32 {pl0}, {lane}, 0;")
+        # the softmax warps branch to their code, which setmaxnreg.inc
+        # dominates; everyone else gives up registers first.  The two regions
+        # never merge again (each ends in its own barrier and exit): code
+        # reached from both would need one register assignment valid under
+        # both limits
+        pwg = k.reg("p")
+        k(f"setp.lt.u32 {pwg}, {warp}, {4 * NT};")
+        soft_entry = k.label("SOFTMAX")
+        k(f"@{pwg} bra {soft_entry};")
+        k(f"setmaxnreg.dec.sync.aligned.u32 {ROLE_REGS};")
+        teardown = k.label("TEARDOWN")
+        soft_teardown = k.label("SOFT_TEARDOWN")
         wait = GemmTemplate._wait
 
         def bar(slot, idx=None):
-            """Address of barrier ``slot`` (+ a 0/1 register index)."""
+            """Address of barrier ``slot`` (+ a register index)."""
             r = k.reg("r")
             if idx is None:
                 k(f"add.u32 {r}, {bars}, {8 * slot};")
@@ -247,15 +282,6 @@ class AttentionTemplate:
                 k(f"mad.lo.u32 {r}, {idx}, 8, {bars};")
                 k(f"add.u32 {r}, {r}, {8 * slot};")
             return r
-
-        j = k.reg("r")
-        b = k.reg("r")      # j % 2  (ring stage and score buffer)
-        ph = k.reg("r")     # (j / 2) % 2
-
-        def split(jreg):
-            k(f"and.b32 {b}, {jreg}, 1;")
-            k(f"shr.u32 {ph}, {jreg}, 1;")
-            k(f"and.b32 {ph}, {ph}, 1;")
 
         def ring_slot(jreg, depth):
             """(stage, phase) of block j in a ring of ``depth`` stages."""
@@ -266,6 +292,11 @@ class AttentionTemplate:
             k(f"and.b32 {ph_}, {ph_}, 1;")
             return st_, ph_
 
+        def commit(addr):
+            k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{addr}];")
+
+        j = k.reg("r")
+
         def producer(which, warp_id, tmap, ring, depth, full, empty, load_q):
             pp = k.reg("p")
             k(f"setp.eq.u32 {pp}, {warp}, {warp_id};")
@@ -274,10 +305,14 @@ class AttentionTemplate:
             k(f"@!{pp} bra {end_p};")
             if load_q:
                 qf = bar(Q_FULL)
-                k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qf}], {TB};")
-                for i in range(NBX):
-                    k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-                      f"[{qs}+{i * 16384}], [{tq}, {{{64 * i}, {qrow0}}}], [{qf}];")
+                k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qf}], {NT * TB};")
+                for t in range(NT):
+                    qr = k.reg("r")
+                    k(f"add.u32 {qr}, {qrow0}, {128 * t};")
+                    for i in range(NBX):
+                        k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx"
+                          f"::bytes [{qs}+{t * TB + i * 16384}], [{tq}, {{{64 * i}, {qr}}}], "
+                          f"[{qf}];")
             k(f"mov.u32 {j}, 0;")
             top = k.label(f"PROD_{which}")
             k.mark(top)
@@ -294,22 +329,24 @@ class AttentionTemplate:
             for i in range(NBX):
                 k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
                   f"[{dst}+{i * 16384}], [{tmap}, {{{64 * i}, {kr}}}], [{fb}];")
+            k.comment(f"@trace {10 if load_q else 11} {j}")
             k(f"add.u32 {j}, {j}, 1;")
             pl = k.reg("p")
             k(f"setp.lt.u32 {pl}, {j}, {NB};")
             k(f"@{pl} bra {top};")
             k.mark(end_p)
 
-        # ---------------- producers: K (and Q) on warp 0, V on warp 2 ----------------
-        producer("K", 0, tk, kring, SK, K_FULL, K_EMPTY, True)
-        producer("V", 2, tv, vring, SV, V_FULL, V_EMPTY, False)
+        # ---------------- producers: Q and K on one warp, V on another ----------------
+        producer("K", PROD_K_WARP, tk, kring, SK, K_FULL, K_EMPTY, True)
+        producer("V", PROD_V_WARP, tv, vring, SV, V_FULL, V_EMPTY, False)
 
-        # ---------------- MMA issuer: warp 1 lane 0 ----------------
+        # ---------------- MMA issuer ----------------
         pm = k.reg("p")
-        k(f"setp.eq.u32 {pm}, {warp}, 1;")
+        k(f"setp.eq.u32 {pm}, {warp}, {MMA_WARP};")
         k(f"and.pred {pm}, {pm}, {pl0};")
         end_mma = k.label("END_MMA")
-        k(f"@!{pm} bra {end_mma};")
+        skip_mma = k.label("SKIP_MMA")
+        k(f"@!{pm} bra {skip_mma};")
         iqk = k.reg("r")
         k(f"mov.u32 {iqk}, {idesc_mma(128, 128, False)};")
         ipv = k.reg("r")
@@ -318,131 +355,154 @@ class AttentionTemplate:
         hiV = _desc_hi(16384, 1024)
         ptrue = k.reg("p")
         k(f"setp.eq.u32 {ptrue}, 0, 0;")
+        pfalse = k.reg("p")
+        k(f"setp.ne.u32 {pfalse}, 0, 0;")
         zero = k.reg("r")
         k(f"mov.u32 {zero}, 0;")
         wait(k, bar(Q_FULL), zero, status, 2, end_mma)
-        dq = GemmTemplate._desc(k, qs, hiK)
-        o_tm = k.reg("r")
-        k(f"add.u32 {o_tm}, {tmem}, 256;")
+        dq = []
+        for t in range(NT):
+            qa = k.reg("r")
+            k(f"add.u32 {qa}, {qs}, {t * TB};")
+            dq.append(GemmTemplate._desc(k, qa, hiK))
 
-        def issue_qk(jreg):
+        def k_ready(jreg):
+            """Wait for K block ``jreg``; return (its descriptor, its stage)."""
             kst, kph = ring_slot(jreg, SK)
             wait(k, bar(K_FULL, kst), kph, status, 2, end_mma)
             k("tcgen05.fence::after_thread_sync;")
             kad = k.reg("r")
             k(f"mad.lo.u32 {kad}, {kst}, {TB}, {kring};")
-            dk = GemmTemplate._desc(k, kad, hiK)
-            sb = k.reg("r")
-            k(f"and.b32 {sb}, {jreg}, 1;")
-            s_tm = k.reg("r")
-            k(f"mad.lo.u32 {s_tm}, {sb}, 128, {tmem};")
-            pfirst = k.reg("p")
-            k(f"setp.ne.u32 {pfirst}, 0, 0;")       # the first MMA overwrites S
+            return GemmTemplate._desc(k, kad, hiK), kst
+
+        def issue_qk(t, dk, jreg):
+            """S_t = Q_t K^T (overwrites the tile's score buffer)."""
             for kk in range(D // 16):
                 off = (kk % 4) * 2 + (kk // 4) * 1024
                 a = k.reg("rd")
-                k(f"add.s64 {a}, {dq}, {off};")
+                k(f"add.s64 {a}, {dq[t]}, {off};")
                 bd = k.reg("rd")
                 k(f"add.s64 {bd}, {dk}, {off};")
-                k(f"tcgen05.mma.cta_group::1.kind::f16 [{s_tm}], {a}, {bd}, {iqk}, "
-                  f"{pfirst if kk == 0 else ptrue};")
-            k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-              f"[{bar(S_FULL, sb)}];")
-            k.comment(f"@trace 0 {jreg}")
-            k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-              f"[{bar(K_EMPTY, kst)}];")
+                k(f"tcgen05.mma.cta_group::1.kind::f16 [{s_tm[t]}], {a}, {bd}, {iqk}, "
+                  f"{pfalse if kk == 0 else ptrue};")
+            commit(bar(S_FULL + t))
+            k.comment(f"@trace {3 * t} {jreg}")
 
-        def issue_pv(ireg, first_pred):
-            split(ireg)
-            wait(k, bar(P_READY, b), ph, status, 2, end_mma)
-            k.comment(f"@trace 1 {ireg}")
-            k("tcgen05.fence::after_thread_sync;")
-            vst, vph = ring_slot(ireg, SV)
+        def issue_pv(t, dv, pacc):
+            """O_t += P_t V (P: the first 64 columns of the score buffer)."""
+            for kk in range(8):                     # 128 keys, K=16 per MMA
+                a = k.reg("r")
+                k(f"add.u32 {a}, {s_tm[t]}, {8 * kk};")  # 16 bf16 = 8 TMEM columns
+                bd = k.reg("rd")
+                k(f"add.s64 {bd}, {dv}, {kk * 128};")   # +16 key rows * 128 B
+                k(f"tcgen05.mma.cta_group::1.kind::f16 [{o_tm[t]}], [{a}], {bd}, {ipv}, "
+                  f"{pacc if kk == 0 else ptrue};")
+
+        s_tm, o_tm = [], []
+        for t in range(NT):
+            r1 = k.reg("r")
+            k(f"add.u32 {r1}, {tmem}, {128 * t};")
+            s_tm.append(r1)
+            r2 = k.reg("r")
+            k(f"add.u32 {r2}, {tmem}, {256 + D * t};")
+            o_tm.append(r2)
+        # block 0 scores of every tile
+        k(f"mov.u32 {j}, 0;")
+        dk0, kst0 = k_ready(j)
+        for t in range(NT):
+            issue_qk(t, dk0, j)
+        commit(bar(K_EMPTY, kst0))
+        jn = k.reg("r")
+        pacc = k.reg("p")
+        par = k.reg("r")
+
+        def block(last: bool):
+            """P V of block j for every tile, each followed (unless ``last``)
+            by that tile's scores of block j+1."""
+            vst, vph = ring_slot(j, SV)
             wait(k, bar(V_FULL, vst), vph, status, 2, end_mma)
+            k.comment(f"@trace 8 {j}")
+            k("tcgen05.fence::after_thread_sync;")
             vad = k.reg("r")
             k(f"mad.lo.u32 {vad}, {vst}, {TB}, {vring};")
             dv = GemmTemplate._desc(k, vad, hiV)
-            p_tm = k.reg("r")
-            k(f"mad.lo.u32 {p_tm}, {b}, 128, {tmem};")
-            for kk in range(8):                     # 128 keys, K=16 per MMA
-                a = k.reg("r")
-                k(f"add.u32 {a}, {p_tm}, {8 * kk};")   # 16 bf16 = 8 TMEM columns
-                bd = k.reg("rd")
-                k(f"add.s64 {bd}, {dv}, {kk * 128};")  # +16 key rows * 128 B
-                k(f"tcgen05.mma.cta_group::1.kind::f16 [{o_tm}], [{a}], {bd}, {ipv}, "
-                  f"{first_pred if kk == 0 else ptrue};")
-            k.comment(f"@trace 2 {ireg}")
-            k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-              f"[{bar(O_DONE)}];")
-            k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-              f"[{bar(V_EMPTY, vst)}];")
+            k(f"setp.ne.u32 {pacc}, {j}, 0;")
+            k(f"and.b32 {par}, {j}, 1;")
+            dk = kst = None
+            for t in range(NT):
+                wait(k, bar(P_READY + t), par, status, 2, end_mma)
+                k.comment(f"@trace {3 * t + 1} {j}")
+                k("tcgen05.fence::after_thread_sync;")
+                issue_pv(t, dv, pacc)
+                k.comment(f"@trace {3 * t + 2} {j}")
+                if last:
+                    commit(bar(FINAL + t))
+                else:
+                    if t == 0:
+                        k(f"add.u32 {jn}, {j}, 1;")
+                        dk, kst = k_ready(jn)
+                        k.comment(f"@trace 9 {jn}")
+                    issue_qk(t, dk, jn)
+            commit(bar(V_EMPTY, vst))
+            if not last:
+                commit(bar(K_EMPTY, kst))
 
-        k(f"mov.u32 {j}, 0;")
-        issue_qk(j)
-        k(f"mov.u32 {j}, 1;")
-        jm = k.reg("r")
-        pacc = k.reg("p")
         if NB > 1:
             top2 = k.label("MMA")
             k.mark(top2)
-            issue_qk(j)
-            k(f"sub.u32 {jm}, {j}, 1;")
-            k(f"setp.ne.u32 {pacc}, {jm}, 0;")
-            issue_pv(jm, pacc)
+            block(False)
             k(f"add.u32 {j}, {j}, 1;")
             pl2 = k.reg("p")
-            k(f"setp.lt.u32 {pl2}, {j}, {NB};")
+            k(f"setp.lt.u32 {pl2}, {j}, {NB - 1};")
             k(f"@{pl2} bra {top2};")
-        k(f"mov.u32 {jm}, {NB - 1};")
-        k(f"setp.ne.u32 {pacc}, {jm}, 0;")
-        issue_pv(jm, pacc)
-        k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
-          f"[{bar(FINAL)}];")
+        k(f"mov.u32 {j}, {NB - 1};")
+        block(True)
         k.mark(end_mma)
+        # wait (bounded) for this thread's tensor-core operations still in
+        # flight, so that no MMA outlives the TMEM allocation on an error path
+        commit(bar(DRAIN))
+        wait(k, bar(DRAIN), zero, status, 6, skip_mma)
+        k.mark(skip_mma)
+        k(f"bra {teardown};")
 
-        # ------------- softmax warps 4-11: two threads per query row -------------
-        # warp w: rows 32*(w%4) + lane (its TMEM lanes), half h = (w-4)/4 of the
-        # 128 score columns and of the D output columns
-        psm = k.reg("p")
-        k(f"setp.ge.u32 {psm}, {warp}, 4;")
-        psm2 = k.reg("p")
-        k(f"setp.lt.u32 {psm2}, {warp}, 12;")
-        k(f"and.pred {psm}, {psm}, {psm2};")
+        # ------------- softmax warps 0..4*NT-1: one thread per query row -------------
+        k.mark(soft_entry)
+        k(f"setmaxnreg.inc.sync.aligned.u32 {SOFT_REGS};")
         end_sm = k.label("END_SM")
-        k(f"@!{psm} bra {end_sm};")
         q4 = k.reg("r")
         k(f"and.b32 {q4}, {warp}, 3;")
-        hh = k.reg("r")
-        k(f"sub.u32 {hh}, {warp}, 4;")
-        k(f"shr.u32 {hh}, {hh}, 2;")
+        tt = k.reg("r")                            # query tile of this warp
+        k(f"shr.u32 {tt}, {warp}, 2;")
         row = k.reg("r")
         k(f"mad.lo.u32 {row}, {q4}, 32, {lane};")
         trow = k.reg("r")
         k(f"shl.b32 {trow}, {q4}, 21;")            # TMEM lane field (32*q4) << 16
         k(f"add.u32 {trow}, {trow}, {tmem};")
-        scol = k.reg("r")
-        k(f"shl.b32 {scol}, {hh}, 6;")             # 64*h score columns
-        pcol = k.reg("r")
-        k(f"shl.b32 {pcol}, {hh}, 5;")             # 32*h packed P columns
-        ocol = k.reg("r")
-        k(f"mul.lo.u32 {ocol}, {hh}, {D // 2};")
-        k(f"add.u32 {ocol}, {ocol}, 256;")
-        otm = k.reg("r")
-        k(f"add.u32 {otm}, {trow}, {ocol};")
-        xb = k.reg("r")                            # exchange mbarrier of this row pair
-        k(f"mad.lo.u32 {xb}, {q4}, 8, {bars};")
-        k(f"add.u32 {xb}, {xb}, {8 * XBAR};")
-        mine = k.reg("r")                          # &xch[0][h][row]
-        k(f"mad.lo.u32 {mine}, {hh}, 512, {xch};")
-        k(f"mad.lo.u32 {mine}, {row}, 4, {mine};")
-        other = k.reg("r")                         # &xch[0][1-h][row]
-        k(f"xor.b32 {other}, {hh}, 1;")
-        k(f"mad.lo.u32 {other}, {other}, 512, {xch};")
-        k(f"mad.lo.u32 {other}, {row}, 4, {other};")
+        srow = k.reg("r")
+        k(f"mad.lo.u32 {srow}, {tt}, 128, {trow};")
+        orow_tm = k.reg("r")
+        k(f"mad.lo.u32 {orow_tm}, {tt}, {D}, {trow};")
+        k(f"add.u32 {orow_tm}, {orow_tm}, 256;")
+        sfull = k.reg("r")
+        k(f"mad.lo.u32 {sfull}, {tt}, 8, {bars};")
+        pready = k.reg("r")
+        k(f"add.u32 {pready}, {sfull}, {8 * P_READY};")
+        fin = k.reg("r")
+        k(f"add.u32 {fin}, {sfull}, {8 * FINAL};")
+        k(f"add.u32 {sfull}, {sfull}, {8 * S_FULL};")
         sc = k.reg("f")
         k(f"ld.global.nc.f32 {sc}, [{sbuf}];")
         k(f"rcp.rn.f32 {sc}, {sc};")
         k(f"mul.rn.f32 {sc}, {sc}, 0f{_f32hex(LOG2E)};")     # c = s * log2(e)
+        sc2 = k.reg("rd")
+        k(f"mov.b64 {sc2}, {{{sc}, {sc}}};")
+        cst = {}
+        for nm, val in (("magic", 0x4B400000), ("clamp", _bits(-126.0))) + tuple(
+                (f"c{i}", _bits(c)) for i, c in enumerate(EXP2_POLY)):
+            r = k.reg("rd" if nm != "clamp" else "f")
+            k(f"mov.b64 {r}, 0x{val:08X}{val:08X};" if nm != "clamp" else f"mov.b32 {r}, 0x{val:08X};")
+            cst[nm] = r
+        poly = self.poly_pairs()
         m = k.reg("f")                             # max used for the exponents
         k(f"mov.f32 {m}, 0fFF800000;")
         lsum = k.reg("f")
@@ -450,50 +510,183 @@ class AttentionTemplate:
         k(f"mov.u32 {j}, 0;")
         top3 = k.label("SMX")
         k.mark(top3)
-        split(j)
-        wait(k, bar(S_FULL, b), ph, status, 3, teardown)
-        k.comment(f"@trace 3 {j}")
+        spar = k.reg("r")
+        k(f"and.b32 {spar}, {j}, 1;")
+        wait(k, sfull, spar, status, 3, soft_teardown)
+        k.comment(f"@trace 6 {j}")
         k("tcgen05.fence::after_thread_sync;")
-        srow = k.reg("r")
-        k(f"mad.lo.u32 {srow}, {b}, 128, {trow};")
-        sa = k.reg("r")
-        k(f"add.u32 {sa}, {srow}, {scol};")
-        sv = k.regs("r", 64)
-        for c2 in range(2):
-            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv[32 * c2:32 * c2 + 32])}}}, "
-              f"[{sa}+{32 * c2}];")
-        k("tcgen05.wait::ld.sync.aligned;")
+
+        def ld32(col):
+            regs = k.regs("r", 32)
+            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{srow}+{col}];")
+            return regs
+
+        def wait_ld():
+            k("tcgen05.wait::ld.sync.aligned;")
+
+        def max_into(mx, vals, first):
+            """Fold ``vals`` into the eight partial maxima (3-input max)."""
+            rest = list(vals)
+            if first:
+                for i in range(8):
+                    k(f"max.f32 {mx[i]}, {rest[i]}, {rest[i + 8]}, {rest[i + 16]};")
+                rest = rest[24:]
+            for i in range(0, len(rest), 2):
+                k(f"max.f32 {mx[(i // 2) % 8]}, {mx[(i // 2) % 8]}, {rest[i]}, {rest[i + 1]};")
+
+        def exp_pack(vals, negm2, ps2):
+            """p = 2^(s*c - m) of 32 scores (f32 pairs), summed into ``ps2``;
+            returns 16 bf16 pairs.  Pairs in ``poly`` evaluate 2^x on the FMA
+            pipe instead of the MUFU."""
+            packed = k.regs("r", 16)
+            for pi in range(16):
+                x2 = k.reg("rd")
+                k(f"mov.b64 {x2}, {{{vals[2 * pi]}, {vals[2 * pi + 1]}}};")
+                k(f"fma.rn.f32x2 {x2}, {x2}, {sc2}, {negm2};")
+                e0, e1 = k.reg("f"), k.reg("f")
+                if pi in poly:
+                    self._exp2_poly(k, x2, e0, e1, cst)
+                else:
+                    t0, t1 = k.reg("f"), k.reg("f")
+                    k(f"mov.b64 {{{t0}, {t1}}}, {x2};")
+                    k(f"ex2.approx.ftz.f32 {e0}, {t0};")
+                    k(f"ex2.approx.ftz.f32 {e1}, {t1};")
+                e2 = k.reg("rd")
+                k(f"mov.b64 {e2}, {{{e0}, {e1}}};")
+                k(f"add.rn.f32x2 {ps2[pi % 4]}, {ps2[pi % 4]}, {e2};")
+                k(f"cvt.rn.bf16x2.f32 {packed[pi]}, {e1}, {e0};")
+            return packed
+
+        def st16(col, pk):
+            k(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{srow}+{col}], {{{', '.join(pk)}}};")
+
+        def rescale_o(factor):
+            """O row *= factor in TMEM (32 columns at a time)."""
+            f2 = k.reg("rd")
+            k(f"mov.b64 {f2}, {{{factor}, {factor}}};")
+            for c in range(D // 32):
+                ov = k.regs("r", 32)
+                k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, "
+                  f"[{orow_tm}+{32 * c}];")
+                wait_ld()
+                self._scale_pairs(k, ov, f2)
+                k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{orow_tm}+{32 * c}], "
+                  f"{{{', '.join(ov)}}};")
+
+        def p_ready_arrive():
+            """This warp's P (and O) stores are complete: one arrival per warp
+            on the tile's P_READY barrier (lane 0, after the warp converges)."""
+            k("tcgen05.wait::st.sync.aligned;")
+            k("tcgen05.fence::before_thread_sync;")
+            k("bar.warp.sync 0xffffffff;")
+            k(f"@{pl0} mbarrier.arrive.shared::cta.b64 _, [{pready}];")
+
+        def row_sum(ps2):
+            k(f"add.rn.f32x2 {ps2[0]}, {ps2[0]}, {ps2[1]};")
+            k(f"add.rn.f32x2 {ps2[2]}, {ps2[2]}, {ps2[3]};")
+            k(f"add.rn.f32x2 {ps2[0]}, {ps2[0]}, {ps2[2]};")
+            s0, s1 = k.reg("f"), k.reg("f")
+            k(f"mov.b64 {{{s0}, {s1}}}, {ps2[0]};")
+            k(f"add.rn.f32 {s0}, {s0}, {s1};")
+            return s0
+
+        # the row's 128 scores stay in registers for the whole block
+        sv = ld32(0) + ld32(32) + ld32(64) + ld32(96)
+        wait_ld()
+        k.comment(f"@trace 12 {j}")
+        ps2 = [k.reg("rd") for _ in range(4)]      # row-sum partials, f32 pairs
+        negm = k.reg("f")
+        negm2 = k.reg("rd")
         mx = [k.reg("f") for _ in range(8)]
-        for i in range(8):
-            k(f"max.f32 {mx[i]}, {sv[i]}, {sv[i + 8]};")
-        for i in range(16, 64):
-            k(f"max.f32 {mx[i % 8]}, {mx[i % 8]}, {sv[i]};")
-        for w in (4, 2, 1):
-            for i in range(w):
-                k(f"max.f32 {mx[i]}, {mx[i]}, {mx[i + w]};")
-        # exchange the half-row maxima (buffer by iteration parity)
-        par2 = k.reg("r")
-        k(f"and.b32 {par2}, {j}, 1;")
-        po = k.reg("r")
-        k(f"shl.b32 {po}, {par2}, 10;")
-        wa = k.reg("r")
-        k(f"add.u32 {wa}, {mine}, {po};")
-        k(f"st.shared.f32 [{wa}], {mx[0]};")
-        k(f"mbarrier.arrive.shared::cta.b64 _, [{xb}];")
-        wait(k, xb, par2, status, 5, teardown)
-        ra = k.reg("r")
-        k(f"add.u32 {ra}, {other}, {po};")
-        om = k.reg("f")
-        k(f"ld.shared.f32 {om}, [{ra}];")
-        k(f"max.f32 {mx[0]}, {mx[0]}, {om};")
-        # lazy rescaling: move the exponent base only when the row max grew by
-        # more than 2^8 (p stays <= 256); the final 1/l uses the same base
+
+        def p_pass(base, fold_max):
+            """P = 2^(s*c - base) of the 128 scores over S columns 0..63 (P of
+            32-column chunk c at 16c), summed into ``ps2``; with ``fold_max``
+            the row max is folded into ``mx`` on the way (it does not feed the
+            exponentials).  One software-pipelined stream over the 64 column
+            pairs: step s issues the scale of pair s+1, the exponentials of
+            pair s, the sum and bf16 pack of pair s-2 and one max, so the FMA
+            and ALU work issues while the MUFU works through the ex2s."""
+            k(f"neg.f32 {negm}, {base};")
+            k(f"mov.b64 {negm2}, {{{negm}, {negm}}};")
+            for r in ps2:
+                k(f"mov.b64 {r}, 0;")
+            LEAD, LAG = 1, 2
+            t2, es = {}, {}
+            packed = {}
+            maxops = []
+            if fold_max:
+                for i in range(8):
+                    maxops.append((mx[i], sv[i], sv[i + 8], sv[i + 16]))
+                rest = sv[24:]
+                for i in range(0, len(rest), 2):
+                    slot = mx[(i // 2) % 8]
+                    maxops.append((slot, slot, rest[i], rest[i + 1]))
+
+            def stage_a(q):
+                x2 = k.reg("rd")
+                k(f"mov.b64 {x2}, {{{sv[2 * q]}, {sv[2 * q + 1]}}};")
+                k(f"fma.rn.f32x2 {x2}, {x2}, {sc2}, {negm2};")
+                t2[q] = x2
+
+            def stage_b(q):
+                e0, e1 = k.reg("f"), k.reg("f")
+                if q % 16 in poly:
+                    self._exp2_poly(k, t2.pop(q), e0, e1, cst)
+                else:
+                    a0, a1 = k.reg("f"), k.reg("f")
+                    k(f"mov.b64 {{{a0}, {a1}}}, {t2.pop(q)};")
+                    k(f"ex2.approx.ftz.f32 {e0}, {a0};")
+                    k(f"ex2.approx.ftz.f32 {e1}, {a1};")
+                es[q] = (e0, e1)
+
+            def stage_c(q):
+                e0, e1 = es.pop(q)
+                e2 = k.reg("rd")
+                k(f"mov.b64 {e2}, {{{e0}, {e1}}};")
+                k(f"add.rn.f32x2 {ps2[q % 4]}, {ps2[q % 4]}, {e2};")
+                c, pi = divmod(q, 16)
+                if pi == 0:
+                    packed[c] = k.regs("r", 16)
+                k(f"cvt.rn.bf16x2.f32 {packed[c][pi]}, {e1}, {e0};")
+                if pi == 15:
+                    st16(16 * c, packed.pop(c))
+
+            stage_a(0)
+            for st_ in range(64 + LAG):
+                if st_ + LEAD < 64:
+                    stage_a(st_ + LEAD)
+                if st_ < 64:
+                    stage_b(st_)
+                if st_ - LAG >= 0:
+                    stage_c(st_ - LAG)
+                if maxops:
+                    d_, a_, b_, c_ = maxops.pop(0)
+                    k(f"max.f32 {d_}, {a_}, {b_}, {c_};")
+            assert not maxops and not t2 and not es and not packed
+
+        # speculative pass against the current base m; it stands unless a row
+        # max grew by more than 2^8 (lazy rescaling: p stays <= 256, and the
+        # final 1/l uses the same base, so this is exact)
+        p_pass(m, True)
+        k(f"max.f32 {mx[0]}, {mx[0]}, {mx[1]}, {mx[2]};")
+        k(f"max.f32 {mx[3]}, {mx[3]}, {mx[4]}, {mx[5]};")
+        k(f"max.f32 {mx[6]}, {mx[6]}, {mx[7]}, {mx[0]};")
+        k(f"max.f32 {mx[0]}, {mx[3]}, {mx[6]};")
         cand = k.reg("f")
         k(f"mul.rn.f32 {cand}, {mx[0]}, {sc};")
         thr = k.reg("f")
         k(f"add.rn.f32 {thr}, {m}, 0f41000000;")         # m + 8
         need = k.reg("p")
         k(f"setp.gt.f32 {need}, {cand}, {thr};")
+        anyw = k.reg("p")
+        k(f"vote.sync.any.pred {anyw}, {need}, 0xffffffff;")
+        fast = k.label("P_FAST")
+        k(f"@!{anyw} bra {fast};")
+        # slow path (always on the first block): new base, P again from the
+        # scores in registers, l and this warp's running O rows rescaled by
+        # 2^(m_old - m_new) (the tile's previous P V completed before its
+        # scores were released; the first block's O is not yet written)
         meff = k.reg("f")
         k(f"selp.f32 {meff}, {cand}, {m}, {need};")
         alpha = k.reg("f")
@@ -501,109 +694,111 @@ class AttentionTemplate:
         k(f"sub.rn.f32 {dlt}, {m}, {meff};")
         k(f"ex2.approx.ftz.f32 {alpha}, {dlt};")
         k(f"@!{need} mov.f32 {alpha}, 0f3F800000;")
-        negm = k.reg("f")
-        k(f"neg.f32 {negm}, {meff};")
-        ps = [k.reg("f") for _ in range(8)]
-        packed = k.regs("r", 32)
-        for i in range(0, 64, 2):
-            e2 = []
-            for ii in (i, i + 1):
-                t = k.reg("f")
-                k(f"fma.rn.f32 {t}, {sv[ii]}, {sc}, {negm};")
-                e = k.reg("f")
-                k(f"ex2.approx.ftz.f32 {e}, {t};")
-                if ii < 8:
-                    k(f"mov.f32 {ps[ii]}, {e};")
-                else:
-                    k(f"add.rn.f32 {ps[ii % 8]}, {ps[ii % 8]}, {e};")
-                e2.append(e)
-            k(f"cvt.rn.bf16x2.f32 {packed[i // 2]}, {e2[1]}, {e2[0]};")
-        pa = k.reg("r")
-        k(f"add.u32 {pa}, {srow}, {pcol};")
-        k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{pa}], {{{', '.join(packed)}}};")
-        k.comment(f"@trace 4 {j}")
-        for w in (4, 2, 1):
-            for i in range(w):
-                k(f"add.rn.f32 {ps[i]}, {ps[i]}, {ps[i + w]};")
-        k(f"fma.rn.f32 {lsum}, {lsum}, {alpha}, {ps[0]};")
-        # rescale this warp's half of the running O rows if any of its rows
-        # moved (warp-uniform), after the previous P.V has landed
+        p_pass(meff, False)
         skip_rs = k.label("NO_RESCALE")
         pj0 = k.reg("p")
         k(f"setp.eq.u32 {pj0}, {j}, 0;")
         k(f"@{pj0} bra {skip_rs};")
-        anyw = k.reg("p")
-        k(f"vote.sync.any.pred {anyw}, {need}, 0xffffffff;")
-        k(f"@!{anyw} bra {skip_rs};")
-        jp = k.reg("r")
-        k(f"sub.u32 {jp}, {j}, 1;")
-        k(f"and.b32 {jp}, {jp}, 1;")
-        wait(k, bar(O_DONE), jp, status, 3, teardown)
-        k("tcgen05.fence::after_thread_sync;")
-        half = D // 2
-        ov = k.regs("r", half)
-        for c in range(half // 32):
-            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov[32 * c:32 * c + 32])}}}, "
-              f"[{otm}+{32 * c}];")
-        k("tcgen05.wait::ld.sync.aligned;")
-        for r in ov:
-            k(f"mul.rn.f32 {r}, {r}, {alpha};")
-        for c in range(half // 32):
-            k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{otm}+{32 * c}], "
-              f"{{{', '.join(ov[32 * c:32 * c + 32])}}};")
+        rescale_o(alpha)
         k.mark(skip_rs)
-        k("tcgen05.wait::st.sync.aligned;")
-        k("tcgen05.fence::before_thread_sync;")
-        k(f"mbarrier.arrive.shared::cta.b64 _, [{bar(P_READY, b)}];")
-        k.comment(f"@trace 5 {j}")
+        k(f"mul.rn.f32 {lsum}, {lsum}, {alpha};")
         k(f"mov.f32 {m}, {meff};")
+        k.mark(fast)
+        p_ready_arrive()
+        k.comment(f"@trace 7 {j}")
+        rsum = row_sum(ps2)
+        k(f"add.rn.f32 {lsum}, {lsum}, {rsum};")
         k(f"add.u32 {j}, {j}, 1;")
         pl3 = k.reg("p")
         k(f"setp.lt.u32 {pl3}, {j}, {NB};")
         k(f"@{pl3} bra {top3};")
-        # epilogue: row sum of both halves, O half-row * (1 / l) -> global
-        k(f"st.shared.f32 [{mine}+2048], {lsum};")
-        k(f"mbarrier.arrive.shared::cta.b64 _, [{xb}];")
-        k(f"mov.u32 {par2}, {NB & 1};")
-        wait(k, xb, par2, status, 5, teardown)
-        ol = k.reg("f")
-        k(f"ld.shared.f32 {ol}, [{other}+2048];")
-        k(f"add.rn.f32 {lsum}, {lsum}, {ol};")
-        wait(k, bar(FINAL), self._zero(k), status, 3, teardown)
+        # epilogue: O row * (1 / l) -> global
+        wait(k, fin, self._zero(k), status, 3, soft_teardown)
         k("tcgen05.fence::after_thread_sync;")
         inv = k.reg("f")
         k(f"rcp.rn.f32 {inv}, {lsum};")
-        orow = k.reg("r")
-        k(f"add.u32 {orow}, {qrow0}, {row};")
+        inv2 = k.reg("rd")
+        k(f"mov.b64 {inv2}, {{{inv}, {inv}}};")
+        grow = k.reg("r")
+        k(f"mad.lo.u32 {grow}, {tt}, 128, {row};")
+        k(f"add.u32 {grow}, {grow}, {qrow0};")
         oa = k.reg("rd")
-        k(f"mul.wide.u32 {oa}, {orow}, {D * 4};")
+        k(f"mul.wide.u32 {oa}, {grow}, {D * 4};")
         k(f"add.s64 {oa}, {oa}, {obase};")
-        hoff = k.reg("rd")
-        k(f"mul.wide.u32 {hoff}, {hh}, {half * 4};")
-        k(f"add.s64 {oa}, {oa}, {hoff};")
-        for c in range(half // 32):
+        for c in range(D // 32):
             regs = k.regs("r", 32)
-            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{otm}+{32 * c}];")
-            k("tcgen05.wait::ld.sync.aligned;")
-            for r in regs:
-                k(f"mul.rn.f32 {r}, {r}, {inv};")
+            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, "
+              f"[{orow_tm}+{32 * c}];")
+            wait_ld()
+            self._scale_pairs(k, regs, inv2)
             for v8 in range(4):
                 k(f"st.global.v8.b32 [{oa}+{128 * c + 32 * v8}], "
                   f"{{{', '.join(regs[8 * v8:8 * v8 + 8])}}};")
         k.mark(end_sm)
+        k.mark(soft_teardown)
+        k("tcgen05.fence::before_thread_sync;")
+        k("barrier.sync 0;")
+        k("ret;")
 
-        # ---------------- teardown ----------------
+        # ---------------- teardown of the other warps ----------------
         k.mark(teardown)
         k("tcgen05.fence::before_thread_sync;")
         k("barrier.sync 0;")
         end = k.label("END")
-        k(f"@!{pw1} bra {end};")
+        k(f"@!{pwm} bra {end};")
         k("bar.warp.sync 0xffffffff;")
         k("tcgen05.fence::after_thread_sync;")
         k(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tmem}, 512;")
         k.mark(end)
         k("ret;")
         return k.render()
+
+    def poly_pairs(self) -> set:
+        """Which of the 16 column pairs of a 32-column chunk take the FMA-pipe
+        exp2 (``POLY`` of them, spread evenly)."""
+        n = self.POLY[self.D] if isinstance(self.POLY, dict) else self.POLY
+        return {(2 * i + 1) * 16 // (2 * n) for i in range(n)} if n else set()
+
+    @staticmethod
+    def _exp2_poly(k, t2, e0, e1, cst):
+        """2^x of an f32 pair on the FMA pipe (Cody-Waite split): x clamped to
+        >= -126, n = round(x) by adding 1.5 * 2^23, f = x - n in [-0.5, 0.5],
+        2^f by the degree-3 minimax polynomial ``EXP2_POLY`` (relative error
+        7.5e-5, below the bf16 rounding of P), then n added to the exponent
+        field (n * 2^23 taken from the low bits of x + 1.5 * 2^23)."""
+        t0, t1 = k.reg("f"), k.reg("f")
+        k(f"mov.b64 {{{t0}, {t1}}}, {t2};")
+        k(f"max.f32 {t0}, {t0}, {cst['clamp']};")
+        k(f"max.f32 {t1}, {t1}, {cst['clamp']};")
+        x2 = k.reg("rd")
+        k(f"mov.b64 {x2}, {{{t0}, {t1}}};")
+        j2 = k.reg("rd")
+        k(f"add.rn.f32x2 {j2}, {x2}, {cst['magic']};")
+        n2 = k.reg("rd")
+        k(f"sub.rn.f32x2 {n2}, {j2}, {cst['magic']};")
+        f2 = k.reg("rd")
+        k(f"sub.rn.f32x2 {f2}, {x2}, {n2};")
+        p2 = k.reg("rd")
+        k(f"fma.rn.f32x2 {p2}, {cst['c3']}, {f2}, {cst['c2']};")
+        k(f"fma.rn.f32x2 {p2}, {p2}, {f2}, {cst['c1']};")
+        k(f"fma.rn.f32x2 {p2}, {p2}, {f2}, {cst['c0']};")
+        jr = k.regs("r", 2)
+        k(f"mov.b64 {{{jr[0]}, {jr[1]}}}, {j2};")
+        pr = k.regs("r", 2)
+        k(f"mov.b64 {{{pr[0]}, {pr[1]}}}, {p2};")
+        for e, a, b in ((e0, jr[0], pr[0]), (e1, jr[1], pr[1])):
+            r = k.reg("r")
+            k(f"mad.lo.u32 {r}, {a}, 8388608, {b};")
+            k(f"mov.b32 {e}, {r};")
+
+    @staticmethod
+    def _scale_pairs(k, regs, s2):
+        """regs[i] *= s for 32 f32 registers, as 16 f32x2 multiplies."""
+        for i in range(0, len(regs), 2):
+            x2 = k.reg("rd")
+            k(f"mov.b64 {x2}, {{{regs[i]}, {regs[i + 1]}}};")
+            k(f"mul.rn.f32x2 {x2}, {x2}, {s2};")
+            k(f"mov.b64 {{{regs[i]}, {regs[i + 1]}}}, {x2};")
 
     @staticmethod
     def _zero(k):
@@ -612,6 +807,9 @@ class AttentionTemplate:
         return r
 
 
+def _bits(v: float) -> int:
+    return struct.unpack("<I", struct.pack("<f", float(v)))[0]
+
+
 def _f32hex(v: float) -> str:
-    import struct
-    return "%08X" % struct.unpack("<I", struct.pack("<f", float(v)))[0]
+    return "%08X" % _bits(v)

@@ -528,12 +528,16 @@ class GemmTemplate:
     def _wait(k, bar, parity, status, code, fail_label):
         """Spin on ``mbarrier.try_wait.parity`` for at most WAIT_NS of
         %globaltimer; on expiry store ``code`` to ``__emmy_status`` and jump
-        to ``fail_label``."""
+        to ``fail_label``.  The first try runs before the clock is read: a
+        %globaltimer read costs hundreds of cycles, which would otherwise sit
+        on the path of every wait that succeeds at once."""
+        p = k.reg("p")
+        top, ok = k.label("WAIT"), k.label("WAIT_OK")
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar}], {parity};")
+        k(f"@{p} bra {ok};")
         t0 = k.reg("rd")
         k(f"mov.u64 {t0}, %globaltimer;")
-        top, ok = k.label("WAIT"), k.label("WAIT_OK")
         k.mark(top)
-        p = k.reg("p")
         k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar}], {parity};")
         k(f"@{p} bra {ok};")
         t1 = k.reg("rd")

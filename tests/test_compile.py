@@ -110,3 +110,83 @@ def test_generic_lowering_assembles_all_goldens(native_lib, monkeypatch):
         c = compile_graph(g, m)
         assert c.kind == "generic"
         native.Image(c.render())
+
+
+@pytest.mark.parametrize("name", ["attention", "attention_d64"])
+@pytest.mark.parametrize("bm", [128, 256])
+def test_attention_register_split(name, bm):
+    """The attention kernel hands registers between warpgroups with
+    setmaxnreg: the assembled function must hold exactly the declared count
+    per thread at launch (.maxnreg with setmaxnreg), the shares must add up to
+    no more than the launch's registers, and each setmaxnreg must match its
+    share (an .inc that asks for more than was freed would wait forever)."""
+    import re
+    from emmy_b200 import harness, synth
+    g, m = synth.config(name, B=1, H=2, S=512, BM=bm).build()
+    ck = harness.CompiledKernel(g, m)
+    mo = harness._REGSPLIT_RE.search(ck.ptx)
+    assert mo, "no regsplit declaration"
+    launch, threads = int(mo.group(1)), int(mo.group(2))
+    shares = [int(x) for x in mo.group(3).split(",")]
+    assert f".maxnreg {launch}" in ck.ptx
+    assert ck.image.registers()[ck.entry] == launch
+    assert threads == 128 * len(shares) and 128 * sum(shares) <= threads * launch
+    incs = {int(x) for x in re.findall(r"setmaxnreg\.inc\.sync\.aligned\.u32 (\d+);", ck.ptx)}
+    decs = {int(x) for x in re.findall(r"setmaxnreg\.dec\.sync\.aligned\.u32 (\d+);", ck.ptx)}
+    assert incs == {max(shares)} and decs == {min(shares)}
+    harness.check_regsplit(ck.ptx, launch)
+    with pytest.raises(RuntimeError):
+        harness.check_regsplit(ck.ptx, launch - 8)
+
+
+def _defs_uses(lines):
+    """(registers written, registers read) by PTX instruction lines."""
+    reg = re.compile(r"%[a-z]+\d+")
+    stores = ("st.", "mbarrier.arrive", "mbarrier.init", "tcgen05.st", "tcgen05.mma",
+              "tcgen05.commit", "tcgen05.dealloc", "cp.async", "bar", "prefetch", "fence",
+              "tcgen05.fence", "tcgen05.wait", "red.", "bra", "ret")
+    d, u = set(), set()
+    for ln in lines:
+        s = ln.strip()
+        if not s or s.startswith(("//", "$", ".")):
+            continue
+        g = re.match(r"^@!?(%p\d+)\s+", s)
+        if g:
+            u.add(g.group(1))
+            s = s[g.end():]
+        op, _, rest = s.partition(" ")
+        regs = reg.findall(rest)
+        if op.startswith("mbarrier.try_wait") or op.startswith("mbarrier.test_wait"):
+            d.add(regs[0])
+            u.update(regs[1:])
+        elif op.startswith(stores):
+            u.update(regs)
+        elif rest.startswith("{"):
+            d.update(reg.findall(rest[:rest.index("}")]))
+            u.update(reg.findall(rest[rest.index("}"):]))
+        elif regs:
+            d.add(regs[0])
+            u.update(regs[1:])
+    return d, u
+
+
+@pytest.mark.parametrize("kw", [dict(B=1, H=1, S=128, D=128, BM=128), dict(B=1, H=2, S=512),
+                                dict(B=1, H=2, S=512, D=64)])
+def test_attention_role_regions_self_contained(kw):
+    """After the setmaxnreg split the softmax warps and the other warps run
+    under different register limits, in code regions that never merge: every
+    register a region reads must be written in that region or in the common
+    prologue before the split (a value from the other side would be
+    undefined there)."""
+    from emmy_b200 import harness, synth
+    g, m = synth.attention(**kw).build()
+    L = harness.CompiledKernel(g, m).ptx.split("\n")
+    first = next(i for i, ln in enumerate(L) if ln.startswith("{"))
+    split = next(i for i, ln in enumerate(L) if "bra $L_SOFTMAX_" in ln)
+    soft = next(i for i, ln in enumerate(L) if ln.startswith("$L_SOFTMAX_"))
+    role_end = next(i for i, ln in enumerate(L) if ln.startswith("$L_TEARDOWN_"))
+    common = _defs_uses(L[first:split + 1])[0]
+    for lo, hi, extra in ((split + 1, soft, (role_end, len(L))), (soft, role_end, None)):
+        lines = L[lo:hi] + (L[extra[0]:extra[1]] if extra else [])
+        d, u = _defs_uses(lines)
+        assert not sorted(u - d - common), (lo, sorted(u - d - common))

@@ -1,25 +1,28 @@
 """Parity on the GPU for the tcgen05 flash-attention template against the
 float64 CPU oracle on the same bf16-rounded Q/K/V: rel 2e-2 with
 atol = rtol * max|O| (BASELINE), and in practice far tighter (2e-3 of max|O|
-checked): small shapes in full (one key block, several, both head dims), the
+checked): small shapes in full (one key block, several, both head dims, one
+and two 128-row query tiles per CTA), the
 BASELINE shape (B=8, H=32, S=4096) on sampled (batch, head) pairs.  The
 kernel's bounded waits must not fire (status word 0)."""
 import numpy as np
 import pytest
 
 from emmy_b200 import synth
-from emmy_b200.data import bf16_to_f32, materialize
+from emmy_b200.data import bf16_bits, bf16_to_f32, materialize
 from oracle import expr
 
 pytestmark = pytest.mark.gpu
 
 
-def _run(p, heads=None):
+def _run(p, heads=None, transform=None):
     import torch
     from emmy_b200 import harness, native
     g, m = p.build()
     k = m["kernels"][0]
     ins = {a["name"]: materialize(a) for a in k["args"] if not a.get("output")}
+    if transform is not None:
+        ins = transform(ins)
     outs, kern = harness.run(g, m, ins)
     assert kern.kind == "attention"
     addr, _ = kern.module().global_addr("__emmy_status")
@@ -37,11 +40,14 @@ def _run(p, heads=None):
     assert err <= 4e-3 * float(np.max(np.abs(ref))), err
 
 
-CASES = [dict(B=1, H=1, S=128, D=128), dict(B=1, H=2, S=256, D=128), dict(B=2, H=2, S=512, D=64),
-         dict(B=1, H=3, S=1024, D=128)]
+# BM = 256: two query tiles per CTA (the benchmark form); BM = 128: one
+CASES = [dict(B=1, H=1, S=128, D=128, BM=128), dict(B=1, H=2, S=256, D=128),
+         dict(B=2, H=2, S=512, D=64), dict(B=1, H=3, S=1024, D=128),
+         dict(B=1, H=2, S=640, D=64, BM=128), dict(B=2, H=1, S=768, D=128, BM=128)]
 
 
-@pytest.mark.parametrize("kw", CASES, ids=[f"{c['B']}x{c['H']}x{c['S']}x{c['D']}" for c in CASES])
+@pytest.mark.parametrize("kw", CASES, ids=[f"{c['B']}x{c['H']}x{c['S']}x{c['D']}"
+                                           f"_bm{c.get('BM', 256)}" for c in CASES])
 def test_attention_small(kw):
     _run(synth.attention(**kw))
 
@@ -52,3 +58,20 @@ def test_attention_baseline_heads():
 
 def test_attention_d64_baseline_heads():
     _run(synth.config("attention_d64"), heads=[(1, 5), (6, 30)])
+
+
+def _key_ramp(ins, step=8.0):
+    """Scale key s by 1 + s/step: every 32-key chunk's row max then exceeds
+    the previous one by about 13 binades, so the exponent base moves inside
+    blocks (stored P chunks, row sums and O rescaled by 2^-k)."""
+    kf = bf16_to_f32(ins["k"]).astype(np.float32)
+    S = kf.shape[2]
+    kf = kf * (1.0 + np.arange(S, dtype=np.float32) / step)[None, None, :, None]
+    return {**ins, "k": bf16_bits(kf).reshape(ins["k"].shape)}
+
+
+@pytest.mark.parametrize("kw", [dict(B=1, H=2, S=256, D=128), dict(B=1, H=2, S=512, D=64),
+                                dict(B=1, H=1, S=384, D=128, BM=128)],
+                         ids=["d128_bm256", "d64_bm256", "d128_bm128"])
+def test_attention_growing_scores(kw):
+    _run(synth.attention(**kw), transform=_key_ramp)
