@@ -25,6 +25,7 @@ from pathlib import Path
 
 from . import ir as _ir
 from .context import KernelContext
+from .ops import UnsupportedOp
 from .templates import TEMPLATES, TemplateMismatch
 
 Graph = _ir.Graph
@@ -67,7 +68,18 @@ class Compiler:
 
     def compile(self):
         self.template = self.select()
-        self.ptx = self.template.emit()
+        try:
+            self.ptx = self.template.emit()
+        except UnsupportedOp as e:
+            # a template accepted the schedule but its op emitter lacks one of
+            # the IR's elementwise ops: the statement-by-statement lowering
+            # has the full op set
+            if getattr(self.template, "name", "generic") == "generic":
+                raise
+            self.rejections.append((self.template.name, str(e)))
+            from .generic import GenericLowering
+            self.template = GenericLowering(self.ctx)
+            self.ptx = self.template.emit()
         return self
 
     def render(self) -> str:

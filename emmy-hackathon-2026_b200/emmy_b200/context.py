@@ -38,6 +38,13 @@ class KernelContext:
                 raise ValueError("meta.json has no kernels")
             info = kernels[0]
         self.info = info
+        # the launch descriptor's argument dtypes are what the runtime
+        # allocates; where the graph's tensor dtype disagrees (an IR whose
+        # writes convert, e.g. f32 arithmetic stored to an i32 buffer), the
+        # buffer's own dtype wins
+        for a in info.get("args", []):
+            if not a.get("scalar") and a.get("dtype") and a["name"] in self.bufs.dtypes:
+                self.bufs.dtypes[a["name"]] = a["dtype"]
         self.arg_order = list(info["arg_order"])
         self.scalar_tys = {a["name"]: a["dtype"] for a in info.get("args", []) if a.get("scalar")}
         self.grid = tuple(int(x) for x in info["grid"])

@@ -737,6 +737,15 @@ class GenericLowering:
             root = self.ival(I_Var(iv))
         base = self._iadd(self._imul(tid, scale), root)
         bid = int(s.barrier_id or 0)
+        # the tree reads entries [0, length) (times ``scale``, plus the inner
+        # root < scale): a tree longer than its buffer would read shared
+        # memory outside it, so such an IR is refused rather than lowered
+        for buf in s.bufs:
+            entries = prod(self.smem[buf]["extents"])
+            if (s.length - 1) * scale + (scale - 1) >= entries:
+                raise NotImplementedError(
+                    f"TreeHalve of length {s.length} (scale {scale}) reads past its "
+                    f"shared buffer {buf} of {entries} entries")
         # halving steps (n live entries -> ceil(n/2)); for a power of two this
         # is the plain tree: level = n/2, entries [0, level) fold [level, n)
         steps = []
@@ -828,7 +837,10 @@ class GenericLowering:
             a = [self.convert(v, t, cty) for v, t in args]
             p = k.reg("p")
             pt = cty if cty in ("f32", "f64") else PTY[cty]
-            k(f"setp.{CMP[op]}.{pt} {p}, {a[0]}, {a[1]};")
+            # C '!=' is true when either side is NaN: the unordered form for
+            # floats (reference compile.py:1532-1551 negates an ordered eq)
+            cmp = "neu" if op == "not_equal" and cty in ("f32", "f64") else CMP[op]
+            k(f"setp.{cmp}.{pt} {p}, {a[0]}, {a[1]};")
             r = k.reg("r")
             k(f"selp.u32 {r}, 1, 0, {p};")
             res = (r, "bool")
@@ -879,7 +891,10 @@ class GenericLowering:
             q = k.reg("f")
             k(f"div.rn.f32 {q}, {a[0]}, {a[1]};")
             t = k.reg("f")
-            rnd = "rzi" if op == "fmod" else "rmi"
+            # floor_divide floors; mod / remainder / fmod are C '%' on floats
+            # (truncated quotient, the result keeps the dividend's sign), as
+            # the reference lowers all three (compile.py:752-770)
+            rnd = "rmi" if op == "floor_divide" else "rzi"
             k(f"cvt.{rnd}.f32.f32 {t}, {q};")
             if op == "floor_divide":
                 return t
