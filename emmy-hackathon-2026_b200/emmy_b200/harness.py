@@ -91,6 +91,30 @@ class CompiledKernel:
         self._module = None
         self._kernel = None
 
+    @classmethod
+    def from_ptx(cls, ptx: str, kernel_info: dict, arch: str = "sm_100a") -> "CompiledKernel":
+        """A kernel given as PTX text (a file, another compiler's output),
+        launched under one ``meta.json`` kernel entry: parameters in its
+        ``arg_order``, scalars from its ``args``, tensor maps if the PTX
+        declares any."""
+        from types import SimpleNamespace
+        self = cls.__new__(cls)
+        self.graph_dict = self.meta = self.compiler = None
+        self.ptx = ptx
+        self.kind = "ptx"
+        self.info = kernel_info
+        self.ctx = SimpleNamespace(
+            entry=kernel_info["entry"], arg_order=list(kernel_info["arg_order"]),
+            scalar_tys={a["name"]: a["dtype"] for a in kernel_info.get("args", [])
+                        if a.get("scalar")},
+            info=kernel_info)
+        self.image = native.Image(ptx, arch)
+        self.tmaps = parse_tmaps(ptx)
+        self.cluster = parse_cluster(ptx)
+        self._module = None
+        self._kernel = None
+        return self
+
     @property
     def entry(self) -> str:
         return self.ctx.entry

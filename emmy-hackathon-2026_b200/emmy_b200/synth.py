@@ -23,7 +23,11 @@ reference's convention: an input's seed is its index in ``graph.inputs``
 """
 from __future__ import annotations
 
+import json
 import math
+from pathlib import Path
+
+import numpy as np
 
 from . import ir as I
 
@@ -217,6 +221,171 @@ class Problem:
 
     def build(self) -> tuple[dict, dict]:
         return self.graph(), self.meta()
+
+    def write(self, folder, expected: dict | None = None) -> Path:
+        """The problem as a folder in the reference's format."""
+        return write_problem(folder, {self.entry: self.graph()}, self.meta(), expected)
+
+
+def write_problem(folder, irs: dict, meta: dict, expected: dict | None = None) -> Path:
+    """A problem folder as the reference's generator lays it out (reference
+    ``tools/generate.py:177-199``): ``<entry>.ir.json`` per kernel,
+    ``meta.json``, and ``expected.npz`` (graph output -> array) when given."""
+    folder = Path(folder)
+    folder.mkdir(parents=True, exist_ok=True)
+    for entry, g in irs.items():
+        (folder / f"{entry}.ir.json").write_text(json.dumps(g, indent=1))
+    (folder / "meta.json").write_text(json.dumps(meta, indent=1))
+    if expected is not None:
+        np.savez(folder / "expected.npz", **expected)
+    return folder
+
+
+class Pipeline:
+    """A problem of several kernels run in order, later ones reading buffers
+    earlier ones wrote -- the shape of Emmy's multi-kernel lowerings as the
+    reference's generator packages them (``tools/generate.py:108-146``: an
+    argument no InputOp or ConstantOp provides is ``intermediate``; a kernel is
+    ``final`` when it writes a graph output) and its ``submit.py`` chains them
+    (``:112-122``).  Each stage is a :class:`Problem` whose inputs name graph
+    inputs or earlier stages' outputs."""
+
+    def __init__(self, pid: str, code: str, stages: list, graph_inputs: list,
+                 graph_outputs: list, rtol: float, atol: float, oracle: dict | None = None):
+        self.pid, self.code, self.stages = pid, code, stages
+        self.graph_inputs = graph_inputs          # [(name, dist or None)]
+        self.graph_outputs = graph_outputs
+        self.rtol, self.atol, self.oracle = rtol, atol, oracle
+
+    def build(self) -> tuple[dict, dict]:
+        gin = [n for n, _ in self.graph_inputs]
+        dists = dict(self.graph_inputs)
+        irs, kernels, produced = {}, [], set()
+        for st in self.stages:
+            irs[st.entry] = st.graph()
+            args, order = [], []
+            for name, value in st.consts:
+                args.append({"name": name, "dtype": "f32", "shape": [1], "data": [value]})
+                order.append(name)
+            for name, shape, dt, _ in st.inputs:
+                a = {"name": name, "dtype": dt, "shape": list(shape)}
+                if name in gin:
+                    a["seed"] = gin.index(name)
+                    if dists[name]:
+                        a["dist"] = dists[name]
+                elif name in produced:
+                    a["intermediate"] = True
+                else:
+                    raise ValueError(f"{st.entry}: {name} is neither a graph input nor "
+                                     f"written by an earlier kernel")
+                args.append(a)
+                order.append(name)
+            oname, oshape, odt = st.out
+            args.append({"name": oname, "dtype": odt, "shape": list(oshape), "output": True})
+            order.append(oname)
+            produced.add(oname)
+            kernels.append({"node": st.node, "entry": st.entry, "arg_order": order,
+                            "grid": list(st.grid), "block": list(st.block),
+                            "smem_bytes": st.smem, "zero_outputs": list(st.zero),
+                            "args": args, "final": oname in self.graph_outputs})
+        meta = {"id": self.pid, "code": self.code, "rtol": self.rtol, "atol": self.atol,
+                "graph_inputs": gin, "graph_outputs": list(self.graph_outputs),
+                "kernels": kernels, "oracle": self.oracle}
+        return irs, meta
+
+    def write(self, folder, expected: dict | None = None) -> Path:
+        irs, meta = self.build()
+        return write_problem(folder, irs, meta, expected)
+
+
+def _row_reduce_stage(entry, node, src_load, value_ops, acc_op, combine, post, out, rows, cols,
+                      block, inputs, consts=()):
+    """One CTA per row: a strided loop folds ``value_ops`` into acc0, the block
+    combines, ``post`` finishes, thread 0 of the row writes ``out[row]``."""
+    st = Problem(node, "", entry, node)
+    for c, v in consts:
+        st.add_const(c, v)
+    for name, shape in inputs:
+        st.add_input(name, shape)
+    st.out = (out, (rows,), "f32")
+    loop = strided(axis("a1", cols), V("a1_co"), block,
+                   [src_load] + list(value_ops) + [accum("acc0", "v_in", op=acc_op, axes=("a1",))])
+    st.body = tile([axis("a0", rows), axis("a1_co", block)],
+                   [loop] + combine_block(["acc0"], block, combine) + list(post) +
+                   [I.Cond(eq(V("a1_co"), Lit(0)), (write(out, (V("a0"),), ("r_out",)),), ())])
+    st.grid, st.block = (rows, 1, 1), (block, 1, 1)
+    return st
+
+
+def _elementwise_stage(entry, node, body, out, rows, cols, inputs, consts=(), threads=256):
+    """One thread per (row, column) element."""
+    st = Problem(node, "", entry, node)
+    for c, v in consts:
+        st.add_const(c, v)
+    for name, shape in inputs:
+        st.add_input(name, shape)
+    st.out = (out, (rows, cols), "f32")
+    st.body = tile([axis("a0", rows), axis("a1", cols)], body)
+    n = rows * cols
+    st.grid, st.block = (-(-n // threads), 1, 1), (threads, 1, 1)
+    return st
+
+
+def rmsnorm_two_kernel(rows: int = 256, cols: int = 1024, block: int = 128,
+                       eps: float = 1e-6) -> Pipeline:
+    """RMSNorm as two kernels: ``ms[r] = mean(x[r]^2)`` into an intermediate,
+    then ``y = x * rsqrt(ms + eps) * w``."""
+    s1 = _row_reduce_stage(
+        "k_rms_meansq", "ms", load("in0", "x", V("a0"), V("a1")),
+        [assign("v_in", "multiply", "in0", "in0")], "add", add_combine(),
+        [load("c0", "mean_count", Lit(0)), assign("rc", "reciprocal", "c0"),
+         assign("r_out", "multiply", "acc0", "rc")],
+        "ms", rows, cols, block, [("x", (rows, cols))], consts=[("mean_count", cols)])
+    s2 = _elementwise_stage(
+        "k_rms_apply", "mul_1",
+        [load("m", "ms", V("a0")), load("e", "add_c1", Lit(0)), assign("v0", "add", "m", "e"),
+         assign("v1", "sqrt", "v0"), assign("v2", "reciprocal", "v1"),
+         load("xi", "x", V("a0"), V("a1")), assign("v3", "multiply", "xi", "v2"),
+         load("wi", "w", V("a1")), assign("v4", "multiply", "wi", "v3"),
+         write("mul_1", (V("a0"), V("a1")), ("v4",))],
+        "mul_1", rows, cols, [("x", (rows, cols)), ("ms", (rows,)), ("w", (cols,))],
+        consts=[("add_c1", eps)])
+    return Pipeline(f"rmsnorm2k_{rows}x{cols}", "x * rsqrt(mean(x^2)+eps) * w", [s1, s2],
+                    [("x", None), ("w", {"kind": "uniform", "lo": 0.5, "hi": 1.5})], ["mul_1"],
+                    rtol=1e-5, atol=1e-5,
+                    oracle={"family": "rmsnorm", "args": {"x": "x", "w": "w"},
+                            "output": "mul_1", "eps": eps})
+
+
+def softmax_three_kernel(rows: int = 128, cols: int = 2048, block: int = 128,
+                         scale: float = 4.0) -> Pipeline:
+    """Row softmax of ``scale * x`` as three kernels: row max, row sum of
+    ``exp(scale*x - max)``, then the normalised exponentials."""
+    sx = [load("c0", "mul_c1", Lit(0)), assign("sxv", "multiply", "in0", "c0")]
+    s1 = _row_reduce_stage(
+        "k_sm_max", "rmax", load("in0", "x", V("a0"), V("a1")),
+        sx + [assign("v_in", "copy", "sxv")], "maximum",
+        [assign("acc0", "maximum", "acc0", "acc0__o", dtype=None)],
+        [assign("r_out", "copy", "acc0")], "rmax", rows, cols, block,
+        [("x", (rows, cols))], consts=[("mul_c1", scale)])
+    s2 = _row_reduce_stage(
+        "k_sm_sum", "rsum", load("in0", "x", V("a0"), V("a1")),
+        sx + [load("mx", "rmax", V("a0")), assign("d", "subtract", "sxv", "mx"),
+              assign("v_in", "exp", "d")], "add", add_combine(),
+        [assign("r_out", "copy", "acc0")], "rsum", rows, cols, block,
+        [("x", (rows, cols)), ("rmax", (rows,))], consts=[("mul_c1", scale)])
+    s3 = _elementwise_stage(
+        "k_sm_norm", "softmax",
+        [load("in0", "x", V("a0"), V("a1"))] + sx +
+        [load("mx", "rmax", V("a0")), assign("d", "subtract", "sxv", "mx"),
+         assign("e", "exp", "d"), load("sm", "rsum", V("a0")), assign("y", "divide", "e", "sm"),
+         write("softmax", (V("a0"), V("a1")), ("y",))],
+        "softmax", rows, cols, [("x", (rows, cols)), ("rmax", (rows,)), ("rsum", (rows,))],
+        consts=[("mul_c1", scale)])
+    return Pipeline(f"softmax3k_{rows}x{cols}", f"softmax({scale} * x, -1)", [s1, s2, s3],
+                    [("x", None)], ["softmax"], rtol=1e-5, atol=1e-6,
+                    oracle={"family": "softmax", "args": {"x": "x"}, "output": "softmax",
+                            "scale": scale})
 
 
 # --------------------------------------------------------------------------
