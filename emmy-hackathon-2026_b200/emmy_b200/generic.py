@@ -29,7 +29,7 @@ import math
 import struct
 from math import prod
 
-from .analysis import kind
+from .analysis import kind, walk
 from .ir import dim
 from .ops import LN2, UnsupportedOp, emit_exp, emit_op_f32, identity_f32
 from .ptx import PARAM_TYPES, Kernel, f32_hex, f64_hex
@@ -109,6 +109,8 @@ class GenericLowering:
                 self.vals[a] = (r, cty)
             else:
                 self.base[a] = k.param_ptr(a)
+        self.tmaps = {}      # TmaDescriptor name -> (param address register, info)
+        self._declare_mbarriers(ctx.tile)
         self.compile_tile(ctx.tile)
         k("ret;")
         if self.dynamic:
@@ -680,7 +682,7 @@ class GenericLowering:
         nb = NBYTES.get(ty, 4)
         size = prod(extents) * nb
         align = max(int(s.align or 0), (4 if nb <= 4 else 2) * nb, 4)
-        info = {"extents": extents, "ty": ty, "nbytes": nb}
+        info = {"extents": extents, "ty": ty, "nbytes": nb, "align": align}
         if self.dynamic:
             off = -(-self.smem_used // align) * align
             self.smem_used = off + size
@@ -819,6 +821,223 @@ class GenericLowering:
         ga = self.gaddr(s.src, self.flat(s.src_index, self.shape_of(s.src)), NBYTES.get(src_ty, 4))
         ins = "cp.async.cg.shared.global" if s.nbytes == 16 else "cp.async.ca.shared.global"
         k(f"{ins} [{sa}], [{ga}], {s.nbytes};")
+
+    # ------------------------------------------------- TMA and mbarriers
+    # The reference defines these nodes without lowering them (TASK.md
+    # "Transport into shared memory", starred).  A TmaDescriptor becomes a
+    # trailing 128-byte tensor-map parameter plus an ``// @emmy tmap`` line
+    # the host harness encodes; TmaLoad is one ``cp.async.bulk.tensor`` by each
+    # thread that reaches it; mbarrier waits are bounded by %globaltimer.
+    TMA_DTYPE = {"u8": 0, "u16": 1, "u32": 2, "i32": 3, "u64": 4, "i64": 5, "f16": 6,
+                 "f32": 7, "f64": 8, "bf16": 9}
+    TMA_SWIZZLE = {None: 0, "NONE": 0, "B32": 1, "B64": 2, "B128": 3}
+    # destination alignment a box copy needs in shared memory, by swizzle
+    TMA_SMEM_ALIGN = {0: 128, 1: 256, 2: 512, 3: 1024}
+    WAIT_NS = 2_000_000_000
+
+    def _declare_mbarriers(self, tile):
+        """mbarriers the IR uses without declaring an Smem array for them get
+        one static 8-byte slot per literal slot index."""
+        declared = {s.name for s in walk(tile.body) if kind(s) == "Smem"}
+        need = {}
+        for s in walk(tile.body):
+            kd = kind(s)
+            if kd in ("MbarrierInit", "MbarrierArriveExpectTx", "MbarrierArrive", "MbarrierWait",
+                      "TmaLoad"):
+                name = s.mbar
+                slot = s.mbar_slot if kd == "TmaLoad" else s.slot
+                if name in declared:
+                    continue
+                v = self._literal_int(slot)
+                if v is None:
+                    raise NotImplementedError(
+                        f"mbarrier {name} indexed by an expression needs an Smem declaration")
+                need[name] = max(need.get(name, 0), v + 1)
+        for name, n in need.items():
+            sym = f"__emmy_mbar_{name}"
+            self.k.decl(f".shared .align 8 .b8 {sym}[{8 * n}];")
+            self.smem[name] = {"extents": (n,), "ty": "u64", "nbytes": 8, "sym": sym,
+                               "static": True}
+
+    @staticmethod
+    def _literal_int(e):
+        if e is None:
+            return 0
+        if isinstance(e, int):
+            return e
+        if kind(e) == "Literal":
+            return int(e.value)
+        return None
+
+    def _slot(self, e) -> str:
+        if e is None:
+            return "0"
+        if isinstance(e, int):
+            return str(e)
+        return self.ival(e)
+
+    def mbar_addr(self, name, slot) -> str:
+        if name not in self.smem:
+            raise NotImplementedError(f"mbarrier {name} is not declared")
+        info = self.smem[name]
+        if info.get("static"):
+            k = self.k
+            base = k.reg("r")
+            k(f"mov.u32 {base}, {info['sym']};")
+            sl = self._slot(slot)
+            if _is_imm(sl):
+                if int(sl):
+                    k(f"add.u32 {base}, {base}, {8 * int(sl)};")
+                return base
+            a = k.reg("r")
+            k(f"mad.lo.s32 {a}, {sl}, 8, {base};")
+            return a
+        return self.saddr(name, self._slot(slot))
+
+    def _status(self):
+        if not getattr(self, "_has_status", False):
+            self.k.decl(".global .align 4 .u32 __emmy_status;")
+            self._has_status = True
+        r = self.k.reg("rd")
+        self.k(f"mov.u64 {r}, __emmy_status;")
+        return r
+
+    def s_TmaDescriptor(self, s):
+        k = self.k
+        ty = getattr(s.dtype, "name", s.dtype) or self.ctx.bufs.dtypes.get(s.src_buf, "f32")
+        if ty not in self.TMA_DTYPE:
+            raise NotImplementedError(f"TMA dtype {ty}")
+        shape = [dim(d) for d in s.src_shape]
+        box = [dim(d) for d in s.box_extents]
+        if len(shape) != len(box) or not 1 <= len(shape) <= 5:
+            raise NotImplementedError("TMA descriptor rank")
+        if s.src_buf not in self.base:
+            raise NotImplementedError(f"TMA source {s.src_buf} is not a kernel argument")
+        if prod(shape) > self.ctx.bufs.size(s.src_buf):
+            raise NotImplementedError(f"TMA shape {shape} exceeds buffer {s.src_buf}")
+        nb = NBYTES[ty]
+        sw = self.TMA_SWIZZLE.get(s.swizzle if s.swizzle is None else str(s.swizzle))
+        if sw is None:
+            raise NotImplementedError(f"TMA swizzle {s.swizzle}")
+        dims = list(reversed(shape))
+        boxr = list(reversed(box))
+        strides, acc = [], nb
+        for d in dims[:-1]:
+            acc *= d
+            strides.append(acc)
+        param = f"tmap_{s.name}"
+        k.params.append((param, ".align 64 .b8", "[128]"))
+        sdir = f" strides={','.join(map(str, strides))}" if strides else ""
+        k.directive(f"tmap {param} buf={s.src_buf} dtype={self.TMA_DTYPE[ty]} "
+                    f"dims={','.join(map(str, dims))}{sdir} box={','.join(map(str, boxr))} "
+                    f"swizzle={sw}")
+        r = k.reg("rd")
+        k(f"mov.u64 {r}, param_{param};")
+        k(f"cvta.param.u64 {r}, {r};")
+        self.tmaps[s.name] = (r, {"ty": ty, "nb": nb, "box": box, "swizzle": sw,
+                                  "bytes": prod(box) * nb})
+
+    def s_TmaLoad(self, s):
+        k = self.k
+        if s.desc not in self.tmaps:
+            raise NotImplementedError(f"TmaLoad of undeclared descriptor {s.desc}")
+        tm, info = self.tmaps[s.desc]
+        coords = [self.ival(c) for c in s.coords]
+        if len(coords) != len(info["box"]):
+            raise NotImplementedError("TmaLoad coordinate count")
+        coords = list(reversed(coords))        # innermost first
+        per16 = 16 // info["nb"] if info["nb"] < 16 else 1
+        sinfo = self.smem[s.smem]
+        align = self.TMA_SMEM_ALIGN[info["swizzle"]]
+        if not self.dynamic and int(sinfo.get("align", 0) or 0) < align:
+            raise NotImplementedError(f"TMA destination {s.smem} must be {align}-byte aligned")
+        dst = self.saddr(s.smem, self.flat(s.smem_index, sinfo["extents"]))
+        mb = self.mbar_addr(s.mbar, s.mbar_slot)
+        skip = k.label("TMA_SKIP")
+        done = k.label("TMA_DONE")
+        # the innermost coordinate times the element size must be a multiple
+        # of 16 bytes, and the destination aligned for the swizzle mode; a copy
+        # that breaks either is not issued (status 9) -- waits on its barrier
+        # then time out instead of the copy faulting
+        if _is_imm(coords[0]):
+            if int(coords[0]) % per16:
+                raise NotImplementedError("TMA innermost coordinate not 16-byte aligned")
+        else:
+            t = k.reg("r")
+            k(f"and.b32 {t}, {coords[0]}, {per16 - 1};")
+            p = k.reg("p")
+            k(f"setp.ne.u32 {p}, {t}, 0;")
+            k(f"@{p} bra {skip};")
+        t2 = k.reg("r")
+        k(f"and.b32 {t2}, {dst}, {align - 1};")
+        p2 = k.reg("p")
+        k(f"setp.ne.u32 {p2}, {t2}, 0;")
+        k(f"@{p2} bra {skip};")
+        cs = []
+        for c in coords:
+            if _is_imm(c):
+                r = k.reg("r")
+                k(f"mov.u32 {r}, {int(c)};")
+                c = r
+            cs.append(c)
+        n = len(cs)
+        k(f"cp.async.bulk.tensor.{n}d.shared::cluster.global.mbarrier::complete_tx::bytes "
+          f"[{dst}], [{tm}, {{{', '.join(cs)}}}], [{mb}];")
+        k(f"bra {done};")
+        k.mark(skip)
+        st = self._status()
+        k(f"st.global.u32 [{st}], 9;")
+        k.mark(done)
+
+    def s_MbarrierInit(self, s):
+        a = self.mbar_addr(s.mbar, s.slot)
+        cnt = self.ival(s.count) if not isinstance(s.count, int) else str(s.count)
+        self.k(f"mbarrier.init.shared::cta.b64 [{a}], {cnt};")
+        self.k("fence.mbarrier_init.release.cluster;")
+
+    def s_MbarrierArriveExpectTx(self, s):
+        a = self.mbar_addr(s.mbar, s.slot)
+        nb = self.ival(s.bytes_) if not isinstance(s.bytes_, int) else str(s.bytes_)
+        self.k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{a}], {nb};")
+
+    def s_MbarrierArrive(self, s):
+        a = self.mbar_addr(s.mbar, s.slot)
+        self.k(f"mbarrier.arrive.shared::cta.b64 _, [{a}];")
+
+    def s_MbarrierWait(self, s):
+        k = self.k
+        a = self.mbar_addr(s.mbar, s.slot)
+        ph = self.ival(s.phase) if not isinstance(s.phase, int) else str(s.phase)
+        par = k.reg("r")
+        if _is_imm(ph):
+            k(f"mov.u32 {par}, {int(ph) & 1};")
+        else:
+            k(f"and.b32 {par}, {ph}, 1;")
+        p = k.reg("p")
+        top, ok = k.label("MBAR_WAIT"), k.label("MBAR_OK")
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{a}], {par};")
+        k(f"@{p} bra {ok};")
+        t0 = k.reg("rd")
+        k(f"mov.u64 {t0}, %globaltimer;")
+        k.mark(top)
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{a}], {par};")
+        k(f"@{p} bra {ok};")
+        t1 = k.reg("rd")
+        k(f"mov.u64 {t1}, %globaltimer;")
+        k(f"sub.s64 {t1}, {t1}, {t0};")
+        q = k.reg("p")
+        k(f"setp.lt.s64 {q}, {t1}, {self.WAIT_NS};")
+        k(f"@{q} bra {top};")
+        st = self._status()
+        k(f"st.global.u32 [{st}], 8;")
+        k.mark(ok)
+
+    def s_SetMaxNReg(self, s):
+        # honoured as the hint it is: register use stays ptxas's choice.  An
+        # .inc is only safe when the launch's registers cover every
+        # warpgroup's share, which this lowering cannot see, and an .inc that
+        # asks for more than was freed waits forever
+        self.k.comment(f"SetMaxNReg {s.direction} {s.count}: hint, not emitted")
 
     def s_CpAsyncCommit(self, s):
         self.k("cp.async.commit_group;")

@@ -751,3 +751,61 @@ def algorithmic_bytes(p: Problem) -> int:
     n += 4 * len(p.consts)
     n += math.prod(p.out[1]) * 4 if p.out[1] else 4
     return n
+
+
+def tma_scale(rows: int = 512, box_rows: int = 32, box_cols: int = 64, boxes: int = 2,
+              block: int = 128, declare_mbar: bool = True) -> Problem:
+    """``y = 2 x + 1`` over x f32[rows, boxes * box_cols], staged through shared
+    memory with the TMA statements the reference defines but does not lower
+    (TmaDescriptor, TmaLoad, MbarrierInit / ArriveExpectTx / Wait, SetMaxNReg):
+    each CTA's thread 0 loads ``boxes`` boxes of box_rows x box_cols, one
+    mbarrier slot each; every thread waits, then reads shared memory."""
+    cols = boxes * box_cols
+    p = Problem(f"tma_scale_{rows}x{cols}", "2 * x + 1", "k_tma_scale", "y")
+    p.add_input("x", (rows, cols))
+    p.out = ("y", (rows, cols), "f32")
+    t0 = eq(V("a1_co"), Lit(0))
+    body = [I.SetMaxNReg(64, "dec"),
+            I.Smem("tile", (boxes, box_rows, box_cols), "float", 1024)]
+    if declare_mbar:
+        body.append(I.Smem("bar", (boxes,), "uint64_t", 8))
+    body += [I.TmaDescriptor("xd", "x", (rows, cols), (box_rows, box_cols), "NONE", F32),
+             I.Cond(t0, tuple(I.MbarrierInit("bar", 1, i) for i in range(boxes)), ()),
+             I.Sync(0, None, False)]
+    issue = []
+    for i in range(boxes):
+        issue += [I.MbarrierArriveExpectTx("bar", box_rows * box_cols * 4, i),
+                  I.TmaLoad("tile", (Lit(i), Lit(0), Lit(0)), "xd",
+                            (mul(V("a0"), Lit(box_rows)), Lit(i * box_cols)), "bar", i)]
+    body.append(I.Cond(t0, tuple(issue), ()))
+    for i in range(boxes):
+        body.append(I.MbarrierWait("bar", 0, i))
+        inner = strided(axis("c", box_cols), V("a1_co"), block, [
+            load("v", "tile", Lit(i), V("r"), V("c")),
+            I.Let("two", Lit(2.0), F32), I.Let("one", Lit(1.0), F32),
+            assign("v2", "multiply", "v", "two"), assign("v3", "add", "v2", "one"),
+            write("y", (add(mul(V("a0"), Lit(box_rows)), V("r")), add(Lit(i * box_cols), V("c"))),
+                  ("v3",))])
+        body.append(I.Loop(axis("r", box_rows), (inner,), False, False))
+    p.body = tile([axis("a0", rows // box_rows), axis("a1_co", block)], body)
+    p.grid, p.block = (rows // box_rows, 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 0, 0
+    return p
+
+
+def mbarrier_timeout(n: int = 1024, block: int = 128) -> Problem:
+    """An mbarrier wait that no arrival completes: the bounded wait gives up
+    after 2 s of %globaltimer, records status 8 in ``__emmy_status`` and the
+    kernel finishes (``y = x``) -- the failure path, with no fault and no hang."""
+    p = Problem(f"mbar_timeout_{n}", "x", "k_mbar_timeout", "y")
+    p.add_input("x", (n,))
+    p.out = ("y", (n,), "f32")
+    p.body = tile([axis("a0", n)], [
+        I.Smem("bar", (1,), "uint64_t", 8),
+        I.Cond(eq(V("a0"), Lit(0)), (I.MbarrierInit("bar", 2, 0),), ()),
+        I.Sync(0, None, False),
+        I.Cond(eq(V("a0"), Lit(0)), (I.MbarrierWait("bar", 0, 0),), ()),
+        load("v", "x", V("a0")), write("y", (V("a0"),), ("v",))])
+    p.grid, p.block = (n // block, 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 0, 0
+    return p
