@@ -36,6 +36,14 @@ int fail(int code, const char *fmt, ...) {
   return code;
 }
 
+}  // namespace
+
+// Not exported: lets the library's other translation units (emmy_noalloc.cu)
+// report failures through emmy_last_error().
+int emmy_internal_fail(int code, const char *msg) { return fail(code, "%s", msg); }
+
+namespace {
+
 // ---------------------------------------------------------------------------
 // driver API table
 // ---------------------------------------------------------------------------

@@ -18,6 +18,7 @@ ROOT = PKG.parent
 REPO = ROOT.parent
 LIB_PATH = PKG / "libemmy_b200.so"
 SRC = ROOT / "csrc" / "emmy_runtime.cpp"
+NOALLOC_SRC = ROOT / "csrc" / "emmy_noalloc.cu"
 HEADER = REPO / "include" / "emmy_b200.h"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
@@ -28,7 +29,7 @@ EXPORTS = [
     "emmy_module_load", "emmy_module_unload", "emmy_kernel_get", "emmy_kernel_attrs",
     "emmy_module_global", "emmy_tensormap_encode", "emmy_launch", "emmy_memset_async",
     "emmy_memcpy_htod_async", "emmy_memcpy_dtoh_async", "emmy_stream_sync", "emmy_mem_alloc",
-    "emmy_mem_free", "emmy_time_launches", "emmy_run_host",
+    "emmy_mem_free", "emmy_time_launches", "emmy_run_host", "emmy_rmsnorm_noalloc",
 ]
 
 
@@ -41,17 +42,29 @@ class EmmyError(RuntimeError):
 def build(force: bool = False, verbose: bool = False) -> Path:
     """Compile the runtime library in-tree (host C++ only; the GPU code is the
     PTX each IR compiles to)."""
-    deps = [SRC, HEADER]
+    deps = [SRC, NOALLOC_SRC, HEADER]
     if LIB_PATH.exists() and not force and all(
             LIB_PATH.stat().st_mtime >= d.stat().st_mtime for d in deps):
         return LIB_PATH
     inc = CUDA_HOME / "include"
     ptxc = CUDA_HOME / "lib64" / "libnvptxcompiler_static.a"
     tmp = LIB_PATH.with_suffix(".so.tmp")
+    # the no-allocation entry point holds its scratch in a __device__ array:
+    # its one .cu file is compiled by nvcc for sm_100a, with the CUDA runtime
+    # linked statically
+    obj = LIB_PATH.with_suffix(".noalloc.o")
+    r = subprocess.run([str(CUDA_HOME / "bin" / "nvcc"), "-c", "-O2", "-std=c++17",
+                        "-gencode", "arch=compute_100a,code=sm_100a",
+                        "-Xcompiler", "-fPIC,-fvisibility=hidden", str(NOALLOC_SRC),
+                        "-o", str(obj)], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"compiling {NOALLOC_SRC.name} failed:\n{r.stderr[-4000:]}")
     cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-Wextra",
            "-fvisibility=hidden", "-Wl,--exclude-libs,ALL", "-s",
-           f"-I{inc}", str(SRC), "-o", str(tmp), str(ptxc), "-ldl", "-lpthread", "-lrt"]
+           f"-I{inc}", str(SRC), str(obj), "-o", str(tmp), str(ptxc),
+           f"-L{CUDA_HOME / 'lib64'}", "-lcudart_static", "-ldl", "-lpthread", "-lrt"]
     r = subprocess.run(cmd, capture_output=True, text=True)
+    obj.unlink(missing_ok=True)
     if r.returncode != 0:
         raise RuntimeError(f"building {LIB_PATH.name} failed:\n{r.stderr[-4000:]}")
     if verbose and r.stderr:
@@ -119,6 +132,9 @@ def lib() -> ctypes.CDLL:
                                     ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_int),
                                     ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
                                     ctypes.c_void_p]
+        L.emmy_rmsnorm_noalloc.argtypes = [ctypes.c_void_p, c_u32p, c_u32p, ctypes.c_void_p,
+                                           c_u32p, c_u32p] + [ctypes.c_uint64] * 5 + [
+                                           ctypes.c_int, ctypes.c_void_p]
         _LIB = L
     return _LIB
 
