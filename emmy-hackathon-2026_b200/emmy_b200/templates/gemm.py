@@ -72,6 +72,9 @@ def idesc_mma(M: int, N: int, b_mn_major: bool, tf32: bool = False) -> int:
 
 class GemmTemplate:
     name = "gemm"
+    # bf16 128x256 tiles whose M-neighbours can pair up run as CTA pairs
+    # (templates/gemm_pair.py); False forces the single-CTA kernel
+    PAIR = True
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -200,10 +203,18 @@ class GemmTemplate:
             raise TemplateMismatch("meta smem_bytes too small for a 2-stage ring")
         self.NB = ext["a1_b"]
         self.hw_trunc = False
+        from .gemm_pair import pair_stages
+        self.pair_S = pair_stages(ctx.smem_bytes, SMEM_LIMIT)
+        self.pair = (cls.PAIR and mode == "bf16" and BM == 128 and BN == 256
+                     and (M // BM) % 2 == 0 and self.pair_S >= 2
+                     and tuple(ctx.grid[1:]) == (1, 1))
         return self
 
     # ------------------------------------------------------------------- emit
     def emit(self) -> str:
+        if self.pair:
+            from .gemm_pair import emit_pair
+            return emit_pair(self)
         ctx = self.ctx
         BM, BN, BK, S, K = self.BM, self.BN, self.BK, self.S, self.K
         es = self.esize

@@ -190,3 +190,25 @@ def test_attention_role_regions_self_contained(kw):
         lines = L[lo:hi] + (L[extra[0]:extra[1]] if extra else [])
         d, u = _defs_uses(lines)
         assert not sorted(u - d - common), (lo, sorted(u - d - common))
+
+
+@pytest.mark.parametrize("kw,pair", [(dict(), True), (dict(M=256, N=256, K=64), True),
+                                     (dict(M=128, N=256, K=64), False),
+                                     (dict(M=256, N=256, K=256, BN=128, U0=8, U1=32), False)])
+def test_gemm_cta_pair_selection_and_assembly(kw, pair, native_lib):
+    """bf16 128x256 tiles with an even number of M tiles become CTA pairs
+    (cluster of 2, cta_group::2); the rest keep the single-CTA kernel.  Both
+    assemble, pass the static checker, and load no TMA with multicast."""
+    from emmy_b200 import native, ptxcheck
+    g, m = synth.matmul(**kw).build()
+    c = compile_graph(g, m)
+    ptx = c.render()
+    assert c.kind == "gemm"
+    assert ("tcgen05.mma.cta_group::2" in ptx) == pair
+    assert (".reqnctapercluster 2, 1, 1" in ptx) == pair
+    assert ("// @emmy cluster 2 1 1" in ptx) == pair
+    assert ptxcheck.check(ptx) == []
+    assert not any("cp.async.bulk" in ln and "multicast" in ln for ln in ptx.splitlines())
+    img = native.Image(ptx)
+    assert img.registers()[c.entry] <= 128
+    assert "spill" not in img.log or "0 bytes spill stores" in img.log
