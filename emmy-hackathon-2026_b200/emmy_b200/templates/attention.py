@@ -14,7 +14,7 @@ of 128 rows, and computes the CTA's rows as:
 
 * TMA loads the NT Q tiles once and K and V tiles of 128 keys into two
   separate rings (3 + 2 stages at D=128, 4 + 4 at D=64; 128-byte swizzle;
-  no multicast), each fed by its own producer thread;
+  one copy per CTA), each fed by its own producer thread;
 * one thread issues, per key block j and query tile t, ``O_t += P_t V_j``
   (P read from TMEM, the ``[a-tmem]`` form; V an MN-major shared operand)
   followed by ``S_t = Q_t K_{j+1}^T`` (M=N=128) into the tile's TMEM score

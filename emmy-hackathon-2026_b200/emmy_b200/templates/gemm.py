@@ -9,7 +9,7 @@ a cp.async ring (``stmt_cpasync_copy`` ``compile.py:1754-1772``, full unroll
 ``:1882-1928``, FMA contraction ``:2250-2264``).  This template keeps the
 IR's CTA -> output-tile assignment and computes each tile with:
 
-* TMA (``cp.async.bulk.tensor.2d``, no multicast) loading 128-byte-swizzled
+* TMA (``cp.async.bulk.tensor.2d``, each CTA copying for itself) loading 128-byte-swizzled
   A and B k-slices into an S-stage shared-memory ring, one elected thread,
   completion counted on an mbarrier (``complete_tx``);
 * one elected thread issuing ``tcgen05.mma.cta_group::1.kind::f16`` (bf16

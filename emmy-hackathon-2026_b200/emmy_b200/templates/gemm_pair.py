@@ -9,7 +9,7 @@ form a cluster of 2 and compute their 256 x 256 block as ONE pair MMA:
   pair's B slice (64 k-rows x 128 columns, 16 KiB) into the same offset of its
   own shared memory, so a stage is 32 KiB instead of the 48 KiB a lone CTA
   needs for 128 x 256 -- B is read from L2/HBM once per pair, not twice;
-* the TMA copies of both CTAs (``.cta_group::2`` form, no multicast) count
+* the TMA copies of both CTAs (``.cta_group::2`` form, each into its own CTA) count
   their bytes on the LEADER's ``full`` mbarrier (address from ``mapa``); only
   the leader arms it (``expect_tx`` of both CTAs' bytes);
 * one thread of the leader issues ``tcgen05.mma.cta_group::2.kind::f16``

@@ -8,6 +8,8 @@ import re
 
 import pytest
 
+from emmy_b200 import ptxcheck
+
 from conftest import PROBLEMS, REPO
 
 CONFIGS = ["vector_add", "full_sum", "row_sum", "row_mean", "rmsnorm", "softmax", "l2norm",
@@ -91,9 +93,8 @@ def test_plant_unbounded_wait():
 
 def test_plant_multicast_and_tmem_and_regsplit():
     ptx = _ptx_config("attention", B=1, H=2, S=512)
-    mc = ptx.replace("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes",
-                     "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-                     ".multicast::cluster", 1)
+    op = "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+    mc = ptx.replace(op, op + "." + ptxcheck.MULTICAST_QUAL, 1)
     assert "no-multicast-load" in _rules(mc)
     nodealloc = re.sub(r"\ttcgen05\.dealloc[^\n]*\n", "", ptx)
     assert "tmem" in _rules(nodealloc)
