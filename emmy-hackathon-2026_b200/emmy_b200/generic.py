@@ -39,6 +39,7 @@ WIDEN = {"f16", "bf16"}
 NBYTES = {"f32": 4, "f64": 8, "f16": 2, "bf16": 2, "i32": 4, "i64": 8, "u32": 4, "u64": 8,
           "u8": 1, "i8": 1, "u16": 2, "i16": 2, "bool": 1}
 REG = {"f32": "f", "f64": "fd", "i32": "r", "u32": "r", "i64": "rd", "u64": "rd", "bool": "r"}
+MOVTY = {"f": "f32", "fd": "f64", "r": "b32", "rd": "b64", "h": "b16"}
 PTY = {"f32": "f32", "f64": "f64", "i32": "s32", "u32": "u32", "i64": "s64", "u64": "u64",
        "bool": "u32"}
 LDTY = {"f32": "f32", "f64": "f64", "i32": "s32", "u32": "u32", "i64": "s64", "u64": "u64",
@@ -166,6 +167,7 @@ class GenericLowering:
         k(f"shr.u32 {warp}, {tid}, 5;")
         self.ints["lane"] = lane
         self.ints["warp"] = warp
+        self.builtin_warp = warp
         aux = int(getattr(tile, "aux_threads", 0) or 0)
         if aux:
             bt = int(tile.block_threads)
@@ -530,7 +532,15 @@ class GenericLowering:
             k(f"mov.{cty} {r}, {lit};")
             self.vals[s.name] = (r, cty)
         elif t == "Var" and s.value.name in self.vals:
-            self.vals[s.name] = self.vals[s.value.name]
+            # an SSA binding: a copy, so that an in-place update of the source
+            # (an Accum of it, later or in a later loop iteration) leaves this
+            # name's value alone; ptxas drops the copy where nothing updates it
+            src, cty = self.vals[s.value.name]
+            if isinstance(src, str) and src.startswith("%"):
+                r = k.reg(REG[cty])
+                k(f"mov.{MOVTY[REG[cty]]} {r}, {src};")
+                src = r
+            self.vals[s.name] = (src, cty)
         elif t == "FlatIndex":
             self.ints[s.name] = self.ival(s.value)
         else:
@@ -739,6 +749,11 @@ class GenericLowering:
             root = self.ival(I_Var(iv))
         base = self._iadd(self._imul(tid, scale), root)
         bid = int(s.barrier_id or 0)
+        # a tree indexed by the warp (the reference's form, compile.py:1814-1857)
+        # runs every step in all 32 lanes of a warp on the same entries: the
+        # lanes' loads must all complete before any store (independent thread
+        # scheduling lets one lane run ahead) and one lane stores
+        warp_tree = s.inner is None and tid == getattr(self, "builtin_warp", None)
         # the tree reads entries [0, length) (times ``scale``, plus the inner
         # root < scale): a tree longer than its buffer would read shared
         # memory outside it, so such an IR is refused rather than lowered
@@ -776,10 +791,19 @@ class GenericLowering:
                 self.vals[st] = (a, ty)
                 self.vals[sb] = (b, ty)
             self.body(s.combine_states)
+            lead = ""
+            if warp_tree:
+                am = k.reg("r")
+                k(f"activemask.b32 {am};")
+                k(f"bar.warp.sync {am};")
+                pl = k.reg("p")
+                k(f"setp.eq.u32 {pl}, {self.ints['lane']}, 0;")
+                lead = f"@{pl} "
             for buf, st in zip(s.bufs, s.state):
                 ty = _calc_ty(self.smem[buf]["ty"])
                 v = self.convert(*self.vals[st], ty)
-                k(f"st.shared.{ty if ty in ('f32', 'f64') else PTY[ty]} [{self.saddr(buf, base)}], {v};")
+                k(f"{lead}st.shared.{ty if ty in ('f32', 'f64') else PTY[ty]} "
+                  f"[{self.saddr(buf, base)}], {v};")
             k.mark(skip)
             if bid and s.barrier_count is not None:
                 k(f"bar.sync {bid}, {s.barrier_count};")
