@@ -728,7 +728,7 @@ def config(name: str, **kw) -> Problem:
         "rmsnorm": rmsnorm,
         "softmax": softmax,
         "l2norm": l2norm,
-        "matmul_bf16": lambda **k: matmul(dtype="bf16", **k),
+        "matmul_bf16": lambda **k: matmul(**{"dtype": "bf16", "stages": 4, **k}),
         "matmul_f32": lambda **k: matmul(**{"dtype": "f32", "BK": 32, "stages": 4, **k}),
         "attention": attention,
         "attention_d64": lambda **k: attention(**{"D": 64, **k}),

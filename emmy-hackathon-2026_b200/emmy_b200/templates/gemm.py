@@ -75,6 +75,9 @@ class GemmTemplate:
     # bf16 128x256 tiles whose M-neighbours can pair up run as CTA pairs
     # (templates/gemm_pair.py); False forces the single-CTA kernel
     PAIR = True
+    # pair kernels whose ring fits 4+ stages (one CTA per SM) run persistent
+    # with a double-buffered accumulator (templates/gemm_persistent.py)
+    PERSISTENT = True
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -213,6 +216,9 @@ class GemmTemplate:
     # ------------------------------------------------------------------- emit
     def emit(self) -> str:
         if self.pair:
+            from .gemm_persistent import PERSISTENT_MIN_STAGES, emit_pair_persistent
+            if type(self).PERSISTENT and self.pair_S >= PERSISTENT_MIN_STAGES:
+                return emit_pair_persistent(self)
             from .gemm_pair import emit_pair
             return emit_pair(self)
         ctx = self.ctx
@@ -536,20 +542,21 @@ class GemmTemplate:
         return d
 
     @staticmethod
-    def _wait(k, bar, parity, status, code, fail_label):
+    def _wait(k, bar, parity, status, code, fail_label, sem=""):
         """Spin on ``mbarrier.try_wait.parity`` for at most WAIT_NS of
         %globaltimer; on expiry store ``code`` to ``__emmy_status`` and jump
-        to ``fail_label``.  The first try runs before the clock is read: a
+        to ``fail_label``.  ``sem`` (e.g. ``.acquire.cluster``) widens the
+        wait's acquire to the cluster for arrivals from the peer CTA.  The first try runs before the clock is read: a
         %globaltimer read costs hundreds of cycles, which would otherwise sit
         on the path of every wait that succeeds at once."""
         p = k.reg("p")
         top, ok = k.label("WAIT"), k.label("WAIT_OK")
-        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar}], {parity};")
+        k(f"mbarrier.try_wait.parity{sem}.shared::cta.b64 {p}, [{bar}], {parity};")
         k(f"@{p} bra {ok};")
         t0 = k.reg("rd")
         k(f"mov.u64 {t0}, %globaltimer;")
         k.mark(top)
-        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar}], {parity};")
+        k(f"mbarrier.try_wait.parity{sem}.shared::cta.b64 {p}, [{bar}], {parity};")
         k(f"@{p} bra {ok};")
         t1 = k.reg("rd")
         k(f"mov.u64 {t1}, %globaltimer;")

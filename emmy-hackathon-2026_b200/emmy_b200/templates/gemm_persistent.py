@@ -1,0 +1,355 @@
+"""bf16 matmul on persistent CTA pairs with a double-buffered accumulator.
+
+The IR launches one CTA per 128 x 256 output tile; when its shared-memory
+budget allows a deep ring (at least 4 pair stages, so one CTA per SM), the
+first ``WORKERS`` clusters of 2 CTAs (one per SM pair of the B200's 148 SMs)
+do all the work and every other cluster returns at once (measured: 3,948
+such CTAs cost about 6 us in total).  Cluster c computes the 256 x 256 pair
+tiles ``c, c + WORKERS, c + 2*WORKERS, ...`` (tile t: rows ``256*(t / NB)``,
+columns ``256*(t % NB)``), exactly the CTA-pair scheme of ``gemm_pair``
+(leader-issued ``tcgen05.mma.cta_group::2``, each CTA loading its A rows and
+half of B, both CTAs' copies completing on the leader's ``full`` barrier),
+with three changes:
+
+* the shared-memory ring runs continuously across tiles: the producer
+  starts the next tile's k-slices while the MMA thread finishes the current
+  one;
+* tensor memory holds two 256-column accumulators (all 512 columns): tile i
+  accumulates into buffer ``i % 2``;
+* warps 4-7 of both CTAs are the epilogue: they wait for the tile's ``acc``
+  barrier, drain their 32 rows x 256 columns (``tcgen05.ld.32x32b.x32``,
+  32-byte stores), then arrive on the leader's ``acc_empty`` barrier for that
+  buffer (8 arrivals: 4 warps x 2 CTAs, the follower's through ``mapa``),
+  which the MMA thread waits on before reusing the buffer -- so each CTA's
+  epilogue overlaps its own next main loop.
+
+Warp 0 lane 0 is the producer, warp 1 allocates tensor memory and its lane
+0 in the leader issues the MMAs; warps 2-3 only join the teardown.  Every
+mbarrier wait is bounded by ``%globaltimer`` (codes 1 producer, 2 MMA issuer,
+3 epilogue, 6 accumulator reuse); a role whose wait expires leaves its loop.
+"""
+from __future__ import annotations
+
+from ..ptx import Kernel
+from .gemm import GemmTemplate, _desc_hi, idesc_mma
+
+WORKERS = 74                 # clusters of 2 CTAs: the 148 SMs of a B200
+PERSISTENT_MIN_STAGES = 4    # 4 x 32 KiB ring: one CTA per SM
+EPI_CHUNK = 16               # accumulator columns per tcgen05.ld in the epilogue
+
+
+def emit_pair_persistent(t) -> str:
+    ctx = t.ctx
+    BM, BN, BK, S, K = 128, 256, 64, t.pair_S, t.K
+    KT = K // BK
+    SA = BM * BK * 2
+    SBH = BK * 128 * 2
+    STG = SA + SBH
+    BOXN = 64
+    NB = t.NB                                  # 256-column tiles per row band
+    TILES = (t.M // 256) * NB                  # pair tiles
+    W = min(WORKERS, TILES)
+    params = ctx.params() + [("tmapA", ".align 64 .b8", "[128]"),
+                             ("tmapB", ".align 64 .b8", "[128]")]
+    k = Kernel(ctx.entry, params)
+    k.maxntid = (256, 1, 1)
+    k.maxnreg = 128              # one CTA per SM: room for the 32-register drains
+    k.reqnctapercluster = (2, 1, 1)
+    k.directive("cluster 2 1 1")
+    k.decl(".extern .shared .align 1024 .b8 __emmy_smem[];")
+    k.decl(".global .align 4 .u32 __emmy_status;")
+    k.directive(f"tmap tmapA buf={t.A} dtype=9 dims={K},{t.M} strides={K * 2} "
+                f"box={BK},{BM} swizzle=3")
+    k.directive(f"tmap tmapB buf={t.B} dtype=9 dims={t.N},{K} strides={t.N * 2} "
+                f"box={BOXN},{BK} swizzle=3")
+    k.comment(f"emmy-b200 template: tcgen05 gemm bf16 M={t.M} N={t.N} K={K}, persistent CTA "
+              f"pairs ({W} workers, {TILES} pair tiles), stages={S}, 2 accumulators")
+    cta = k.special("%ctaid.x")
+    clus = k.reg("r")
+    k(f"shr.u32 {clus}, {cta}, 1;")
+    pidle = k.reg("p")
+    k(f"setp.ge.u32 {pidle}, {clus}, {W};")
+    idle = k.label("IDLE")
+    k(f"@{pidle} bra {idle};")
+    cbase = k.param_ptr(t.C)
+    ta = k.reg("rd")
+    k(f"mov.u64 {ta}, param_tmapA;")
+    k(f"cvta.param.u64 {ta}, {ta};")
+    tb = k.reg("rd")
+    k(f"mov.u64 {tb}, param_tmapB;")
+    k(f"cvta.param.u64 {tb}, {tb};")
+    tid = k.special("%tid.x")
+    warp = k.reg("r")
+    k(f"shr.u32 {warp}, {tid}, 5;")
+    lane = k.reg("r")
+    k(f"and.b32 {lane}, {tid}, 31;")
+    rank = k.special("%cluster_ctarank")
+    plead = k.reg("p")
+    k(f"setp.eq.u32 {plead}, {rank}, 0;")
+    # this cluster's tile count: ceil((TILES - clus) / W)
+    ntile = k.reg("r")
+    k(f"sub.u32 {ntile}, {TILES + W - 1}, {clus};")
+    k(f"div.u32 {ntile}, {ntile}, {W};")
+    # shared memory: S stages of [A 16K | B half 16K], then the mbarriers
+    # full[S], empty[S], acc[2], acc_empty[2] and the tensor-memory slot
+    raw = k.reg("r")
+    k(f"mov.u32 {raw}, __emmy_smem;")
+    ring = k.reg("r")
+    k(f"add.u32 {ring}, {raw}, 1023;")
+    k(f"and.b32 {ring}, {ring}, -1024;")
+    bars = k.reg("r")
+    k(f"add.u32 {bars}, {ring}, {S * STG};")
+    accb = k.reg("r")                          # acc[2]
+    k(f"add.u32 {accb}, {bars}, {16 * S};")
+    acce = k.reg("r")                          # acc_empty[2] (used in the leader)
+    k(f"add.u32 {acce}, {accb}, 16;")
+    tslot = k.reg("r")
+    k(f"add.u32 {tslot}, {accb}, 32;")
+    status = k.reg("rd")
+    k(f"mov.u64 {status}, __emmy_status;")
+    p0 = k.reg("p")
+    k(f"setp.eq.u32 {p0}, {tid}, 0;")
+    skip_init = k.label("SKIP_INIT")
+    k(f"@!{p0} bra {skip_init};")
+    for s in range(2 * S):
+        k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 1;")
+    for b in range(2):
+        k(f"mbarrier.init.shared::cta.b64 [{accb}+{8 * b}], 1;")
+        k(f"mbarrier.init.shared::cta.b64 [{acce}+{8 * b}], 8;")
+    k("fence.mbarrier_init.release.cluster;")
+    k(f"prefetch.tensormap [{ta}];")
+    k(f"prefetch.tensormap [{tb}];")
+    k.mark(skip_init)
+    pw1 = k.reg("p")
+    k(f"setp.eq.u32 {pw1}, {warp}, 1;")
+    skip_alloc = k.label("SKIP_ALLOC")
+    k(f"@!{pw1} bra {skip_alloc};")
+    k(f"tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [{tslot}], 512;")
+    k("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;")
+    k.mark(skip_alloc)
+    k("tcgen05.fence::before_thread_sync;")
+    k("bar.sync 0;")
+    k("barrier.cluster.arrive.release.aligned;")
+    k("barrier.cluster.wait.acquire.aligned;")
+    k("tcgen05.fence::after_thread_sync;")
+    tmem = k.reg("r")
+    k(f"ld.shared.u32 {tmem}, [{tslot}];")
+    teardown = k.label("TEARDOWN")
+    pl0 = k.reg("p")
+    k(f"setp.eq.u32 {pl0}, {lane}, 0;")
+    it, kt, st, ph = k.reg("r"), k.reg("r"), k.reg("r"), k.reg("r")
+
+    def bar_addr(group, stage_reg):
+        r = k.reg("r")
+        k(f"mad.lo.u32 {r}, {stage_reg}, 8, {bars};")
+        if group:
+            k(f"add.u32 {r}, {r}, {8 * S * group};")
+        return r
+
+    def stage_base(stage_reg):
+        r = k.reg("r")
+        k(f"mad.lo.u32 {r}, {stage_reg}, {STG}, {ring};")
+        return r
+
+    def tile_coords():
+        """(m0 of this CTA, n0 of the pair tile, this CTA's B columns) for
+        tile iteration ``it``."""
+        tt = k.reg("r")
+        k(f"mad.lo.u32 {tt}, {it}, {W}, {clus};")
+        mp = k.reg("r")
+        k(f"div.u32 {mp}, {tt}, {NB};")
+        nbk = k.reg("r")
+        k(f"rem.u32 {nbk}, {tt}, {NB};")
+        m0 = k.reg("r")
+        k(f"mad.lo.u32 {m0}, {mp}, 2, {rank};")
+        k(f"mul.lo.u32 {m0}, {m0}, {BM};")
+        n0 = k.reg("r")
+        k(f"mul.lo.u32 {n0}, {nbk}, {BN};")
+        nh = k.reg("r")
+        k(f"mad.lo.u32 {nh}, {rank}, 128, {n0};")
+        return m0, n0, nh
+
+    def tile_loop_head(label):
+        k(f"mov.u32 {it}, 0;")
+        top = k.label(label)
+        k.mark(top)
+        return top
+
+    def tile_loop_tail(top):
+        k(f"add.u32 {it}, {it}, 1;")
+        pl = k.reg("p")
+        k(f"setp.lt.u32 {pl}, {it}, {ntile};")
+        k(f"@{pl} bra {top};")
+
+    def k_loop_tail(top):
+        GemmTemplate._advance(k, st, ph, S)
+        k(f"add.u32 {kt}, {kt}, 1;")
+        pl = k.reg("p")
+        k(f"setp.lt.u32 {pl}, {kt}, {KT};")
+        k(f"@{pl} bra {top};")
+
+    # ---------------- producer: warp 0, lane 0 of both CTAs ----------------
+    pprod = k.reg("p")
+    k(f"setp.eq.u32 {pprod}, {warp}, 0;")
+    k(f"and.pred {pprod}, {pprod}, {pl0};")
+    end_prod = k.label("END_PROD")
+    k(f"@!{pprod} bra {end_prod};")
+    lead_full = k.reg("r")
+    k(f"mapa.shared::cluster.u32 {lead_full}, {bars}, 0;")
+    k(f"mov.u32 {st}, 0;")
+    k(f"mov.u32 {ph}, 0;")
+    ptop = tile_loop_head("PTILE")
+    m0, n0, nh = tile_coords()
+    k(f"mov.u32 {kt}, 0;")
+    pk = k.label("PK")
+    k.mark(pk)
+    par = k.reg("r")
+    k(f"xor.b32 {par}, {ph}, 1;")
+    GemmTemplate._wait(k, bar_addr(1, st), par, status, 1, end_prod)
+    fb = k.reg("r")
+    k(f"mad.lo.u32 {fb}, {st}, 8, {lead_full};")
+    own_fb = bar_addr(0, st)
+    k(f"@{plead} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{own_fb}], {2 * STG};")
+    kc = k.reg("r")
+    k(f"mul.lo.u32 {kc}, {kt}, {BK};")
+    da = stage_base(st)
+    k(f"cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      f"[{da}], [{ta}, {{{kc}, {m0}}}], [{fb}];")
+    for i in range(2):
+        nx = k.reg("r")
+        k(f"add.u32 {nx}, {nh}, {BOXN * i};")
+        db = k.reg("r")
+        k(f"add.u32 {db}, {da}, {SA + i * BK * 128};")
+        k(f"cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx"
+          f"::bytes [{db}], [{tb}, {{{nx}, {kc}}}], [{fb}];")
+    k_loop_tail(pk)
+    tile_loop_tail(ptop)
+    k.mark(end_prod)
+
+    # ---------------- MMA issuer: warp 1, lane 0 of the leader ----------------
+    pmma = k.reg("p")
+    k(f"setp.eq.u32 {pmma}, {warp}, 1;")
+    k(f"and.pred {pmma}, {pmma}, {pl0};")
+    k(f"and.pred {pmma}, {pmma}, {plead};")
+    end_mma = k.label("END_MMA")
+    k(f"@!{pmma} bra {end_mma};")
+    mask = k.reg("h")
+    k(f"mov.b16 {mask}, 3;")
+    idesc = k.reg("r")
+    k(f"mov.u32 {idesc}, {idesc_mma(2 * BM, BN, True)};")
+    hiA = _desc_hi(16, 1024)
+    hiB = _desc_hi(BK * 128, 1024)
+    k(f"mov.u32 {st}, 0;")
+    k(f"mov.u32 {ph}, 0;")
+    mtop = tile_loop_head("MTILE")
+    buf = k.reg("r")
+    k(f"and.b32 {buf}, {it}, 1;")
+    aph = k.reg("r")                              # use count of this buffer, parity
+    k(f"shr.u32 {aph}, {it}, 1;")
+    k(f"and.b32 {aph}, {aph}, 1;")
+    k(f"xor.b32 {aph}, {aph}, 1;")
+    ae = k.reg("r")
+    k(f"mad.lo.u32 {ae}, {buf}, 8, {acce};")
+    GemmTemplate._wait(k, ae, aph, status, 6, end_mma, sem=".acquire.cluster")
+    k("tcgen05.fence::after_thread_sync;")
+    dacc = k.reg("r")
+    k(f"mad.lo.u32 {dacc}, {buf}, {BN}, {tmem};")
+    k(f"mov.u32 {kt}, 0;")
+    mk = k.label("MK")
+    k.mark(mk)
+    GemmTemplate._wait(k, bar_addr(0, st), ph, status, 2, end_mma)
+    k("tcgen05.fence::after_thread_sync;")
+    sb = stage_base(st)
+    bad = k.reg("r")
+    k(f"add.u32 {bad}, {sb}, {SA};")
+    adesc = GemmTemplate._desc(k, sb, hiA)
+    bdesc = GemmTemplate._desc(k, bad, hiB)
+    pacc = k.reg("p")
+    k(f"setp.ne.u32 {pacc}, {kt}, 0;")
+    ptrue = k.reg("p")
+    k(f"setp.eq.u32 {ptrue}, 0, 0;")
+    for kk in range(BK // 16):
+        ad = k.reg("rd")
+        k(f"add.s64 {ad}, {adesc}, {kk * 2};")
+        bd = k.reg("rd")
+        k(f"add.s64 {bd}, {bdesc}, {kk * 16 * 8};")
+        k(f"tcgen05.mma.cta_group::2.kind::f16 [{dacc}], {ad}, {bd}, {idesc}, "
+          f"{pacc if kk == 0 else ptrue};")
+    k(f"tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      f"[{bar_addr(1, st)}], {mask};")
+    k_loop_tail(mk)
+    af = k.reg("r")
+    k(f"mad.lo.u32 {af}, {buf}, 8, {accb};")
+    k(f"tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      f"[{af}], {mask};")
+    tile_loop_tail(mtop)
+    k.mark(end_mma)
+
+    # ---------------- epilogue: warps 4-7 of each CTA ----------------
+    k("bar.warp.sync 0xffffffff;")
+    pepi = k.reg("p")
+    k(f"setp.ge.u32 {pepi}, {warp}, 4;")
+    k(f"@!{pepi} bra {teardown};")
+    q = k.reg("r")
+    k(f"and.b32 {q}, {warp}, 3;")
+    lead_ae = k.reg("r")                          # acc_empty[0] of the leader
+    k(f"mapa.shared::cluster.u32 {lead_ae}, {acce}, 0;")
+    tl = k.reg("r")
+    k(f"shl.b32 {tl}, {q}, 21;")                  # (32*q) << 16: TMEM lane field
+    k(f"add.u32 {tl}, {tl}, {tmem};")
+    etop = tile_loop_head("ETILE")
+    m0e, n0e, _ = tile_coords()
+    ebuf = k.reg("r")
+    k(f"and.b32 {ebuf}, {it}, 1;")
+    eph = k.reg("r")
+    k(f"shr.u32 {eph}, {it}, 1;")
+    k(f"and.b32 {eph}, {eph}, 1;")
+    eaf = k.reg("r")
+    k(f"mad.lo.u32 {eaf}, {ebuf}, 8, {accb};")
+    GemmTemplate._wait(k, eaf, eph, status, 3, teardown)
+    k("tcgen05.fence::after_thread_sync;")
+    row = k.reg("r")
+    k(f"mad.lo.u32 {row}, {q}, 32, {lane};")
+    k(f"add.u32 {row}, {row}, {m0e};")
+    off = k.reg("rd")
+    k(f"mul.wide.u32 {off}, {row}, {t.N * 4};")
+    c2 = k.reg("rd")
+    k(f"mul.wide.u32 {c2}, {n0e}, 4;")
+    k(f"add.s64 {off}, {off}, {c2};")
+    cptr = k.reg("rd")
+    k(f"add.s64 {cptr}, {cbase}, {off};")
+    taddr = k.reg("r")
+    k(f"mad.lo.u32 {taddr}, {ebuf}, {BN}, {tl};")
+    CH = EPI_CHUNK
+    for c in range(BN // CH):
+        regs = k.regs("r", CH)
+        ta2 = k.reg("r")
+        k(f"add.u32 {ta2}, {taddr}, {CH * c};")
+        k(f"tcgen05.ld.sync.aligned.32x32b.x{CH}.b32 {{{', '.join(regs)}}}, [{ta2}];")
+        k("tcgen05.wait::ld.sync.aligned;")
+        for v in range(CH // 8):
+            k(f"st.global.v8.b32 [{cptr}+{4 * CH * c + 32 * v}], "
+              f"{{{', '.join(regs[8 * v:8 * v + 8])}}};")
+    # this warp's reads of the buffer are complete: release it to the MMA
+    k("tcgen05.fence::before_thread_sync;")
+    k("bar.warp.sync 0xffffffff;")
+    eae = k.reg("r")
+    k(f"mad.lo.u32 {eae}, {ebuf}, 8, {lead_ae};")
+    k(f"@{pl0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{eae}];")
+    tile_loop_tail(etop)
+
+    # ---------------- teardown ----------------
+    k.mark(teardown)
+    k("tcgen05.fence::before_thread_sync;")
+    k("barrier.sync 0;")
+    k("barrier.cluster.arrive.release;")
+    k("barrier.cluster.wait.acquire;")
+    end = k.label("END")
+    k(f"@!{pw1} bra {end};")
+    k("bar.warp.sync 0xffffffff;")
+    k("tcgen05.fence::after_thread_sync;")
+    k(f"tcgen05.dealloc.cta_group::2.sync.aligned.b32 {tmem}, 512;")
+    k.mark(end)
+    k.mark(idle)
+    k("ret;")
+    return k.render()

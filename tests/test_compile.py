@@ -192,6 +192,24 @@ def test_attention_role_regions_self_contained(kw):
         assert not sorted(u - d - common), (lo, sorted(u - d - common))
 
 
+def test_gemm_persistent_selection(native_lib):
+    """A 4-stage IR ring (one CTA per SM) selects the persistent pair kernel:
+    512 tensor-memory columns, idle clusters beyond the 74 workers, clean
+    static checks; 2- and 3-stage rings keep the per-tile pair kernel."""
+    from emmy_b200 import native, ptxcheck, racecheck
+    for stages, persistent in ((4, True), (3, True), (2, False)):
+        g, m = synth.matmul(M=1024, N=1024, K=512, stages=stages).build()
+        c = compile_graph(g, m)
+        ptx = c.render()
+        assert ("persistent CTA pairs" in ptx) == persistent, stages
+        assert ptxcheck.check(ptx) == [] and racecheck.check(ptx)[0] == []
+        img = native.Image(ptx)
+        assert "spill" not in img.log or "0 bytes spill stores" in img.log
+        if persistent:
+            assert "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32" in ptx
+            assert ", 512;" in ptx and "mbarrier.arrive.release.cluster.shared::cluster" in ptx
+
+
 @pytest.mark.parametrize("kw,pair", [(dict(), True), (dict(M=256, N=256, K=64), True),
                                      (dict(M=128, N=256, K=64), False),
                                      (dict(M=256, N=256, K=256, BN=128, U0=8, U1=32), False)])

@@ -53,8 +53,17 @@ def test_gemm_small(kw):
 
 
 def test_gemm_baseline_rows():
+    """BASELINE shape, 2-stage IR ring: the per-tile CTA-pair kernel."""
     p = synth.matmul()
     rows = np.sort(np.random.default_rng(3).choice(16384, 48, replace=False))
+    _run(p, rows=rows)
+
+
+def test_gemm_baseline_rows_persistent():
+    """BASELINE shape as benchmarked (4-stage IR ring): the persistent
+    CTA-pair kernel, 28 tiles per worker cluster."""
+    p = synth.config("matmul_bf16")
+    rows = np.sort(np.random.default_rng(11).choice(16384, 48, replace=False))
     _run(p, rows=rows)
 
 
@@ -92,4 +101,28 @@ def test_gemm_pair_and_single(kw, pair, monkeypatch):
     g, m = synth.matmul(**kw).build()
     assert ("cta_group::2" in compiler.compile_graph(g, m).render()) == pair
     got, ref = _run(synth.matmul(**kw))
+    assert np.max(np.abs(got - ref)) <= 1e-3 * max(1.0, float(np.max(np.abs(ref))))
+
+
+PERSISTENT_CASES = [dict(M=256, N=256, K=64), dict(M=1024, N=768, K=512),
+                    dict(M=512, N=512, K=1024), dict(M=4096, N=2048, K=512),
+                    dict(M=8192, N=4096, K=256)]
+
+
+@pytest.mark.parametrize("kw", PERSISTENT_CASES,
+                         ids=[f"{c['M']}x{c['N']}x{c['K']}" for c in PERSISTENT_CASES])
+def test_gemm_persistent_pairs(kw):
+    """IR rings of 4 stages (198 KiB: one CTA per SM) run the persistent
+    pair kernel: 74 worker clusters, two tensor-memory accumulators, the
+    epilogue of tile i overlapping the main loop of tile i+1.  The large
+    shapes give each worker up to 7 tiles (both accumulators reused several
+    times) and are checked on sampled rows."""
+    from emmy_b200 import compiler
+    p = synth.matmul(stages=4, **kw)
+    g, m = p.build()
+    assert "persistent CTA pairs" in compiler.compile_graph(g, m).render()
+    rows = None
+    if kw["M"] >= 4096:
+        rows = np.sort(np.random.default_rng(7).choice(kw["M"], 64, replace=False))
+    got, ref = _run(p, rows=rows)
     assert np.max(np.abs(got - ref)) <= 1e-3 * max(1.0, float(np.max(np.abs(ref))))
