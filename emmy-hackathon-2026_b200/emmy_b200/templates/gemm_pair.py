@@ -22,7 +22,8 @@ form a cluster of 2 and compute their 256 x 256 block as ONE pair MMA:
   ``acc`` barriers; each CTA then drains its own tensor memory exactly like
   the single-CTA template (``tcgen05.ld.32x32b.x32``, ``st.global.v8``).
 
-Cluster barriers (``barrier.cluster``) order the mbarrier initialisation and
+Pair p (CTAs 2p and 2p+1) takes pair tile p in the grouped order of
+``gemm_persistent.raster``.  Cluster barriers (``barrier.cluster``) order the mbarrier initialisation and
 tensor-memory allocation before any cross-CTA traffic, and keep each CTA
 alive until its peer is done with it.  Every mbarrier wait is bounded by
 ``%globaltimer`` as in the single-CTA template (codes 1 producer, 2 MMA
@@ -81,10 +82,8 @@ def emit_pair(t) -> str:
     cta = k.special("%ctaid.x")
     pair = k.reg("r")
     k(f"shr.u32 {pair}, {cta}, 1;")
-    mp = k.reg("r")
-    k(f"div.u32 {mp}, {pair}, {t.NB};")
-    nbk = k.reg("r")
-    k(f"rem.u32 {nbk}, {pair}, {t.NB};")
+    from .gemm_persistent import raster
+    mp, nbk = raster(k, pair, t.M // 256, t.NB)
     m0 = k.reg("r")                              # (2 * mp + rank) * 128
     k(f"mad.lo.u32 {m0}, {mp}, 2, {rank};")
     k(f"mul.lo.u32 {m0}, {m0}, {BM};")
