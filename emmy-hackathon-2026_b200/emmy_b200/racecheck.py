@@ -59,35 +59,43 @@ UNIFORM_SPECIAL = ("%ctaid", "%nctaid", "%ntid", "%cluster", "%nclusterid", "%cl
 
 
 class Aff:
-    """w*warp + l*lane + c + sum(coef * symbol); symbols are uniform."""
-    __slots__ = ("w", "l", "c", "u")
+    """A per-thread integer value: ``arr[t] + sum(coef * symbol)``, the
+    symbols uniform (the same in every thread)."""
+    __slots__ = ("arr", "u")
 
-    def __init__(self, w=0, l=0, c=0, u=()):
-        self.w, self.l, self.c = w, l, c
+    def __init__(self, arr, u=()):
+        self.arr = arr
         self.u = tuple(sorted((s, k) for s, k in dict(u).items() if k))
 
     def __add__(self, o):
         u = dict(self.u)
         for s, k in o.u:
             u[s] = u.get(s, 0) + k
-        return Aff(self.w + o.w, self.l + o.l, self.c + o.c, u)
+        return Aff(self.arr + o.arr, u)
 
     def scale(self, k):
-        return Aff(self.w * k, self.l * k, self.c * k, {s: v * k for s, v in self.u})
+        return Aff(self.arr * k, {s: v * k for s, v in self.u})
 
     def neg(self):
         return self.scale(-1)
 
     @property
     def uniform(self):
-        return self.w == 0 and self.l == 0
+        return bool((self.arr == self.arr[0]).all())
 
     @property
     def const(self):
-        return self.uniform and not self.u
+        return not self.u and self.uniform
+
+    @property
+    def c(self):
+        return int(self.arr[0])
+
+    def divisible(self, d):
+        return all(k % d == 0 for _, k in self.u)
 
     def offsets(self, t):
-        return self.w * (t >> 5) + self.l * (t & 31) + self.c
+        return self.arr[t]
 
 
 def _imm(tok):
@@ -150,25 +158,28 @@ class _Kernel:
         return var
 
     # -------------------------------------------------------------- values
+    def C(self, v=0, u=()):
+        return Aff(np.full(self.n, v, dtype=np.int64), u)
+
     def aff(self, tok):
         tok = tok.strip()
         if IMM.match(tok):
-            return Aff(c=_imm(tok))
+            return self.C(_imm(tok))
         if tok.startswith("%tid.x"):
-            return Aff(w=32, l=1)
+            return Aff(self.t.copy())
         if tok.startswith(("%tid.y", "%tid.z")):
-            return Aff() if self.tid_yz_zero else None
+            return self.C() if self.tid_yz_zero else None
         if tok.startswith("%laneid"):
-            return Aff(l=1)
+            return Aff(self.t & 31)
         if tok.startswith(UNIFORM_SPECIAL):
-            return Aff(u={tok: 1})
+            return self.C(0, {tok: 1})
         if tok.startswith("%"):
             if tok not in self.memo:
                 self.memo[tok] = None            # cycle guard
                 self.memo[tok] = self._reg_aff(tok)
             return self.memo[tok]
         if re.match(r"^[A-Za-z_$][\w$]*$", tok):
-            return Aff(u={"&" + tok: 1})        # a variable's address
+            return self.C(0, {"&" + tok: 1})    # a variable's address
         return None
 
     def _reg_aff(self, r):
@@ -189,10 +200,10 @@ class _Kernel:
                     if init is not None:
                         key = f"iter({r})"
                         if step.const:
-                            return init + Aff(u={key: step.c})
-                        return init + Aff(u={f"{key}*{ops[2]}": 1})
+                            return init + self.C(0, {key: step.c})
+                        return init + self.C(0, {f"{key}*{ops[2]}": 1})
         if r not in self.varying:
-            return Aff(u={r: 1})
+            return self.C(0, {r: 1})
         return None
 
     def _eval(self, r, text):
@@ -200,53 +211,52 @@ class _Kernel:
         ops = _operands(rest)
         base = op.split(".")[0]
         src = ops[1:]
-        if pred is not None:
-            return Aff(u={r: 1}) if r not in self.varying else None
+        fallback = self.C(0, {r: 1}) if r not in self.varying else None
+        if pred is not None or ".f" in op[len(base):] or ".hi" in op:
+            return fallback
+        vals = [self.aff(x) for x in src]
+        if any(v is None for v in vals):
+            return fallback
         try:
-            if base == "mov" and len(src) == 1:
-                return self.aff(src[0])
-            if base == "cvta" or (base == "cvt" and ".rn" not in op and ".f" not in op[3:]):
-                return self.aff(src[0])
-            if base in ("add", "sub") and len(src) == 2 and ".f" not in op:
-                a, b = self.aff(src[0]), self.aff(src[1])
-                if a is not None and b is not None:
-                    return a + (b if base == "add" else b.neg())
-            if base == "mul" and len(src) == 2 and ".f" not in op and ".hi" not in op:
-                a, b = self.aff(src[0]), self.aff(src[1])
-                if a is not None and b is not None:
-                    if b.const:
-                        return a.scale(b.c)
-                    if a.const:
-                        return b.scale(a.c)
-            if base == "mad" and len(src) == 3 and ".hi" not in op:
-                a, b, c = (self.aff(x) for x in src)
-                if a is not None and b is not None and c is not None:
-                    if b.const:
-                        return a.scale(b.c) + c
-                    if a.const:
-                        return b.scale(a.c) + c
-            if base == "shl" and len(src) == 2:
-                a, b = self.aff(src[0]), self.aff(src[1])
-                if a is not None and b is not None and b.const:
-                    return a.scale(1 << b.c)
-            if base == "shr" and len(src) == 2:
-                a, b = self.aff(src[0]), self.aff(src[1])
-                if a is not None and b is not None and b.const:
-                    s = b.c
-                    if (a.w, a.l, a.c, a.u) == (32, 1, 0, ()) and s == 5:
-                        return Aff(w=1)
-                    d = 1 << s
-                    if a.l == 0 and a.w % d == 0 and a.c % d == 0 and all(k % d == 0 for _, k in a.u) \
-                            and not a.u:
-                        return Aff(w=a.w // d, c=a.c // d)
-            if base == "and" and len(src) == 2:
-                a, b = self.aff(src[0]), self.aff(src[1])
-                if a is not None and b is not None and b.const and b.c == 31 and \
-                        (a.w, a.l, a.c, a.u) in ((32, 1, 0, ()), (0, 1, 0, ())):
-                    return Aff(l=1)
-        except (ValueError, IndexError):
-            return None
-        return Aff(u={r: 1}) if r not in self.varying else None
+            if base in ("mov", "cvta", "cvt") and len(vals) == 1:
+                return vals[0]
+            if base in ("add", "sub") and len(vals) == 2:
+                a, b = vals
+                return a + (b if base == "add" else b.neg())
+            if base in ("mul", "mad") and len(vals) in (2, 3):
+                a, b = vals[:2]
+                if b.const:
+                    prod = a.scale(b.c)
+                elif a.const:
+                    prod = b.scale(a.c)
+                elif not a.u and not b.u:
+                    prod = Aff(a.arr * b.arr)
+                else:
+                    return fallback
+                return prod + vals[2] if base == "mad" else prod
+            if base == "shl" and len(vals) == 2 and vals[1].const:
+                return vals[0].scale(1 << vals[1].c)
+            if base in ("shr", "div", "rem") and len(vals) == 2 and vals[1].const:
+                a = vals[0]
+                d = (1 << vals[1].c) if base == "shr" else vals[1].c
+                if d <= 0 or not a.divisible(d) or (a.arr < 0).any():
+                    return fallback
+                if base == "rem":
+                    return Aff(a.arr % d)
+                return Aff(a.arr // d, {s: k // d for s, k in a.u})
+            if base == "and" and len(vals) == 2 and vals[1].const:
+                a, m = vals[0], vals[1].c
+                if not a.u or (m >= 0 and (m + 1) & m == 0 and a.divisible(m + 1)):
+                    return Aff(a.arr & m)
+            if base in ("or", "xor", "and", "min", "max") and len(vals) == 2 and \
+                    not vals[0].u and not vals[1].u:
+                a, b = vals[0].arr, vals[1].arr
+                f = {"or": np.bitwise_or, "xor": np.bitwise_xor, "and": np.bitwise_and,
+                     "min": np.minimum, "max": np.maximum}[base]
+                return Aff(f(a, b))
+        except (ValueError, IndexError, OverflowError):
+            return fallback
+        return fallback
 
     # ---------------------------------------------------------- predicates
     def pmask(self, p):
@@ -269,7 +279,7 @@ class _Kernel:
             d = a + b.neg()
             if d.u:
                 return None
-            v = d.offsets(self.t)
+            v = d.arr
             return {"eq": v == 0, "ne": v != 0, "lt": v < 0, "le": v <= 0, "gt": v > 0,
                     "ge": v >= 0, "lo": v < 0, "ls": v <= 0, "hi": v > 0, "hs": v >= 0}.get(cmp)
         if op.startswith(("and.pred", "or.pred", "xor.pred")) and len(ops) == 3:
@@ -398,7 +408,7 @@ def check(ptx: str, threads: int | None = None):
             a = k.aff(m.group(1)) if m else None
             if a is not None and m.group(2):
                 try:
-                    a = a + Aff(c=_imm(m.group(2)))
+                    a = a + k.C(_imm(m.group(2)))
                 except ValueError:
                     a = None
             mask, exact = k.active(IN[bi], (pred, not neg) if pred else None)

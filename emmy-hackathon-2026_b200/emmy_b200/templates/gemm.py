@@ -206,18 +206,22 @@ class GemmTemplate:
             raise TemplateMismatch("meta smem_bytes too small for a 2-stage ring")
         self.NB = ext["a1_b"]
         self.hw_trunc = False
-        from .gemm_pair import pair_stages
-        self.pair_S = pair_stages(ctx.smem_bytes, SMEM_LIMIT)
-        self.pair = (cls.PAIR and mode == "bf16" and BM == 128 and BN == 256
+        from .gemm_pair import PAIR_STAGE, pair_stages
+        # 3xTF32 pairs keep each CTA's raw slice and its low parts: 64 KiB
+        self.pair_S = pair_stages(ctx.smem_bytes, SMEM_LIMIT,
+                                  PAIR_STAGE * (2 if mode == "tf32x3" else 1))
+        self.pair = (cls.PAIR and BM == 128 and BN == 256
                      and (M // BM) % 2 == 0 and self.pair_S >= 2
                      and tuple(ctx.grid[1:]) == (1, 1))
         return self
 
     # ------------------------------------------------------------------- emit
     def emit(self) -> str:
-        if self.pair:
+        if self.pair and (self.mode == "bf16" or type(self).PERSISTENT):
             from .gemm_persistent import PERSISTENT_MIN_STAGES, emit_pair_persistent
-            if type(self).PERSISTENT and self.pair_S >= PERSISTENT_MIN_STAGES:
+            # 3xTF32 pair stages are 64 KiB: two already mean one CTA per SM
+            if type(self).PERSISTENT and (self.pair_S >= PERSISTENT_MIN_STAGES
+                                          or self.mode == "tf32x3"):
                 return emit_pair_persistent(self)
             from .gemm_pair import emit_pair
             return emit_pair(self)

@@ -38,10 +38,11 @@ PAIR_STAGE_MAX = 6
 PAIR_STAGE = 128 * 64 * 2 + 64 * 128 * 2      # A slice + B half, bf16: 32 KiB
 
 
-def pair_stages(smem_bytes: int, limit: int) -> int:
+def pair_stages(smem_bytes: int, limit: int, stage: int = PAIR_STAGE) -> int:
     """Ring depth the meta's dynamic shared memory allows (1 KiB alignment
-    slack and 256 B of barriers are set aside)."""
-    return min(PAIR_STAGE_MAX, (min(smem_bytes, limit) - 1024 - 256) // PAIR_STAGE)
+    slack and 256 B of barriers are set aside); ``stage`` is one CTA's bytes
+    per stage (3xTF32: 64 KiB, raw slices plus their low parts)."""
+    return min(PAIR_STAGE_MAX, (min(smem_bytes, limit) - 1024 - 256) // stage)
 
 
 def emit_pair(t) -> str:

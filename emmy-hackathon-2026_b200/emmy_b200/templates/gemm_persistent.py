@@ -71,31 +71,41 @@ def raster(k, tt, MB, NB, group=None):
 
 
 def emit_pair_persistent(t) -> str:
+    """bf16 (``kind::f16``) or fp32 through 3xTF32 (``kind::tf32``, the
+    operands split into tf32 hi/lo parts in shared memory by warps 4-7)."""
     ctx = t.ctx
-    BM, BN, BK, S, K = 128, 256, 64, t.pair_S, t.K
+    tf32 = t.mode == "tf32x3"
+    es = 4 if tf32 else 2
+    BM, BN, K = 128, 256, t.K
+    BK = 128 // es                   # one 128-byte swizzle row of K per stage
+    S = t.pair_S
     KT = K // BK
-    SA = BM * BK * 2
-    SBH = BK * 128 * 2
-    STG = SA + SBH
-    BOXN = 64
-    NB = t.NB                                  # 256-column tiles per row band
-    MB = t.M // 256                            # 256-row bands
-    TILES = MB * NB                            # pair tiles
+    SA = BM * BK * es                # own A rows: 16 KiB
+    SBH = BK * 128 * es              # own half of B: BK k-rows x 128 columns
+    RAW = SA + SBH
+    STG = 2 * RAW if tf32 else RAW   # 3xTF32 keeps the low parts after the raw slice
+    BOXN = 128 // es                 # B boxes are 128 bytes wide
+    KMMA = 32 // es                  # K per tcgen05.mma
+    NB = t.NB                        # 256-column tiles per row band
+    MB = t.M // 256                  # 256-row bands
+    TILES = MB * NB                  # pair tiles
     W = min(WORKERS, TILES)
     params = ctx.params() + [("tmapA", ".align 64 .b8", "[128]"),
                              ("tmapB", ".align 64 .b8", "[128]")]
     k = Kernel(ctx.entry, params)
     k.maxntid = (256, 1, 1)
-    k.maxnreg = 128              # one CTA per SM: room for the 32-register drains
+    k.maxnreg = 128                  # one CTA per SM: registers are plentiful
     k.reqnctapercluster = (2, 1, 1)
     k.directive("cluster 2 1 1")
     k.decl(".extern .shared .align 1024 .b8 __emmy_smem[];")
     k.decl(".global .align 4 .u32 __emmy_status;")
-    k.directive(f"tmap tmapA buf={t.A} dtype=9 dims={K},{t.M} strides={K * 2} "
+    tm = 7 if tf32 else 9            # CU_TENSOR_MAP_DATA_TYPE_FLOAT32 / BFLOAT16
+    k.directive(f"tmap tmapA buf={t.A} dtype={tm} dims={K},{t.M} strides={K * es} "
                 f"box={BK},{BM} swizzle=3")
-    k.directive(f"tmap tmapB buf={t.B} dtype=9 dims={t.N},{K} strides={t.N * 2} "
-                f"box={BOXN},{BK} swizzle=3")
-    k.comment(f"emmy-b200 template: tcgen05 gemm bf16 M={t.M} N={t.N} K={K}, persistent CTA "
+    # MN-major 32-bit operands: the 128-byte swizzle with 32-byte atoms
+    k.directive(f"tmap tmapB buf={t.B} dtype={tm} dims={t.N},{K} strides={t.N * es} "
+                f"box={BOXN},{BK} swizzle={4 if tf32 else 3}")
+    k.comment(f"emmy-b200 template: tcgen05 gemm {t.mode} M={t.M} N={t.N} K={K}, persistent CTA "
               f"pairs ({W} workers, {TILES} pair tiles), stages={S}, 2 accumulators")
     cta = k.special("%ctaid.x")
     clus = k.reg("r")
@@ -123,8 +133,10 @@ def emit_pair_persistent(t) -> str:
     ntile = k.reg("r")
     k(f"sub.u32 {ntile}, {TILES + W - 1}, {clus};")
     k(f"div.u32 {ntile}, {ntile}, {W};")
-    # shared memory: S stages of [A 16K | B half 16K], then the mbarriers
-    # full[S], empty[S], acc[2], acc_empty[2] and the tensor-memory slot
+    # shared memory: S stages, then the mbarriers full[S], empty[S],
+    # conv[S] (3xTF32, used in the leader), acc[2], acc_empty[2] (leader),
+    # and the tensor-memory slot
+    NBAR = 3 * S if tf32 else 2 * S
     raw = k.reg("r")
     k(f"mov.u32 {raw}, __emmy_smem;")
     ring = k.reg("r")
@@ -133,8 +145,8 @@ def emit_pair_persistent(t) -> str:
     bars = k.reg("r")
     k(f"add.u32 {bars}, {ring}, {S * STG};")
     accb = k.reg("r")                          # acc[2]
-    k(f"add.u32 {accb}, {bars}, {16 * S};")
-    acce = k.reg("r")                          # acc_empty[2] (used in the leader)
+    k(f"add.u32 {accb}, {bars}, {8 * NBAR};")
+    acce = k.reg("r")                          # acc_empty[2]
     k(f"add.u32 {acce}, {accb}, 16;")
     tslot = k.reg("r")
     k(f"add.u32 {tslot}, {accb}, 32;")
@@ -146,6 +158,8 @@ def emit_pair_persistent(t) -> str:
     k(f"@!{p0} bra {skip_init};")
     for s in range(2 * S):
         k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 1;")
+    for s in range(2 * S, NBAR):               # conv[s]: 4 warps x 2 CTAs
+        k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 8;")
     for b in range(2):
         k(f"mbarrier.init.shared::cta.b64 [{accb}+{8 * b}], 1;")
         k(f"mbarrier.init.shared::cta.b64 [{acce}+{8 * b}], 8;")
@@ -184,11 +198,11 @@ def emit_pair_persistent(t) -> str:
         k(f"mad.lo.u32 {r}, {stage_reg}, {STG}, {ring};")
         return r
 
-    def tile_coords():
+    def tile_coords(idx):
         """(m0 of this CTA, n0 of the pair tile, this CTA's B columns) for
-        tile iteration ``it``."""
+        this cluster's tile iteration ``idx``."""
         tt = k.reg("r")
-        k(f"mad.lo.u32 {tt}, {it}, {W}, {clus};")
+        k(f"mad.lo.u32 {tt}, {idx}, {W}, {clus};")
         mp, nbk = raster(k, tt, MB, NB)
         m0 = k.reg("r")
         k(f"mad.lo.u32 {m0}, {mp}, 2, {rank};")
@@ -205,10 +219,10 @@ def emit_pair_persistent(t) -> str:
         k.mark(top)
         return top
 
-    def tile_loop_tail(top):
+    def tile_loop_tail(top, count=ntile):
         k(f"add.u32 {it}, {it}, 1;")
         pl = k.reg("p")
-        k(f"setp.lt.u32 {pl}, {it}, {ntile};")
+        k(f"setp.lt.u32 {pl}, {it}, {count};")
         k(f"@{pl} bra {top};")
 
     def k_loop_tail(top):
@@ -219,39 +233,48 @@ def emit_pair_persistent(t) -> str:
         k(f"@{pl} bra {top};")
 
     # ---------------- producer: warp 0, lane 0 of both CTAs ----------------
+    # bf16: both CTAs' copies complete on the leader's full barrier, which
+    # the leader arms with both CTAs' bytes; 3xTF32: each CTA's converters
+    # need to see their own slice land, so copies complete locally
     pprod = k.reg("p")
     k(f"setp.eq.u32 {pprod}, {warp}, 0;")
     k(f"and.pred {pprod}, {pprod}, {pl0};")
     end_prod = k.label("END_PROD")
     k(f"@!{pprod} bra {end_prod};")
-    lead_full = k.reg("r")
-    k(f"mapa.shared::cluster.u32 {lead_full}, {bars}, 0;")
+    if not tf32:
+        lead_full = k.reg("r")
+        k(f"mapa.shared::cluster.u32 {lead_full}, {bars}, 0;")
     k(f"mov.u32 {st}, 0;")
     k(f"mov.u32 {ph}, 0;")
     ptop = tile_loop_head("PTILE")
-    m0, n0, nh = tile_coords()
+    m0, n0, nh = tile_coords(it)
     k(f"mov.u32 {kt}, 0;")
     pk = k.label("PK")
     k.mark(pk)
     par = k.reg("r")
     k(f"xor.b32 {par}, {ph}, 1;")
     GemmTemplate._wait(k, bar_addr(1, st), par, status, 1, end_prod)
-    fb = k.reg("r")
-    k(f"mad.lo.u32 {fb}, {st}, 8, {lead_full};")
     own_fb = bar_addr(0, st)
-    k(f"@{plead} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{own_fb}], {2 * STG};")
+    if tf32:
+        fb = own_fb
+        k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{own_fb}], {RAW};")
+        copy = ("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes")
+    else:
+        fb = k.reg("r")
+        k(f"mad.lo.u32 {fb}, {st}, 8, {lead_full};")
+        k(f"@{plead} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{own_fb}], {2 * RAW};")
+        copy = ("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::"
+                "complete_tx::bytes")
     kc = k.reg("r")
     k(f"mul.lo.u32 {kc}, {kt}, {BK};")
     da = stage_base(st)
-    k(f"cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
-      f"[{da}], [{ta}, {{{kc}, {m0}}}], [{fb}];")
-    for i in range(2):
+    k(f"{copy} [{da}], [{ta}, {{{kc}, {m0}}}], [{fb}];")
+    for i in range(128 // BOXN):
         nx = k.reg("r")
         k(f"add.u32 {nx}, {nh}, {BOXN * i};")
         db = k.reg("r")
         k(f"add.u32 {db}, {da}, {SA + i * BK * 128};")
-        k(f"cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx"
-          f"::bytes [{db}], [{tb}, {{{nx}, {kc}}}], [{fb}];")
+        k(f"{copy} [{db}], [{tb}, {{{nx}, {kc}}}], [{fb}];")
     k_loop_tail(pk)
     tile_loop_tail(ptop)
     k.mark(end_prod)
@@ -266,9 +289,9 @@ def emit_pair_persistent(t) -> str:
     mask = k.reg("h")
     k(f"mov.b16 {mask}, 3;")
     idesc = k.reg("r")
-    k(f"mov.u32 {idesc}, {idesc_mma(2 * BM, BN, True)};")
+    k(f"mov.u32 {idesc}, {idesc_mma(2 * BM, BN, True, tf32)};")
     hiA = _desc_hi(16, 1024)
-    hiB = _desc_hi(BK * 128, 1024)
+    hiB = _desc_hi(BK * 128, 512, 1) if tf32 else _desc_hi(BK * 128, 1024)
     k(f"mov.u32 {st}, 0;")
     k(f"mov.u32 {ph}, 0;")
     mtop = tile_loop_head("MTILE")
@@ -287,24 +310,42 @@ def emit_pair_persistent(t) -> str:
     k(f"mov.u32 {kt}, 0;")
     mk = k.label("MK")
     k.mark(mk)
-    GemmTemplate._wait(k, bar_addr(0, st), ph, status, 2, end_mma)
+    if tf32:       # both CTAs' converters have split this stage
+        GemmTemplate._wait(k, bar_addr(2, st), ph, status, 2, end_mma, sem=".acquire.cluster")
+    else:
+        GemmTemplate._wait(k, bar_addr(0, st), ph, status, 2, end_mma)
     k("tcgen05.fence::after_thread_sync;")
     sb = stage_base(st)
     bad = k.reg("r")
     k(f"add.u32 {bad}, {sb}, {SA};")
     adesc = GemmTemplate._desc(k, sb, hiA)
     bdesc = GemmTemplate._desc(k, bad, hiB)
+    if tf32:
+        lad = k.reg("r")
+        k(f"add.u32 {lad}, {sb}, {RAW};")
+        lbd = k.reg("r")
+        k(f"add.u32 {lbd}, {sb}, {RAW + SA};")
+        ldesc_a = GemmTemplate._desc(k, lad, hiA)
+        ldesc_b = GemmTemplate._desc(k, lbd, hiB)
     pacc = k.reg("p")
     k(f"setp.ne.u32 {pacc}, {kt}, 0;")
     ptrue = k.reg("p")
     k(f"setp.eq.u32 {ptrue}, 0, 0;")
-    for kk in range(BK // 16):
-        ad = k.reg("rd")
-        k(f"add.s64 {ad}, {adesc}, {kk * 2};")
-        bd = k.reg("rd")
-        k(f"add.s64 {bd}, {bdesc}, {kk * 16 * 8};")
-        k(f"tcgen05.mma.cta_group::2.kind::f16 [{dacc}], {ad}, {bd}, {idesc}, "
-          f"{pacc if kk == 0 else ptrue};")
+    kind_ = "tf32" if tf32 else "f16"
+    first = True
+    for kk in range(BK // KMMA):
+        ao, bo = kk * 2, kk * KMMA * 8    # +32 B along K (A); +KMMA rows of 128 B (B)
+        pairs = [(adesc, bdesc)]
+        if tf32:                          # small terms first: lo*hi + hi*lo, then hi*hi
+            pairs = [(ldesc_a, bdesc), (adesc, ldesc_b), (adesc, bdesc)]
+        for da_, db_ in pairs:
+            ad = k.reg("rd")
+            k(f"add.s64 {ad}, {da_}, {ao};")
+            bd = k.reg("rd")
+            k(f"add.s64 {bd}, {db_}, {bo};")
+            k(f"tcgen05.mma.cta_group::2.kind::{kind_} [{dacc}], {ad}, {bd}, {idesc}, "
+              f"{pacc if first else ptrue};")
+            first = False
     k(f"tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
       f"[{bar_addr(1, st)}], {mask};")
     k_loop_tail(mk)
@@ -315,7 +356,7 @@ def emit_pair_persistent(t) -> str:
     tile_loop_tail(mtop)
     k.mark(end_mma)
 
-    # ---------------- epilogue: warps 4-7 of each CTA ----------------
+    # ------- warps 4-7 of each CTA: (3xTF32: converters, then) epilogue -------
     k("bar.warp.sync 0xffffffff;")
     pepi = k.reg("p")
     k(f"setp.ge.u32 {pepi}, {warp}, 4;")
@@ -327,46 +368,107 @@ def emit_pair_persistent(t) -> str:
     tl = k.reg("r")
     k(f"shl.b32 {tl}, {q}, 21;")                  # (32*q) << 16: TMEM lane field
     k(f"add.u32 {tl}, {tl}, {tmem};")
-    etop = tile_loop_head("ETILE")
-    m0e, n0e, _ = tile_coords()
-    ebuf = k.reg("r")
-    k(f"and.b32 {ebuf}, {it}, 1;")
-    eph = k.reg("r")
-    k(f"shr.u32 {eph}, {it}, 1;")
-    k(f"and.b32 {eph}, {eph}, 1;")
-    eaf = k.reg("r")
-    k(f"mad.lo.u32 {eaf}, {ebuf}, 8, {accb};")
-    GemmTemplate._wait(k, eaf, eph, status, 3, teardown)
-    k("tcgen05.fence::after_thread_sync;")
-    row = k.reg("r")
-    k(f"mad.lo.u32 {row}, {q}, 32, {lane};")
-    k(f"add.u32 {row}, {row}, {m0e};")
-    off = k.reg("rd")
-    k(f"mul.wide.u32 {off}, {row}, {t.N * 4};")
-    c2 = k.reg("rd")
-    k(f"mul.wide.u32 {c2}, {n0e}, 4;")
-    k(f"add.s64 {off}, {off}, {c2};")
-    cptr = k.reg("rd")
-    k(f"add.s64 {cptr}, {cbase}, {off};")
-    taddr = k.reg("r")
-    k(f"mad.lo.u32 {taddr}, {ebuf}, {BN}, {tl};")
-    CH = EPI_CHUNK
-    for c in range(BN // CH):
-        regs = k.regs("r", CH)
-        ta2 = k.reg("r")
-        k(f"add.u32 {ta2}, {taddr}, {CH * c};")
-        k(f"tcgen05.ld.sync.aligned.32x32b.x{CH}.b32 {{{', '.join(regs)}}}, [{ta2}];")
-        k("tcgen05.wait::ld.sync.aligned;")
-        for v in range(CH // 8):
-            k(f"st.global.v8.b32 [{cptr}+{4 * CH * c + 32 * v}], "
-              f"{{{', '.join(regs[8 * v:8 * v + 8])}}};")
-    # this warp's reads of the buffer are complete: release it to the MMA
-    k("tcgen05.fence::before_thread_sync;")
-    k("bar.warp.sync 0xffffffff;")
-    eae = k.reg("r")
-    k(f"mad.lo.u32 {eae}, {ebuf}, 8, {lead_ae};")
-    k(f"@{pl0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{eae}];")
-    tile_loop_tail(etop)
+
+    def epilogue(idx):
+        ebuf = k.reg("r")
+        k(f"and.b32 {ebuf}, {idx}, 1;")
+        eph = k.reg("r")
+        k(f"shr.u32 {eph}, {idx}, 1;")
+        k(f"and.b32 {eph}, {eph}, 1;")
+        eaf = k.reg("r")
+        k(f"mad.lo.u32 {eaf}, {ebuf}, 8, {accb};")
+        GemmTemplate._wait(k, eaf, eph, status, 3, teardown)
+        k("tcgen05.fence::after_thread_sync;")
+        m0e, n0e, _ = tile_coords(idx)
+        row = k.reg("r")
+        k(f"mad.lo.u32 {row}, {q}, 32, {lane};")
+        k(f"add.u32 {row}, {row}, {m0e};")
+        off = k.reg("rd")
+        k(f"mul.wide.u32 {off}, {row}, {t.N * 4};")
+        c2 = k.reg("rd")
+        k(f"mul.wide.u32 {c2}, {n0e}, 4;")
+        k(f"add.s64 {off}, {off}, {c2};")
+        cptr = k.reg("rd")
+        k(f"add.s64 {cptr}, {cbase}, {off};")
+        taddr = k.reg("r")
+        k(f"mad.lo.u32 {taddr}, {ebuf}, {BN}, {tl};")
+        CH = EPI_CHUNK
+        for c in range(BN // CH):
+            regs = k.regs("r", CH)
+            ta2 = k.reg("r")
+            k(f"add.u32 {ta2}, {taddr}, {CH * c};")
+            k(f"tcgen05.ld.sync.aligned.32x32b.x{CH}.b32 {{{', '.join(regs)}}}, [{ta2}];")
+            k("tcgen05.wait::ld.sync.aligned;")
+            for v in range(CH // 8):
+                k(f"st.global.v8.b32 [{cptr}+{4 * CH * c + 32 * v}], "
+                  f"{{{', '.join(regs[8 * v:8 * v + 8])}}};")
+        # this warp's reads of the buffer are complete: release it to the MMA
+        k("tcgen05.fence::before_thread_sync;")
+        k("bar.warp.sync 0xffffffff;")
+        eae = k.reg("r")
+        k(f"mad.lo.u32 {eae}, {ebuf}, 8, {lead_ae};")
+        k(f"@{pl0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{eae}];")
+
+    if not tf32:
+        etop = tile_loop_head("ETILE")
+        epilogue(it)
+        tile_loop_tail(etop)
+    else:
+        # iteration i converts tile i's k-slices (i < ntile), then drains tile
+        # i-1 (i >= 1): the drain overlaps the MMAs of tile i's last stages
+        lead_conv = k.reg("r")                    # conv[0] of the leader
+        k(f"add.u32 {lead_conv}, {bars}, {16 * S};")
+        k(f"mapa.shared::cluster.u32 {lead_conv}, {lead_conv}, 0;")
+        ct = k.reg("r")
+        k(f"and.b32 {ct}, {tid}, 127;")           # converter thread 0..127
+        off0 = k.reg("r")
+        k(f"shl.b32 {off0}, {ct}, 4;")            # 16 bytes per thread per pass
+        ntp1 = k.reg("r")
+        k(f"add.u32 {ntp1}, {ntile}, 1;")
+        k(f"mov.u32 {st}, 0;")
+        k(f"mov.u32 {ph}, 0;")
+        ctop = tile_loop_head("CTILE")
+        pconv = k.reg("p")
+        k(f"setp.lt.u32 {pconv}, {it}, {ntile};")
+        skip_conv = k.label("SKIP_CONV")
+        k(f"@!{pconv} bra {skip_conv};")
+        k(f"mov.u32 {kt}, 0;")
+        ck = k.label("CK")
+        k.mark(ck)
+        GemmTemplate._wait(k, bar_addr(0, st), ph, status, 4, teardown)
+        sbc = stage_base(st)
+        a0 = k.reg("r")
+        k(f"add.u32 {a0}, {sbc}, {off0};")
+        for i in range(RAW // (16 * 128)):
+            x = k.regs("r", 4)
+            ad = f"{a0}+{i * 2048}" if i else a0
+            k(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{ad}];")
+            hi = k.regs("r", 4)
+            lo = k.regs("r", 4)
+            for j in range(4):
+                k(f"cvt.rna.tf32.f32 {hi[j]}, {x[j]};")
+                d = k.reg("f")
+                k(f"sub.rn.f32 {d}, {x[j]}, {hi[j]};")
+                k(f"cvt.rna.tf32.f32 {lo[j]}, {d};")
+            k(f"st.shared.v4.b32 [{ad}], {{{', '.join(hi)}}};")
+            k(f"st.shared.v4.b32 [{a0}+{RAW + i * 2048}], {{{', '.join(lo)}}};")
+        # generic-proxy stores -> the tensor core's async-proxy reads
+        k("fence.proxy.async.shared::cta;")
+        k("bar.warp.sync 0xffffffff;")
+        cv = k.reg("r")
+        k(f"mad.lo.u32 {cv}, {st}, 8, {lead_conv};")
+        k(f"@{pl0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{cv}];")
+        k_loop_tail(ck)
+        k.mark(skip_conv)
+        pdrain = k.reg("p")
+        k(f"setp.ne.u32 {pdrain}, {it}, 0;")
+        skip_drain = k.label("SKIP_DRAIN")
+        k(f"@!{pdrain} bra {skip_drain};")
+        prev = k.reg("r")
+        k(f"sub.u32 {prev}, {it}, 1;")
+        epilogue(prev)
+        k.mark(skip_drain)
+        tile_loop_tail(ctop, ntp1)
 
     # ---------------- teardown ----------------
     k.mark(teardown)

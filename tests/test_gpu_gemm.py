@@ -126,3 +126,27 @@ def test_gemm_persistent_pairs(kw):
         rows = np.sort(np.random.default_rng(7).choice(kw["M"], 64, replace=False))
     got, ref = _run(p, rows=rows)
     assert np.max(np.abs(got - ref)) <= 1e-3 * max(1.0, float(np.max(np.abs(ref))))
+
+
+F32_PERSISTENT_CASES = [dict(M=256, N=256, K=128), dict(M=1024, N=768, K=256),
+                        dict(M=4096, N=2048, K=256), dict(M=8192, N=4096, K=128)]
+
+
+@pytest.mark.parametrize("kw", F32_PERSISTENT_CASES,
+                         ids=[f"{c['M']}x{c['N']}x{c['K']}" for c in F32_PERSISTENT_CASES])
+def test_gemm_f32_persistent_pairs(kw):
+    """fp32 operands on persistent CTA pairs: each CTA's warps 4-7 split its
+    own landed slice into tf32 hi/lo parts and arrive on the leader's
+    conversion barrier; the leader issues lo*hi, hi*lo, hi*hi as
+    ``kind::tf32`` pair MMAs; the same warps drain the previous tile's
+    accumulator.  Rel 2e-5 of max|C| (BASELINE asks 1e-4); large shapes on
+    sampled rows."""
+    from emmy_b200 import compiler
+    p = synth.config("matmul_f32", **kw)
+    g, m = p.build()
+    assert "persistent CTA pairs" in compiler.compile_graph(g, m).render()
+    rows = None
+    if kw["M"] >= 4096:
+        rows = np.sort(np.random.default_rng(9).choice(kw["M"], 64, replace=False))
+    got, ref = _run(p, rows=rows)
+    assert np.max(np.abs(got - ref)) <= 2e-5 * max(1.0, float(np.max(np.abs(ref))))
