@@ -8,15 +8,17 @@ and a write/any pair of two different threads in one region that can hit the
 same address is a race.  This checker keeps that model and makes it exact
 enough for this build's kernels:
 
-* thread coordinates are (warp, lane), tid = 32*warp + lane, so the
-  ``tid >> 5`` / ``tid & 31`` decompositions every template uses stay affine;
-* registers that do not depend on the thread (kernel parameters, block
-  indices, loop counters with uniform steps, values loaded from uniform
-  addresses) are kept as symbolic terms: two addresses are compared only when
-  their symbolic parts are identical, so ``ring + stage*STG + 16*tid`` in two
-  places compares exactly;
+* a value is its concrete number in every thread of the launch plus a sum
+  of symbolic terms: registers that do not depend on the thread (kernel
+  parameters, block indices, loop counters with uniform steps, values loaded
+  from uniform addresses) are symbols, so any integer arithmetic on the
+  thread index (``tid >> 5``, ``tid & 127``, div/rem, xor swizzles) stays
+  exact, and a symbol passes through a shift, div, rem or mask only where it
+  provably divides out; two addresses are compared only when their symbolic
+  parts are identical, so ``ring + stage*STG + 16*tid`` in two places
+  compares exactly;
 * an induction register ``v = init; v += step`` (step uniform) is
-  ``init + step * iter(v)``, so cooperative strided loops stay affine;
+  ``init + step * iter(v)``, so cooperative strided loops stay exact;
 * which threads can execute an access follows from predicates that compare
   thread-affine values with constants (``tid == 0``, ``lane == 0``,
   ``warp < 4``, ...), on the instruction itself and on every branch that
@@ -29,9 +31,10 @@ enough for this build's kernels:
   treated as CTA-wide, as the reference does); ``bar.warp.sync`` orders the
   accesses of one warp.
 
-Reported as ``unresolved`` (never as races): pairs whose addresses depend on
-the thread in a non-affine way, whose symbolic parts differ, or whose guards
-could not be evaluated.  Not modelled: asynchronous-proxy traffic (TMA,
+Reported as ``unresolved`` (never as races): accesses whose address mixes
+the thread index with a symbol in a way that does not divide out, or whose
+guards could not be evaluated; pairs whose symbolic parts differ are not
+compared.  Not modelled: asynchronous-proxy traffic (TMA,
 ``cp.async.bulk``, ``tcgen05``), which the kernels order with mbarriers, and
 pairs from different iterations of a barrier-free loop.
 
