@@ -39,6 +39,7 @@ from __future__ import annotations
 
 from ..analysis import NotAffine, affine, cond_var_eq, flat_index, kind
 from ..ir import dim
+from ..ops import emit_op_f32
 from ..ptx import Kernel, f32_hex
 from .common import (Chain, TemplateMismatch, accum_identity, addr_of, dtype_name,
                      ld_global_f32, pick_vec, st_global_f32)
@@ -49,6 +50,86 @@ BATCH = 4              # vectors per buffer in flight in the streaming loop
 
 def _lit(e, v=None):
     return kind(e) == "Literal" and (v is None or e.value == v)
+
+
+def _online_max_sum(body, post_names):
+    """Recognise the online (max, sum of exponentials) accumulation of a
+    softmax in a pass-1 body (Emmy's form, reference
+    ``problems/f02_row_softmax/k_softmax_05263d.ir.txt:1-27``)::
+
+        gn = maximum(A, v); alpha = exp(A - gn); beta = exp(v - gn)
+        S = S * alpha + beta * w            # Accum add, base = S * alpha
+        A = maximum(A, v)                   # Accum maximum
+
+    with ``v`` and ``w`` computed without A or S.  Folding every element this
+    way gives A = max(v) and S = sum(exp(v - A) * w) (the rescaling
+    telescopes), which the template evaluates as a max tree followed by
+    independent exponentials instead of one dependent chain through every
+    element.  Returns None when the body has any other shape."""
+    defs = {}
+    for st in body:
+        k = kind(st)
+        if k == "Assign":
+            defs[st.name] = st
+        elif k == "Let":
+            defs[st.name] = st
+    accums = [st for st in body if kind(st) == "Accum"]
+    if len(accums) != 2:
+        return None
+    amax = [a for a in accums if a.op.name == "maximum" and not a.base]
+    asum = [a for a in accums if a.op.name == "add" and a.base]
+    if len(amax) != 1 or len(asum) != 1:
+        return None
+    A, S, v = amax[0].name, asum[0].name, amax[0].value
+    accs = {A, S}
+
+    def deps(name, seen=None):
+        seen = set() if seen is None else seen
+        if name in accs:
+            return {name}
+        st = defs.get(name)
+        if st is None or kind(st) != "Assign" or name in seen:
+            return set()
+        seen.add(name)
+        out = set()
+        for a in st.args:
+            out |= deps(a, seen)
+        return out
+
+    def op_of(name, op, n):
+        st = defs.get(name)
+        if st is None or kind(st) != "Assign" or st.op.name != op or len(st.args) != n:
+            return None
+        return list(st.args)
+
+    sa, sb = op_of(asum[0].base, "multiply", 2), op_of(asum[0].value, "multiply", 2)
+    if not sa or not sb or S not in sa:
+        return None
+    alpha = sa[1 - sa.index(S)]
+    dg = op_of(alpha, "exp", 1)
+    sub = dg and op_of(dg[0], "subtract", 2)
+    if not sub or sub[0] != A:
+        return None
+    gn = sub[1]
+    mx = op_of(gn, "maximum", 2)
+    if not mx or sorted(mx) != sorted([A, v]):
+        return None
+    for i, beta in enumerate(sb):
+        w = sb[1 - i]
+        e = op_of(beta, "exp", 1)
+        d = e and op_of(e[0], "subtract", 2)
+        if d and d == [v, gn] and not deps(w):
+            break
+    else:
+        return None
+    if deps(v):
+        return None
+    pattern = {gn, alpha, dg[0], beta, e[0], asum[0].base, asum[0].value}
+    if pattern & post_names:
+        return None
+    pre = [st for st in body if kind(st) != "Accum"
+           and not (kind(st) == "Assign" and (st.name in pattern or deps(st.name)))]
+    return {"max": A, "sum": S, "v": v, "w": w, "pre": pre}
 
 
 class RowsTemplate:
@@ -143,6 +224,10 @@ class RowsTemplate:
         self.V = pick_vec(L, B)
         self.J = L // (self.V * B)
         self._classify_loads()
+        later = []
+        for st in list(post) + list(loop2.body if loop2 is not None else reduce_tail or []):
+            later += list(getattr(st, "args", ()) or ()) + list(getattr(st, "values", ()) or ())
+        self.online = _online_max_sum(loop1.body, set(later))
         return self
 
     @staticmethod
@@ -287,9 +372,12 @@ class RowsTemplate:
             vecs = {b: [self._vec_load(b, j, "elem", hint=".L1::no_allocate") for j in range(self.J)]
                     for b in elem1}
             cvecs = {b: [self._vec_load(b, j, "col") for j in range(self.J)] for b in col1}
-            for j in range(self.J):
-                for ln in range(self.V):
-                    self._run_elem(chain, env, self.loop1.body, vecs, cvecs, j, ln)
+            if self.online:
+                self._online_pass1(chain, env, vecs, cvecs)
+            else:
+                for j in range(self.J):
+                    for ln in range(self.V):
+                        self._run_elem(chain, env, self.loop1.body, vecs, cvecs, j, ln)
             kept = vecs
         else:
             self._stream_pass1(chain, env, elem1, col1)
@@ -361,6 +449,37 @@ class RowsTemplate:
                 continue
             chain.stmt(s)
         chain.load = self._load_scalar
+
+    def _online_pass1(self, chain, env, vecs, cvecs):
+        """The recognised online (max, sum exp) accumulation over the
+        thread's resident elements: v and w per element from the body's
+        accumulator-free statements, A = max tree over the identity and the
+        v's, S = sum tree of exp(v - A) * w (no dependent chain)."""
+        k = self.k
+        o = self.online
+        vs, ws = [], []
+        for j in range(self.J):
+            for ln in range(self.V):
+                self._run_elem(chain, env, o["pre"], vecs, cvecs, j, ln)
+                vs.append(chain.value(o["v"]))
+                ws.append(chain.value(o["w"]))
+
+        def tree(vals, op):
+            while len(vals) > 1:
+                nxt = [emit_op_f32(k, op, [vals[i], vals[i + 1]])
+                       for i in range(0, len(vals) - 1, 2)]
+                vals = nxt + ([vals[-1]] if len(vals) % 2 else [])
+            return vals[0]
+
+        m = tree([env[o["max"]]] + vs, "maximum")
+        terms = []
+        for v, w in zip(vs, ws):
+            d = emit_op_f32(k, "subtract", [v, m])
+            e = emit_op_f32(k, "exp", [d])
+            terms.append(e if w == f32_hex(1.0) else emit_op_f32(k, "multiply", [e, w]))
+        total = tree(terms, "add")
+        k(f"mov.f32 {env[o['max']]}, {m};")
+        k(f"mov.f32 {env[o['sum']]}, {total};")
 
     def _stream_pass1(self, chain, env, elem1, col1):
         """Pass 1 for rows too long to keep in registers: a loop over batches

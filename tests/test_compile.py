@@ -230,3 +230,33 @@ def test_gemm_cta_pair_selection_and_assembly(kw, pair, native_lib):
     img = native.Image(ptx)
     assert img.registers()[c.entry] <= 128
     assert "spill" not in img.log or "0 bytes spill stores" in img.log
+
+
+def test_rows_online_softmax_recognised():
+    """The rows template evaluates Emmy's online (max, sum exp) softmax
+    accumulation as a max tree then independent exponentials; it recognises
+    only that exact structure (synthesised IR and the f02 problem), leaves
+    the other row kernels alone, and falls back to the IR's own recurrence
+    when the body differs (here: the rescale applied to the wrong operand)."""
+    from conftest import PROBLEMS
+    g, m = synth.config("softmax", rows=64, cols=1024).build()
+    c = compile_graph(g, m)
+    assert c.kind == "rows" and c.template.online["max"] == "acc0"
+    folder = next(p for p in PROBLEMS if p.name == "f02_row_softmax")
+    c = compile_graph(json.loads((folder / "kernel.ir.json").read_text()),
+                      json.loads((folder / "meta.json").read_text()))
+    assert c.template.online is not None
+    for name in ("rmsnorm", "l2norm", "row_sum"):
+        gg, mm = synth.config(name, rows=64, cols=1024).build()
+        assert compile_graph(gg, mm).template.online is None
+    bad = json.loads(json.dumps(g))
+    node = next(n for n in bad["nodes"].values() if n["op"] == "KernelOp")
+    body = node["op_fields"]["body"][0]
+    swapped = body.replace("Assign(name='in0__acc1_sa', op=ElementwiseImpl('multiply'), "
+                           "args=('acc1', 'in0__alpha')",
+                           "Assign(name='in0__acc1_sa', op=ElementwiseImpl('multiply'), "
+                           "args=('acc1', 'in0__beta')", 1)
+    assert swapped != body
+    node["op_fields"]["body"][0] = swapped
+    c = compile_graph(bad, m)
+    assert c.kind == "rows" and c.template.online is None
