@@ -64,6 +64,10 @@ class AttentionTemplate:
     # MUFU, by head dim (measured: a polynomial pair costs more issue and
     # FMA-pipe time than two MUFU ex2, so only the MUFU-bound D=64 gains)
     POLY = {64: 4, 128: 0}
+    # P pass software pipeline: the scale of pair s+LEAD and the sum/pack of
+    # pair s-LAG issue around the exponentials of pair s (measured: depth
+    # 1/2, 1/4 and 2/6 time the same)
+    PIPE = (1, 2)
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -611,7 +615,7 @@ class AttentionTemplate:
             k(f"mov.b64 {negm2}, {{{negm}, {negm}}};")
             for r in ps2:
                 k(f"mov.b64 {r}, 0;")
-            LEAD, LAG = 1, 2
+            LEAD, LAG = self.PIPE
             t2, es = {}, {}
             packed = {}
             maxops = []
@@ -652,7 +656,8 @@ class AttentionTemplate:
                 if pi == 15:
                     st16(16 * c, packed.pop(c))
 
-            stage_a(0)
+            for q in range(LEAD):
+                stage_a(q)
             for st_ in range(64 + LAG):
                 if st_ + LEAD < 64:
                     stage_a(st_ + LEAD)
