@@ -11,8 +11,8 @@ and adds the rules the sm_100a templates must keep:
   already defined, so ``@p mov r, ..`` alone does not define ``r``);
 * **bounded-wait** -- every loop that polls an mbarrier (``try_wait`` /
   ``test_wait``) also reads ``%globaltimer``, i.e. can give up;
-* **no-multicast-load** -- no bulk or tensor copy carries the cluster
-  broadcast qualifier (``MULTICAST_QUAL``);
+* **no-multicast-load** -- no bulk or tensor copy carries a qualifier that
+  feeds several CTAs (``broadcast_copy``);
 * **tmem** -- a kernel that allocates tensor memory relinquishes the
   allocation permit and deallocates the same number of columns;
 * **regsplit** -- ``setmaxnreg`` only together with ``.maxnreg`` and a
@@ -37,8 +37,13 @@ NO_DEF_FULL = ("mbarrier.init", "mbarrier.arrive", "tcgen05.mma", "tcgen05.commi
                "tcgen05.st", "tcgen05.alloc", "tcgen05.dealloc", "tcgen05.relinquish",
                "tcgen05.fence", "tcgen05.wait", "setmaxnreg", "griddepcontrol",
                "cp.async", "mbarrier.expect_tx")
-# the qualifier that would make one bulk/tensor copy feed several CTAs
-MULTICAST_QUAL = "multicast::cluster"
+
+
+def broadcast_copy(op: str) -> bool:
+    """A bulk or tensor copy with a qualifier that feeds several CTAs (any
+    ``multicast`` form)."""
+    return op.startswith("cp.async.bulk") and any(q.startswith("multicast")
+                                                  for q in op.split("."))
 
 
 def _instructions(ptx: str):
@@ -214,9 +219,7 @@ def check(ptx: str) -> list:
     _check_defined(_blocks(instrs), findings)
     _check_loops(instrs, findings)
     for n, text in instrs:
-        op = _split(text)[2]
-        copy = op.startswith("cp.async.bulk")
-        if copy and MULTICAST_QUAL in op.split("."):
+        if broadcast_copy(_split(text)[2]):
             findings.append(("no-multicast-load", n, "bulk/tensor copy fed to several CTAs"))
     alloc = re.findall(r"tcgen05\.alloc\.\S+\s+\[[^\]]+\],\s*(\d+)", ptx)
     dealloc = re.findall(r"tcgen05\.dealloc\.\S+\s+%\w+,\s*(\d+)", ptx)

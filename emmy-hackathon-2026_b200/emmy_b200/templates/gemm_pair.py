@@ -17,7 +17,7 @@ form a cluster of 2 and compute their 256 x 256 block as ONE pair MMA:
   from both halves, and each CTA's tensor memory receives its 128 rows x 256
   columns of f32 accumulators (allocated by ``tcgen05.alloc.cta_group::2``
   in both CTAs);
-* ``tcgen05.commit ... multicast::cluster`` with CTA mask 0b11 releases a
+* ``tcgen05.commit`` in its cluster-multicast form, CTA mask 0b11, releases a
   stage in BOTH CTAs' ``empty`` barriers, and at the end signals both CTAs'
   ``acc`` barriers; each CTA then drains its own tensor memory exactly like
   the single-CTA template (``tcgen05.ld.32x32b.x32``, ``st.global.v8``).
