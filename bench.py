@@ -379,6 +379,32 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             categories[nm] = {kk: r[kk] for kk in ("template", "ms_median", "GB/s", "TFLOP/s",
                                                    "frac", "reference_ptx_ms",
                                                    "speedup_vs_reference_ptx") if kk in r}
+    shards = None
+    if world > 1 and not args.no_categories:
+        # the configurations that shard without an exchange, strong scaling:
+        # each rank times its shard of the BASELINE problem; the job's time
+        # is the max over ranks
+        del x_sum, x_rows, devt, host, ptrs, params
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        from emmy_b200 import synth
+        shards = {}
+        for nm in D.SHARDED:
+            kw = D.shard_kwargs(nm, rank, world)
+            try:
+                r = measure_case(nm, kw, 10, 3)
+                ms_r, err = r["ms_median"], None
+            except Exception as e:  # every rank still joins the max below
+                ms_r, err = float("inf"), f"{type(e).__name__}: {e}"[:200]
+            ms_all = D.max_over_ranks(ms_r, device=dev)
+            full = synth.config(nm)
+            flops = synth.algorithmic_flops(full)
+            shards[nm] = {"partition": D.SHARDED[nm][0], "rank0_shard": D.shard_kwargs(nm, 0, world),
+                          "ms_max_over_ranks": round(ms_all, 5),
+                          "TFLOP/s": round(flops / (ms_all / 1e3) / 1e12, 1) if ms_all < 1e30 else None,
+                          "scaling": "strong"}
+            if err:
+                shards[nm]["error"] = err
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
@@ -401,6 +427,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "gpu_launches": 3 * args.steps,
             "clocks": clk.summary(),
             "categories": categories,
+            "shards": shards,
         }
         print(json.dumps(line), flush=True)
 

@@ -70,6 +70,26 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
     return start, start + q + (1 if rank < r else 0)
 
 
+# the configurations whose work shards across GPUs without an exchange, with
+# their BASELINE sizes: matmul by 256-row bands of A and C (B replicated),
+# attention by (batch, head) pairs
+SHARDED = {"matmul_bf16": ("M", 16384, 256), "matmul_f32": ("M", 16384, 256),
+           "attention": ("heads", 8 * 32, 1), "attention_d64": ("heads", 8 * 32, 1)}
+
+
+def shard_kwargs(name: str, rank: int, world: int) -> dict:
+    """Size overrides of ``synth.config(name)`` for ``rank``'s shard of the
+    BASELINE problem (strong scaling: the shards of all ranks together are
+    the single-GPU problem).  Matmul: a contiguous range of 256-row bands
+    (the CTA-pair tiles' rows); attention: a contiguous range of the
+    B x H = 256 (batch, head) pairs, synthesised as B=1, H=count."""
+    dim, total, unit = SHARDED[name]
+    lo, hi = shard_range(total // unit, rank, world)
+    if dim == "M":
+        return {"M": (hi - lo) * unit}
+    return {"B": 1, "H": hi - lo}
+
+
 def global_sum(partial) -> None:
     """In-place all-reduce (sum) of each rank's partial result."""
     import torch.distributed as dist

@@ -81,3 +81,23 @@ def test_shard_ranges_cover(n, world):
         a, b = D.shard_range(n, r, world)
         seen.extend(range(a, b))
     assert seen == list(range(n))
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_shard_kwargs_cover_the_problem(world):
+    """The per-rank shards of the matmul (256-row bands) and attention
+    ((batch, head) pairs) configurations add up to the BASELINE problem,
+    and every shard's IR is one the tensor-core templates accept."""
+    from emmy_b200 import synth
+    from emmy_b200.compiler import compile_graph
+    for name in D.SHARDED:
+        parts = [D.shard_kwargs(name, r, world) for r in range(world)]
+        if name.startswith("matmul"):
+            assert sum(p["M"] for p in parts) == 16384
+            assert all(p["M"] % 256 == 0 for p in parts)
+        else:
+            assert sum(p["B"] * p["H"] for p in parts) == 8 * 32
+    for name in ("matmul_bf16", "attention_d64"):
+        kw = D.shard_kwargs(name, world - 1, world)
+        g, m = synth.config(name, **kw).build()
+        assert compile_graph(g, m).kind in ("gemm", "attention")
