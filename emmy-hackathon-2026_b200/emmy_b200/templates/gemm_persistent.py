@@ -32,7 +32,7 @@ mbarrier wait is bounded by ``%globaltimer`` (codes 1 producer, 2 MMA issuer,
 from __future__ import annotations
 
 from ..ptx import Kernel
-from .gemm import GemmTemplate, _desc_hi, idesc_mma
+from .gemm import GemmTemplate, _desc_hi, idesc_mma, tf32_split
 
 WORKERS = 74                 # clusters of 2 CTAs: the 148 SMs of a B200
 PERSISTENT_MIN_STAGES = 4    # 4 x 32 KiB ring: one CTA per SM
@@ -443,13 +443,7 @@ def emit_pair_persistent(t) -> str:
             x = k.regs("r", 4)
             ad = f"{a0}+{i * 2048}" if i else a0
             k(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{ad}];")
-            hi = k.regs("r", 4)
-            lo = k.regs("r", 4)
-            for j in range(4):
-                k(f"cvt.rna.tf32.f32 {hi[j]}, {x[j]};")
-                d = k.reg("f")
-                k(f"sub.rn.f32 {d}, {x[j]}, {hi[j]};")
-                k(f"cvt.rna.tf32.f32 {lo[j]}, {d};")
+            hi, lo = tf32_split(k, x)
             k(f"st.shared.v4.b32 [{ad}], {{{', '.join(hi)}}};")
             k(f"st.shared.v4.b32 [{a0}+{RAW + i * 2048}], {{{', '.join(lo)}}};")
         # generic-proxy stores -> the tensor core's async-proxy reads
