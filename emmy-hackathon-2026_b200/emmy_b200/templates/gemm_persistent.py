@@ -25,7 +25,8 @@ with three changes:
   epilogue overlaps its own next main loop.
 
 Warp 0 lane 0 is the producer, warp 1 allocates tensor memory and its lane
-0 in the leader issues the MMAs; warps 2-3 only join the teardown.  Every
+0 in the leader issues the MMAs; warps 2-3 join the conversion in 3xTF32
+mode (six converter warps per CTA) and otherwise only the teardown.  Every
 mbarrier wait is bounded by ``%globaltimer`` (codes 1 producer, 2 MMA issuer,
 3 epilogue, 6 accumulator reuse); a role whose wait expires leaves its loop.
 """
@@ -86,6 +87,7 @@ def emit_pair_persistent(t) -> str:
     STG = 2 * RAW if tf32 else RAW   # 3xTF32 keeps the low parts after the raw slice
     BOXN = 128 // es                 # B boxes are 128 bytes wide
     KMMA = 32 // es                  # K per tcgen05.mma
+    CONVW = 6 if tf32 else 0         # 3xTF32 converter warps: 2..7
     NB = t.NB                        # 256-column tiles per row band
     MB = t.M // 256                  # 256-row bands
     TILES = MB * NB                  # pair tiles
@@ -158,8 +160,8 @@ def emit_pair_persistent(t) -> str:
     k(f"@!{p0} bra {skip_init};")
     for s in range(2 * S):
         k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 1;")
-    for s in range(2 * S, NBAR):               # conv[s]: 4 warps x 2 CTAs
-        k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 8;")
+    for s in range(2 * S, NBAR):               # conv[s]: the converter warps of 2 CTAs
+        k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], {2 * CONVW};")
     for b in range(2):
         k(f"mbarrier.init.shared::cta.b64 [{accb}+{8 * b}], 1;")
         k(f"mbarrier.init.shared::cta.b64 [{acce}+{8 * b}], 8;")
@@ -356,11 +358,13 @@ def emit_pair_persistent(t) -> str:
     tile_loop_tail(mtop)
     k.mark(end_mma)
 
-    # ------- warps 4-7 of each CTA: (3xTF32: converters, then) epilogue -------
+    # -- warps 4-7 of each CTA: epilogue (3xTF32: warps 2-7 convert first) --
     k("bar.warp.sync 0xffffffff;")
     pepi = k.reg("p")
     k(f"setp.ge.u32 {pepi}, {warp}, 4;")
-    k(f"@!{pepi} bra {teardown};")
+    prole = k.reg("p")
+    k(f"setp.ge.u32 {prole}, {warp}, {8 - CONVW if tf32 else 4};")
+    k(f"@!{prole} bra {teardown};")
     q = k.reg("r")
     k(f"and.b32 {q}, {warp}, 3;")
     lead_ae = k.reg("r")                          # acc_empty[0] of the leader
@@ -419,10 +423,14 @@ def emit_pair_persistent(t) -> str:
         lead_conv = k.reg("r")                    # conv[0] of the leader
         k(f"add.u32 {lead_conv}, {bars}, {16 * S};")
         k(f"mapa.shared::cluster.u32 {lead_conv}, {lead_conv}, 0;")
+        CT = 32 * CONVW                           # converter threads
         ct = k.reg("r")
-        k(f"and.b32 {ct}, {tid}, 127;")           # converter thread 0..127
+        k(f"sub.u32 {ct}, {tid}, {256 - CT};")    # converter thread 0..CT-1
         off0 = k.reg("r")
         k(f"shl.b32 {off0}, {ct}, 4;")            # 16 bytes per thread per pass
+        NV = RAW // 16                            # 16-byte vectors per stage
+        ptail = k.reg("p")                        # threads of the partial last pass
+        k(f"setp.lt.u32 {ptail}, {ct}, {NV % CT};")
         ntp1 = k.reg("r")
         k(f"add.u32 {ntp1}, {ntile}, 1;")
         k(f"mov.u32 {st}, 0;")
@@ -439,13 +447,20 @@ def emit_pair_persistent(t) -> str:
         sbc = stage_base(st)
         a0 = k.reg("r")
         k(f"add.u32 {a0}, {sbc}, {off0};")
-        for i in range(RAW // (16 * 128)):
+        def convert(i):
             x = k.regs("r", 4)
-            ad = f"{a0}+{i * 2048}" if i else a0
+            ad = f"{a0}+{i * 16 * CT}" if i else a0
             k(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{ad}];")
             hi, lo = tf32_split(k, x)
             k(f"st.shared.v4.b32 [{ad}], {{{', '.join(hi)}}};")
-            k(f"st.shared.v4.b32 [{a0}+{RAW + i * 2048}], {{{', '.join(lo)}}};")
+            k(f"st.shared.v4.b32 [{a0}+{RAW + i * 16 * CT}], {{{', '.join(lo)}}};")
+        for i in range(NV // CT):
+            convert(i)
+        if NV % CT:
+            skip_tail = k.label("CONV_TAIL")
+            k(f"@!{ptail} bra {skip_tail};")
+            convert(NV // CT)
+            k.mark(skip_tail)
         # generic-proxy stores -> the tensor core's async-proxy reads
         k("fence.proxy.async.shared::cta;")
         k("bar.warp.sync 0xffffffff;")
@@ -456,6 +471,7 @@ def emit_pair_persistent(t) -> str:
         k.mark(skip_conv)
         pdrain = k.reg("p")
         k(f"setp.ne.u32 {pdrain}, {it}, 0;")
+        k(f"and.pred {pdrain}, {pdrain}, {pepi};")    # the drain: warps 4-7
         skip_drain = k.label("SKIP_DRAIN")
         k(f"@!{pdrain} bra {skip_drain};")
         prev = k.reg("r")
