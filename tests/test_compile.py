@@ -260,3 +260,42 @@ def test_rows_online_softmax_recognised():
     node["op_fields"]["body"][0] = swapped
     c = compile_graph(bad, m)
     assert c.kind == "rows" and c.template.online is None
+
+
+@pytest.mark.parametrize("MB,NB", [(1, 1), (2, 3), (16, 32), (17, 5), (40, 7), (64, 32), (3, 100)])
+@pytest.mark.parametrize("group", [1, 8, 16])
+def test_gemm_raster_is_a_bijection(MB, NB, group):
+    """The grouped tile order of the CTA-pair GEMMs (``gemm_persistent.raster``,
+    run here by interpreting its emitted integer PTX), together with the
+    persistent schedule (cluster c takes tiles c, c+W, ...), covers every
+    (row band, column block) pair exactly once -- including a last group
+    with fewer bands than the others."""
+    from emmy_b200.ptx import Kernel
+    from emmy_b200.templates.gemm_persistent import WORKERS, raster
+    k = Kernel("t", [])
+    tt = k.reg("r")
+    mp, nbk = raster(k, tt, MB, NB, group)
+    prog = [ln.strip().rstrip(";") for ln in k.lines]
+
+    def run(t):
+        env = {tt: t}
+        for ins in prog:
+            op, args = ins.split(" ", 1)
+            d, *src = [a.strip() for a in args.split(",")]
+            v = [env[x] if x in env else int(x) for x in src]
+            base = op.split(".")[0]
+            env[d] = {"div": lambda a, b: a // b, "rem": lambda a, b: a % b,
+                      "mul": lambda a, b: a * b, "sub": lambda a, b: a - b,
+                      "add": lambda a, b: a + b, "min": min}[base](*v)
+        return env[mp], env[nbk]
+
+    tiles = MB * NB
+    W = min(WORKERS, tiles)
+    seen = set()
+    for c in range(W):
+        ntile = (tiles + W - 1 - c) // W
+        for i in range(ntile):
+            band, blk = run(c + W * i)
+            assert 0 <= band < MB and 0 <= blk < NB
+            seen.add((band, blk))
+    assert len(seen) == tiles
