@@ -107,6 +107,7 @@ class CompiledKernel:
             entry=kernel_info["entry"], arg_order=list(kernel_info["arg_order"]),
             scalar_tys={a["name"]: a["dtype"] for a in kernel_info.get("args", [])
                         if a.get("scalar")},
+            zero_outputs=list(kernel_info.get("zero_outputs", []) or []),
             info=kernel_info)
         self.image = native.Image(ptx, arch)
         self.tmaps = parse_tmaps(ptx)

@@ -43,3 +43,17 @@ def test_assemble_error_log(native_lib):
         native.Image(".version 8.8\n.target sm_100a\n.address_size 64\n"
                      ".visible .entry x() { not_an_instruction; }\n")
     assert e.value.code == -3 and "not_an_instruction" in str(e.value)
+
+
+def test_from_ptx_context_has_what_buffers_need():
+    """A kernel given as PTX text under a meta entry carries everything the
+    buffer setup of ``harness.run`` reads (arguments, scalars, outputs to
+    zero before each launch)."""
+    from emmy_b200 import harness, synth
+    g, m = synth.full_sum(n=1 << 16, ctas=16).build()
+    k = m["kernels"][0]
+    ptx = harness.CompiledKernel(g, m).ptx
+    pk = harness.CompiledKernel.from_ptx(ptx, k)
+    assert pk.ctx.arg_order == k["arg_order"]
+    assert pk.ctx.zero_outputs == list(k.get("zero_outputs", []))
+    assert pk.ctx.zero_outputs                        # the split sum zeroes its output
