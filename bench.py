@@ -480,17 +480,16 @@ def measure_case(name: str, kw: dict, steps: int, warmup: int) -> dict:
                      "frac": round(gbs / hbm, 3), "algorithmic_bytes": nb})
     f = REPO / "oracle" / "_ref" / f"{name}.ptx"
     if f.exists() and not kw:
-        img = native.Image(f.read_text())
-        mod = native.Module(img.data)
-        kh = mod.kernel("ref_" + kern.entry)
-        ref = harness.CompiledKernel.__new__(harness.CompiledKernel)
-        ref.__dict__.update(kern.__dict__)
-        ref._module, ref._kernel = mod, kh
+        # the reference compiler's PTX for the same IR, launched under the same
+        # meta entry from its own text (its parameters are the meta arguments
+        # alone: no tensor maps, no cluster)
+        ref = harness.CompiledKernel.from_ptx(f.read_text(),
+                                              dict(kern.info, entry="ref_" + kern.entry))
         rms = ref.time(bufs.ptrs(), warmup=2, iters=min(steps, 10), stream=stream,
                        flush=flush, zero=bufs.zero_list())
         line["reference_ptx_ms"] = round(float(np.median(rms)), 5)
         line["speedup_vs_reference_ptx"] = round(float(np.median(rms)) / med, 2)
-        mod.unload()
+        ref._module.unload()
     del bufs, fb
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
