@@ -291,28 +291,42 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         "row_mean": {"mean_count": count, "x": x_rows, "mean": out_rm},
     }
     e2e_steps = max(1, min(args.steps, 5))
-    h2d = d2h = 0
+    # a step's inputs cross PCIe once: x_rows feeds both row kernels, so the
+    # second call finds it resident (copied earlier in the same step)
+    from emmy_b200.data import nbytes as nb
+    resident, h2d, d2h = {}, 0, 0
+    seen = set()
     for n in order:
+        resident[n] = set()
         for a in kerns[n].info["args"]:
-            from emmy_b200.data import nbytes as nb
             if a.get("output"):
                 d2h += nb(a)
+                continue
+            key = (host[n][a["name"]].ctypes.data, devt[n][a["name"]].data_ptr())
+            if key in seen:
+                resident[n].add(a["name"])
             else:
+                seen.add(key)
                 h2d += nb(a)
     for n in order:  # warm
-        harness.run_host(kerns[n], host[n], devt[n], sh)
+        harness.run_host(kerns[n], host[n], devt[n], sh, resident[n])
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     D.barrier()
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(e2e_steps):
         for n in order:
-            harness.run_host(kerns[n], host[n], devt[n], sh)
+            harness.run_host(kerns[n], host[n], devt[n], sh, resident[n])
         D.global_sum(out_sum)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = D.max_over_ranks(e0.elapsed_time(e1), device=dev)
     e2e_val = step_bytes * world * e2e_steps / (e2e_ms / 1e3) / 1e9
+    # the host outputs of the end-to-end path are right (row kernels on the
+    # input the step copied once), checked on a few rows outside the timing
+    chk = x_rows_np[:16].astype(np.float64)
+    assert np.allclose(host_out["row_sum"][:16], chk.sum(1), rtol=1e-4, atol=1e-3)
+    assert np.allclose(host_out["row_mean"][:16], chk.mean(1), rtol=1e-4, atol=1e-4)
 
     # reference compiler's PTX for the same IRs, JIT-run on this GPU
     ref_ptx = {}

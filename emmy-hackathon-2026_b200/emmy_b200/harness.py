@@ -324,17 +324,21 @@ def load_problem(folder) -> tuple[dict, dict]:
     return json.loads(irs[0].read_text()), json.loads((folder / "meta.json").read_text())
 
 
-def run_host(kern: CompiledKernel, host: dict, dev: dict, stream=None) -> None:
+def run_host(kern: CompiledKernel, host: dict, dev: dict, stream=None,
+             resident=()) -> None:
     """The reference-facing round trip through ``emmy_run_host``: host inputs
     copied in, outputs zeroed, one launch, host outputs copied back.  ``host``
-    and ``dev`` map arg names to numpy arrays / torch device tensors."""
+    and ``dev`` map arg names to numpy arrays / torch device tensors; inputs
+    named in ``resident`` already hold their data on the device (an earlier
+    call of the same step copied them) and are passed with 0 bytes to copy."""
     k = kern.kernel()
     names = kern.ctx.arg_order
     args = {a["name"]: a for a in kern.info["args"]}
     n = len(names)
     hp = (ctypes.c_void_p * n)(*[host[x].ctypes.data for x in names])
     dp = (ctypes.c_uint64 * n)(*[dev[x].data_ptr() for x in names])
-    nb = (ctypes.c_size_t * n)(*[nbytes(args[x]) for x in names])
+    nb = (ctypes.c_size_t * n)(*[0 if (x in resident and not args[x].get("output"))
+                                 else nbytes(args[x]) for x in names])
     io = (ctypes.c_int * n)(*[1 if args[x].get("output") else 0 for x in names])
     extra = []
     keep = []
