@@ -68,6 +68,8 @@ class AttentionTemplate:
     # pair s-LAG issue around the exponentials of pair s (measured: depth
     # 1/2, 1/4 and 2/6 time the same)
     PIPE = (1, 2)
+    # wait for the next K block at the top of the MMA thread's block loop
+    EARLY_K = True
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -433,6 +435,12 @@ class AttentionTemplate:
             k(f"setp.ne.u32 {pacc}, {j}, 0;")
             k(f"and.b32 {par}, {j}, 1;")
             dk = kst = None
+            if not last and self.EARLY_K:
+                # the next K block (loaded stages ahead) before the P waits:
+                # its wait and descriptor stay off the tiles' critical path
+                k(f"add.u32 {jn}, {j}, 1;")
+                dk, kst = k_ready(jn)
+                k.comment(f"@trace 9 {jn}")
             for t in range(NT):
                 wait(k, bar(P_READY + t), par, status, 2, end_mma)
                 k.comment(f"@trace {3 * t + 1} {j}")
@@ -442,7 +450,7 @@ class AttentionTemplate:
                 if last:
                     commit(bar(FINAL + t))
                 else:
-                    if t == 0:
+                    if t == 0 and dk is None:
                         k(f"add.u32 {jn}, {j}, 1;")
                         dk, kst = k_ready(jn)
                         k.comment(f"@trace 9 {jn}")
