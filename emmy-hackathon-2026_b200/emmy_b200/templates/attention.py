@@ -62,8 +62,9 @@ class AttentionTemplate:
     name = "attention"
     # column pairs per 16 whose exp2 runs on the FMA pipe instead of the
     # MUFU, by head dim (measured: a polynomial pair costs more issue and
-    # FMA-pipe time than two MUFU ex2, so only the MUFU-bound D=64 gains)
-    POLY = {64: 4, 128: 0}
+    # FMA-pipe time than two MUFU ex2, so only the MUFU-bound D=64 gains;
+    # there 3 of 16 beat 2, 4, 5 and 6)
+    POLY = {64: 3, 128: 0}
     # P pass software pipeline: the scale of pair s+LEAD and the sum/pack of
     # pair s-LAG issue around the exponentials of pair s (measured: depth
     # 1/2, 1/4 and 2/6 time the same)
