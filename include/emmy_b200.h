@@ -147,7 +147,9 @@ EMMY_API int emmy_time_launches(emmy_kernel_t k, const uint32_t grid[3], const u
 /* host memory (reference docs/API.md:26-53 "args", submit.py:126-135):       */
 /* copy every input to its device buffer, zero the outputs, launch, copy the  */
 /* outputs back.  n_args buffers in arg_order; is_output[i] selects direction.*/
-/* dev[i] are caller-owned device buffers of bytes[i] bytes.                  */
+/* dev[i] are caller-owned device buffers of bytes[i] bytes.  An input with  */
+/* bytes[i] == 0 is not copied: its device buffer already holds the data     */
+/* (e.g. copied by an earlier call of the same step for another kernel).     */
 /* ------------------------------------------------------------------------ */
 EMMY_API int emmy_run_host(emmy_kernel_t k, const uint32_t grid[3], const uint32_t block[3],
                   uint32_t smem_bytes, const uint32_t *cluster, int n_args,
