@@ -386,7 +386,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         categories = {}
         for nm in CATEGORY_CASES:
             try:
-                r = measure_case(nm, {}, 10, 3)
+                r = measure_case(nm, {}, 30, 5)
             except Exception as e:  # report, keep the headline line
                 categories[nm] = {"error": f"{type(e).__name__}: {e}"[:200]}
                 continue
@@ -510,7 +510,7 @@ def measure_case(name: str, kw: dict, steps: int, warmup: int) -> dict:
     return line
 
 
-CATEGORY_CASES = ["vector_add", "rmsnorm", "softmax", "l2norm", "matmul_bf16", "matmul_f32",
+CATEGORY_CASES = ["vector_add", "vector_add_large", "rmsnorm", "softmax", "l2norm", "matmul_bf16", "matmul_f32",
                   "attention", "attention_d64"]
 
 

@@ -722,6 +722,9 @@ def attention(B: int = 8, H: int = 32, S: int = 4096, D: int = 128, BM: int = 25
 def config(name: str, **kw) -> Problem:
     table = {
         "vector_add": vector_add,
+        # the same IR at 2^28 elements (3 GiB moved) under the same 148 x 256
+        # launch: the pointwise template where bandwidth, not latency, bounds it
+        "vector_add_large": lambda **k: vector_add(**{"n": 268_435_456, **k}),
         "full_sum": full_sum,
         "row_sum": lambda **k: row_reduce(mean=False, **k),
         "row_mean": lambda **k: row_reduce(mean=True, **k),

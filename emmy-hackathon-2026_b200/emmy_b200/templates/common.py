@@ -124,8 +124,9 @@ def ld_global_f32(k: Kernel, addr: str, v: int, *, nc: bool = True, hint: str = 
     return regs
 
 
-def st_global_f32(k: Kernel, addr: str, regs, hint: str = "") -> None:
-    k(f"st.global{hint}{vec_suffix(len(regs))}.f32 [{addr}], {reg_list(regs)};")
+def st_global_f32(k: Kernel, addr: str, regs, hint: str = "", pred: str | None = None) -> None:
+    guard = f"@{pred} " if pred else ""
+    k(f"{guard}st.global{hint}{vec_suffix(len(regs))}.f32 [{addr}], {reg_list(regs)};")
 
 
 def addr_of(k: Kernel, base: str, elem_index_reg: str, nbytes: int = 4) -> str:

@@ -17,7 +17,10 @@ scalars (loads at a constant index), and when the writes cover the output
 exactly once.  Those conditions make any partition of the domain over the
 launched threads produce the same bytes, so the kernel is free to give each
 thread 8 consecutive floats (one ``ld/st.global.v8.f32`` per buffer, 32 B) in
-a grid-stride loop that keeps four vectors per buffer in flight.  The
+a grid-stride loop that keeps a batch of vectors per buffer in flight: the
+batch grows when the IR launches few threads per SM (HBM needs about 128 KB
+in flight per SM) and is predicated, so a thread's last, partial batch is one
+round trip, not a serial tail.  The
 arithmetic uses the ``.rn`` instructions of :mod:`emmy_b200.ops`, so the
 result is bit-identical to numpy's float32 evaluation of the same ops.
 """
@@ -31,7 +34,24 @@ from ..ops import emit_op_f32
 from .common import (Chain, TemplateMismatch, addr_of, dtype_name, ld_global_f32, linear_ids,
                      pick_vec, st_global_f32)
 
-UNROLL = 4
+UNROLL = 4              # smallest batch (vectors per buffer in flight per thread)
+UNROLL_MAX = 16
+INFLIGHT = 128 * 1024   # bytes of loads in flight per SM that the batch aims for
+DATA_REGS = 128         # cap on the batch's loaded registers per thread
+SMS = 148
+
+
+def batch_size(threads: int, inputs: int, vec: int) -> int:
+    """Vectors per input buffer each thread keeps in flight: enough for
+    INFLIGHT bytes per SM at this launch, a power of two in [UNROLL,
+    UNROLL_MAX], and at most DATA_REGS loaded registers."""
+    per_sm = max(1, -(-threads // SMS))
+    inputs = max(1, inputs)
+    u = UNROLL
+    while (u * 2 <= UNROLL_MAX and per_sm * inputs * 4 * vec * u < INFLIGHT
+           and u * 2 * inputs * vec <= DATA_REGS):
+        u *= 2
+    return u
 
 
 class PointwiseTemplate:
@@ -210,50 +230,57 @@ class PointwiseTemplate:
             r = k.reg("f")
             k(f"ld.global.nc.f32 {r}, [{a}];")
             cval[(b, idx)] = r
+        # vectors per thread at most ceil(NV / T): no batch larger than that
+        U = min(batch_size(T, len(self.elem_inputs), V), max(1, -(-NV // T)))
+        self.batch = U
         v = k.reg("r")
         k(f"mov.u32 {v}, {gid};")
         p = k.reg("p")
-        lim = NV - (UNROLL - 1) * T
-        loop4, tail, done = k.label("PW4"), k.label("PW1"), k.label("DONE")
-        if lim > 0:
-            k.mark(loop4)
-            k(f"setp.ge.s32 {p}, {v}, {lim};")
-            k(f"@{p} bra {tail};")
-            self._body(k, base, cval, v, V, T, UNROLL)
-            k(f"add.s32 {v}, {v}, {UNROLL * T};")
-            k(f"bra.uni {loop4};")
-        k.mark(tail)
+        loop, done = k.label("PW"), k.label("DONE")
+        k.mark(loop)
         k(f"setp.ge.s32 {p}, {v}, {NV};")
         k(f"@{p} bra {done};")
-        self._body(k, base, cval, v, V, T, 1)
-        k(f"add.s32 {v}, {v}, {T};")
-        k(f"bra.uni {tail};")
+        self._body(k, base, cval, v, V, T, U, NV)
+        k(f"add.s32 {v}, {v}, {U * T};")
+        k(f"bra.uni {loop};")
         k.mark(done)
         k("ret;")
         return k.render()
 
-    def _body(self, k, base, cval, v, V, T, unroll):
+    def _body(self, k, base, cval, v, V, T, unroll, NV):
+        """One batch: vector v + u*T for u < unroll, all loads issued before
+        the first store.  Vector v exists (the loop tested it); a later one
+        past the end loads the last vector instead (in bounds, never stored)
+        and its store is predicated off."""
         vals = []
         addrs = []
+        preds = []
         for u in range(unroll):
-            idx = v
+            idx, pu = v, None
             if u:
                 idx = k.reg("r")
                 k(f"add.s32 {idx}, {v}, {u * T};")
+                pu = k.reg("p")
+                k(f"setp.lt.s32 {pu}, {idx}, {NV};")
+                k(f"min.s32 {idx}, {idx}, {NV - 1};")
             e = k.reg("r")
             k(f"mul.lo.s32 {e}, {idx}, {V};")
             loaded = {}
             for b in self.elem_inputs:
                 a = addr_of(k, base[b], e)
-                loaded[b] = ld_global_f32(k, a, V, hint=".L1::no_allocate")
+                # coherent loads: they cannot move past the batch's stores (which
+                # may alias), so ptxas keeps the whole batch in flight, where it
+                # sinks read-only (.nc) loads to their uses
+                loaded[b] = ld_global_f32(k, a, V, nc=False, hint=".L1::no_allocate")
             vals.append(loaded)
             addrs.append(e)
+            preds.append(pu)
         for u in range(unroll):
             outs = []
             for lane in range(V):
                 outs.append(self._eval(k, self.program, vals[u], cval, lane, {}))
             a = addr_of(k, base[self.out], addrs[u])
-            st_global_f32(k, a, outs)
+            st_global_f32(k, a, outs, pred=preds[u])
 
     def _eval(self, k, t, loaded, cval, lane, memo):
         key = t

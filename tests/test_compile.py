@@ -299,3 +299,26 @@ def test_gemm_raster_is_a_bijection(MB, NB, group):
             assert 0 <= band < MB and 0 <= blk < NB
             seen.add((band, blk))
     assert len(seen) == tiles
+
+
+def test_pointwise_batch_follows_the_launch():
+    """The pointwise batch (vectors per buffer in flight per thread) grows when
+    the IR launches few threads per SM, stays within the register cap, and is
+    never larger than a thread's share; loads are coherent (ptxas keeps a
+    batch's loads ahead of its stores)."""
+    from emmy_b200 import compiler
+    from emmy_b200.templates.pointwise import DATA_REGS, batch_size
+    assert batch_size(148 * 256, 2, 8) == 8            # one 256-thread CTA per SM
+    assert batch_size(148 * 256 * 4, 2, 8) == 4        # four per SM: the minimum
+    assert batch_size(148 * 256, 2, 1) == 16           # scalar vectors: the maximum
+    for inputs in (1, 2, 3, 5):
+        u = batch_size(148 * 32, inputs, 8)
+        assert u * inputs * 8 <= max(DATA_REGS, 4 * inputs * 8)
+    cases = {(): 4, (("n", 268_435_456),): 8, (("n", 100),): 1}
+    for kw, want in cases.items():
+        g, m = synth.vector_add(**dict(kw)).build()
+        c = compiler.compile_graph(g, m)
+        ptx = c.render()
+        assert c.template.batch == want, (kw, c.template.batch)
+        assert "ld.global.L1::no_allocate." in ptx
+        assert "ld.global.nc" not in ptx

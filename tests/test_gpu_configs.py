@@ -17,6 +17,10 @@ SMALL = [
     ("vector_add", dict(n=1 << 16)),
     ("vector_add", dict(n=1000, threads=256)),          # ragged: n not a multiple of 8*T
     ("vector_add", dict(n=3, threads=256)),             # fewer elements than threads
+    # thin launch (one CTA of 256 per SM): batches of 8 vectors in flight, the
+    # last one partial (5 of 8 vectors of some threads exist)
+    ("vector_add", dict(n=148 * 256 * 8 * 8 * 2 + 8 * 5 * 256)),
+    ("vector_add", dict(n=100_003)),                    # odd n: scalar vectors, batches of 16
     ("full_sum", dict(n=1 << 20, ctas=64)),
     ("full_sum", dict(n=1 << 16, ctas=1, block=128)),   # one CTA (the pinned-coop form)
     ("row_sum", dict(rows=64, cols=2048)),
