@@ -33,7 +33,8 @@ mbarrier wait is bounded by ``%globaltimer`` (codes 1 producer, 2 MMA issuer,
 from __future__ import annotations
 
 from ..ptx import Kernel
-from .gemm import GemmTemplate, _desc_hi, idesc_mma, tf32_split
+from . import gemm as _gemm
+from .gemm import GemmTemplate, _desc_hi, idesc_mma, tf32_lo_trunc, tf32_split
 
 WORKERS = 74                 # clusters of 2 CTAs: the 148 SMs of a B200
 PERSISTENT_MIN_STAGES = 4    # 4 x 32 KiB ring: one CTA per SM
@@ -451,8 +452,11 @@ def emit_pair_persistent(t) -> str:
             x = k.regs("r", 4)
             ad = f"{a0}+{i * 16 * CT}" if i else a0
             k(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{ad}];")
-            hi, lo = tf32_split(k, x)
-            k(f"st.shared.v4.b32 [{ad}], {{{', '.join(hi)}}};")
+            if _gemm.TF32_HI_RAW:
+                lo = tf32_lo_trunc(k, x)
+            else:
+                hi, lo = tf32_split(k, x)
+                k(f"st.shared.v4.b32 [{ad}], {{{', '.join(hi)}}};")
             k(f"st.shared.v4.b32 [{a0}+{RAW + i * 16 * CT}], {{{', '.join(lo)}}};")
         for i in range(NV // CT):
             convert(i)
