@@ -322,3 +322,26 @@ def test_pointwise_batch_follows_the_launch():
         assert c.template.batch == want, (kw, c.template.batch)
         assert "ld.global.L1::no_allocate." in ptx
         assert "ld.global.nc" not in ptx
+
+
+def test_tf32_split_with_raw_high_part():
+    """3xTF32 with the raw slice as the high part: the tensor core keeps a tf32
+    element's top 19 bits, so hi = x & 0xFFFFE000 and the converters write only
+    lo = x - hi, which is exact in f32 and below 2^-10 |x|; the persistent
+    kernel's converters then hold no tf32 rounding and store one tile, not two."""
+    import numpy as np
+    from emmy_b200 import compiler
+    from emmy_b200.templates import gemm as G
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(100_000).astype(np.float32),
+                        np.float32([1.0, -1.0, 3.0e-38, 1.0e38, 0.0])])
+    hi = (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    lo = (x - hi).astype(np.float32)
+    assert np.array_equal((hi.astype(np.float64) + lo.astype(np.float64)).astype(np.float32), x)
+    nz = x != 0
+    assert np.all(np.abs(lo[nz]) < np.abs(x[nz]) * 2.0 ** -10)
+    assert G.TF32_HI_RAW
+    g, m = synth.matmul(dtype="f32", BK=32, stages=4, M=512, N=512, K=256).build()
+    ptx = compiler.compile_graph(g, m).render()
+    assert "cvt.rna.tf32.f32" not in ptx
+    assert "and.b32" in ptx and "-8192" in ptx
