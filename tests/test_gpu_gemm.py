@@ -150,3 +150,27 @@ def test_gemm_f32_persistent_pairs(kw):
         rows = np.sort(np.random.default_rng(9).choice(kw["M"], 64, replace=False))
     got, ref = _run(p, rows=rows)
     assert np.max(np.abs(got - ref)) <= 2e-5 * max(1.0, float(np.max(np.abs(ref))))
+
+
+def test_gemm_f32_3xtf32_error_against_float64():
+    """3xTF32 with the raw fp32 slice as the high part: the normwise error
+    against float64 at 1024 x 1024 x 4096 stays inside the fp32 matmul's rel
+    1e-4 (measured 2.9e-5, the same as with rounded high parts) and the mean
+    error shows no offset.  A tensor core that rounded the raw element to tf32
+    instead of dropping its 13 low bits would leave lo = x - trunc(x) off by up
+    to a tf32 ulp per element, a normwise error near 2^-12, which the first
+    bound rejects."""
+    from emmy_b200 import harness
+    p = synth.matmul(dtype="f32", BK=32, stages=4, M=1024, N=1024, K=4096)
+    g, m = p.build()
+    k = m["kernels"][0]
+    ins = {a["name"]: materialize(a) for a in k["args"] if not a.get("output")}
+    outs, kern = harness.run(g, m, ins)
+    assert kern.kind == "gemm"
+    A = ins["x0"].astype(np.float64).reshape(1024, 4096)
+    B = ins["x1"].astype(np.float64).reshape(4096, 1024)
+    ref = A @ B
+    got = outs["matmul"].astype(np.float64).reshape(1024, 1024)
+    nrm = np.linalg.norm(ref)
+    assert np.linalg.norm(got - ref) / nrm < 1e-4
+    assert abs(float((got - ref).mean())) * 1024 / nrm < 1e-6
