@@ -14,7 +14,18 @@
 // The price: the array (EMMY_NOALLOC_MAX_ROWS floats, 256 KiB) is held by every
 // GPU that loads this library until the process exits; calls may use at most
 // that many rows; and every call shares it, so calls that overlap on the GPU
-// (two streams, two threads) race on it.
+// (two streams, two threads) race on it.  The first call on a device loads
+// this file's device code there, which is when the array is reserved on that
+// device: a caller with a fixed memory budget makes that first call at
+// start-up.
+//
+// The row count is checked against the launches, not only against the
+// caller's word: the first kernel writes one entry per CTA of its grid, so
+// grid1 must be (rows, 1, 1); the second reads the entry of each element's
+// row, one thread per element, so its one-dimensional grid2 x block2 must
+// cover rows x cols elements and no whole block more.  Kernels compiled for
+// other shapes than (rows, cols) are outside what these checks can see: pass
+// the pair compiled from the two IRs for exactly these rows and columns.
 #include "../../include/emmy_b200.h"
 
 #include <cuda_runtime.h>
@@ -57,9 +68,17 @@ int scratch_on_current_device(uint64_t *out) {
   if (!g_scratch_addr[dev]) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_rows_scratch);
-    if (e != cudaSuccess || !p)
-      return fail_msg(EMMY_ENODRIVER, "emmy_rmsnorm_noalloc: cudaGetSymbolAddress failed: %s",
-                      cudaGetErrorString(e));
+    if (e != cudaSuccess || !p) {
+      // the device code is built for sm_100a only: name the device's
+      // architecture, the usual reason for "no kernel image"
+      int major = 0, minor = 0;
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+      return fail_msg(EMMY_ENODRIVER,
+                      "emmy_rmsnorm_noalloc: cudaGetSymbolAddress failed (%s); this library's "
+                      "device code is built for sm_100a, device is sm_%ld%ld",
+                      cudaGetErrorString(e), major, minor);
+    }
     g_scratch_addr[dev] = reinterpret_cast<uint64_t>(p);
   }
   *out = g_scratch_addr[dev];
@@ -72,7 +91,7 @@ extern "C" EMMY_API int emmy_rmsnorm_noalloc(
     emmy_kernel_t meansq, const uint32_t grid1[3], const uint32_t block1[3],
     emmy_kernel_t apply, const uint32_t grid2[3], const uint32_t block2[3],
     uint64_t mean_count, uint64_t add_c1, uint64_t x, uint64_t w, uint64_t y,
-    int rows, void *stream) {
+    int rows, int cols, void *stream) {
   if (!meansq || !apply || !grid1 || !block1 || !grid2 || !block2 || !mean_count || !add_c1 ||
       !x || !w || !y)
     return emmy_internal_fail(EMMY_EINVAL, "emmy_rmsnorm_noalloc: bad argument");
@@ -80,6 +99,25 @@ extern "C" EMMY_API int emmy_rmsnorm_noalloc(
     return fail_msg(EMMY_EINVAL,
                     "emmy_rmsnorm_noalloc: %s %ld rows, the scratch array holds 1..%ld",
                     "cannot take", rows, static_cast<long>(EMMY_NOALLOC_MAX_ROWS));
+  if (cols <= 0)
+    return fail_msg(EMMY_EINVAL, "emmy_rmsnorm_noalloc: %s %ld columns", "cannot take", cols);
+  // the launches must be the ones the row count describes (checked in 64 bits:
+  // a grid of three 32-bit extents overflows 32)
+  const uint64_t g1 = uint64_t(grid1[0]) * grid1[1] * grid1[2];
+  if (grid1[1] != 1 || grid1[2] != 1 || g1 != uint64_t(rows))
+    return fail_msg(EMMY_EINVAL,
+                    "emmy_rmsnorm_noalloc: %s grid1 of %ld CTAs for %ld rows (one CTA per row)",
+                    "refusing", static_cast<long>(g1 > 0x7fffffffull ? 0x7fffffffull : g1), rows);
+  // the element kernel's launch is one-dimensional (at most 2^31 x 1024 threads)
+  const uint64_t t2 = block2[0], g2 = grid2[0];
+  const uint64_t cells = uint64_t(rows) * uint64_t(cols);
+  if (grid2[1] != 1 || grid2[2] != 1 || block2[1] != 1 || block2[2] != 1 || t2 == 0 ||
+      t2 > 1024 || g2 * t2 < cells || g2 * t2 >= cells + t2)
+    return fail_msg(EMMY_EINVAL,
+                    "emmy_rmsnorm_noalloc: %s grid2 x block2 of %ld threads for %ld elements "
+                    "(one thread per element)", "refusing",
+                    static_cast<long>(g2 * t2 > 0x7fffffffull ? 0x7fffffffull : g2 * t2),
+                    static_cast<long>(cells > 0x7fffffffull ? 0x7fffffffull : cells));
   uint64_t ms = 0;
   if (int e = scratch_on_current_device(&ms)) return e;
   // The first kernel writes every row's entry before the second reads it, so

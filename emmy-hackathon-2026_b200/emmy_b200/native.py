@@ -134,7 +134,7 @@ def lib() -> ctypes.CDLL:
                                     ctypes.c_void_p]
         L.emmy_rmsnorm_noalloc.argtypes = [ctypes.c_void_p, c_u32p, c_u32p, ctypes.c_void_p,
                                            c_u32p, c_u32p] + [ctypes.c_uint64] * 5 + [
-                                           ctypes.c_int, ctypes.c_void_p]
+                                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
         _LIB = L
     return _LIB
 

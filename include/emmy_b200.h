@@ -162,22 +162,28 @@ EMMY_API int emmy_run_host(emmy_kernel_t k, const uint32_t grid[3], const uint32
 /* allocator that owns all device memory, code running while a CUDA graph   */
 /* is built, a fixed memory budget: the two-kernel RMSNorm (`meansq` = row   */
 /* mean of squares into an intermediate, then `apply` = x * rsqrt(ms + eps)  */
-/* * w; kernels compiled from those two IRs, params in their meta arg_order) */
-/* with the intermediate in a static device array of EMMY_NOALLOC_MAX_ROWS   */
-/* floats (256 KiB, held by every GPU that loads the library until exit)     */
-/* instead of a caller buffer.  The caller passes inputs (the one-element    */
-/* constant buffers mean_count and add_c1, x[rows, cols], w[cols]) and the   */
-/* output y.  More rows than the array holds -> EMMY_EINVAL, nothing runs.   */
-/* The first call on a device resolves the array's address there (make it   */
-/* before any stream capture); all calls share the array, so calls that     */
-/* overlap on the GPU race.  Nothing is allocated, by this call or later.    */
+/* * w; the pair compiled from those two IRs for exactly rows x cols, params */
+/* in their meta arg_order) with the intermediate in a static device array  */
+/* of EMMY_NOALLOC_MAX_ROWS floats (256 KiB, held by every GPU that loads    */
+/* the library until exit) instead of a caller buffer.  The caller passes    */
+/* inputs (the one-element constant buffers mean_count and add_c1,          */
+/* x[rows, cols], w[cols]) and the output y.  Refused with EMMY_EINVAL      */
+/* before anything runs: more rows than the array holds, a grid1 other than */
+/* (rows, 1, 1) (the first kernel writes one entry per CTA), or a 1-D       */
+/* grid2 x block2 that does not cover rows x cols elements with less than   */
+/* one block to spare (the second reads one entry per element's row).      */
+/* The first call on a device loads the library's device code there and    */
+/* so reserves the array on that device: make it at start-up if the memory */
+/* budget is fixed, and before any stream capture.  All calls share the     */
+/* array, so calls that overlap on the GPU race.  The calls themselves      */
+/* allocate nothing.                                                         */
 /* ------------------------------------------------------------------------ */
 #define EMMY_NOALLOC_MAX_ROWS 65536
 EMMY_API int emmy_rmsnorm_noalloc(emmy_kernel_t meansq, const uint32_t grid1[3],
                                   const uint32_t block1[3], emmy_kernel_t apply,
                                   const uint32_t grid2[3], const uint32_t block2[3],
                                   uint64_t mean_count, uint64_t add_c1, uint64_t x, uint64_t w,
-                                  uint64_t y, int rows, void *stream);
+                                  uint64_t y, int rows, int cols, void *stream);
 
 #ifdef __cplusplus
 }

@@ -29,8 +29,10 @@ import sys
 import types
 from pathlib import Path
 
-REF_ROOT = Path(os.environ.get("EMMY_REFERENCE_ROOT", "/root/reference"))
 REPO = Path(__file__).resolve().parent.parent
+# the reference checkout: EMMY_REFERENCE_ROOT, else a "reference" folder beside
+# this repository
+REF_ROOT = Path(os.environ.get("EMMY_REFERENCE_ROOT") or REPO.parent / "reference")
 REF_OUT = REPO / "oracle" / "_ref"
 
 sys.path.insert(0, str(REPO / "emmy-hackathon-2026_b200"))

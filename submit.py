@@ -6,14 +6,17 @@
     python submit.py path/to/problem_folder --compiler ./compile.py --time
 
 The same command line, messages and exit codes as the reference's ``submit.py``
-(reference ``submit.py:1-161``): with ``--compiler`` every kernel of the problem
+(reference ``submit.py:53-161``: a usage problem prints its message to stderr and
+exits 1, as ``sys.exit(msg)`` does there; argparse's own errors exit 2): with ``--compiler`` every kernel of the problem
 is compiled by ``python <compiler> <entry>.ir.json`` in ``meta.json`` order, the
 buffers an earlier kernel wrote are handed to later ones (``intermediate``
 arguments), and every output named in ``expected.npz`` is compared with
 ``np.allclose(got, ref, rtol, atol)``.  Instead of a remote runner, the kernels
 run on the local B200 through this build's C-ABI runtime.
 
-Exit code 0 = every kernel compiled and the outputs matched within tolerance.
+Exit code 0 = every kernel compiled and the outputs matched within tolerance;
+1 = an unknown problem, a missing PTX/--compiler, a multi-kernel problem given
+one PTX file, a compiler failure or an output outside tolerance.
 """
 from __future__ import annotations
 
@@ -42,15 +45,15 @@ def main(argv=None) -> int:
         print(f"unknown problem {args.problem!r}; choose from: "
               + ", ".join(sorted(p.name for p in PROBLEMS.iterdir()
                                  if (p / "meta.json").exists())), file=sys.stderr)
-        return 2
+        return 1
     meta = json.loads((pdir / "meta.json").read_text())
     if not args.compiler and not args.ptx:
         print("give a PTX file or --compiler", file=sys.stderr)
-        return 2
+        return 1
     if not args.compiler and len(meta["kernels"]) > 1:
         print(f"{args.problem} has {len(meta['kernels'])} kernels - use --compiler",
               file=sys.stderr)
-        return 2
+        return 1
 
     from emmy_b200 import problem
     src = problem.compiler_ptx(args.compiler) if args.compiler else problem.file_ptx(args.ptx)

@@ -12,7 +12,9 @@ sys.path.insert(0, str(REPO))
 GOLDEN = REPO / "tests" / "golden"
 PROBLEMS = sorted(p for p in (GOLDEN / "problems").iterdir() if p.is_dir())
 FIXTURES = sorted(p for p in (GOLDEN / "fixtures").iterdir() if p.is_dir())
-REFERENCE = Path(os.environ.get("EMMY_REFERENCE_ROOT", "/root/reference"))
+# the reference checkout (only the tests that regenerate or compare against it
+# use it): EMMY_REFERENCE_ROOT, else a "reference" folder beside this repository
+REFERENCE = Path(os.environ.get("EMMY_REFERENCE_ROOT") or REPO.parent / "reference")
 
 
 def pytest_configure(config):

@@ -22,7 +22,7 @@ disagrees with its IR and is restated from the IR as well.
 Outputs above 65536 elements are stored as a fixed random sample
 (``idx``, ``val``) to keep the fixtures small.
 
-Usage: python tests/golden/make_corpus.py [--reference /root/reference]
+Usage: python tests/golden/make_corpus.py [--reference <reference checkout>]
 """
 from __future__ import annotations
 
@@ -30,6 +30,7 @@ import argparse
 import hashlib
 import importlib.util
 import json
+import os
 import shutil
 import sys
 from pathlib import Path
@@ -72,7 +73,10 @@ def _restated(name: str, vals: dict):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EMMY_REFERENCE_ROOT")
+                    or str(Path(__file__).resolve().parents[3] / "reference"),
+                    help="the reference checkout (default: EMMY_REFERENCE_ROOT, else "
+                         "a 'reference' folder beside this repository)")
     args = ap.parse_args()
     ref = Path(args.reference)
     spec = importlib.util.spec_from_file_location("refs", ref / "tools" / "harness" / "refs.py")

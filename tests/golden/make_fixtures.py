@@ -11,13 +11,14 @@ code: they are copied verbatim (the IR renamed ``kernel.ir.json``) so that the
 GPU box, which has no reference tree, can run the parity tests, and a
 ``MANIFEST.json`` records each file's SHA-256 and origin.
 
-Usage: python tests/golden/make_fixtures.py [--reference /root/reference]
+Usage: python tests/golden/make_fixtures.py [--reference <reference checkout>]
 """
 from __future__ import annotations
 
 import argparse
 import hashlib
 import json
+import os
 import shutil
 from pathlib import Path
 
@@ -30,7 +31,10 @@ def sha(p: Path) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EMMY_REFERENCE_ROOT")
+                    or str(Path(__file__).resolve().parents[3] / "reference"),
+                    help="the reference checkout (default: EMMY_REFERENCE_ROOT, else "
+                         "a 'reference' folder beside this repository)")
     args = ap.parse_args()
     ref = Path(args.reference)
     manifest = {}
