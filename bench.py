@@ -17,6 +17,16 @@ Multi-GPU (torchrun, one process per GPU): weak scaling -- every rank owns a
 full-size shard of each input (its own seed); the full sum finishes with one
 NCCL all-reduce of the per-rank partial, inside the step.
 
+Every timed kernel is checked in the same run, after its timing: its module's
+``__emmy_status`` word (set when a bounded wait expired) and sampled outputs
+against the CPU oracle (``oracle/expr.py``, the checker only) at the
+configuration's tolerance; a case that fails reports no number.  After the
+headline, N=1 times every other category at its BASELINE size (``categories``,
+each with a bounded CPU baseline); N>1 times every configuration as strong
+scaling of the BASELINE problem (``shards``: rows, element chunks, CTA slices
+of the full sum finished by the all-reduce, 256-row bands of matmul,
+(batch, head) pairs of attention).
+
 ``--impl reference`` times the reference's own CPU evaluation of the same
 expressions (numpy, as in the reference's tools/harness/refs.py:41-124) on
 the host cores, rank 0 only.
@@ -40,6 +50,17 @@ sys.path.insert(0, str(REPO / "emmy-hackathon-2026_b200"))
 METRIC = "per-kernel HBM GB/s as % of B200 roofline (reductions: full sum + row sum + row mean)"
 WORKLOAD = "reductions: sum(x[268435456] ~ U(0,1)) + x[32768,8192].sum(-1) + x.mean(-1), f32"
 FALLBACK_HBM = 6650.0
+FALLBACK_BF16 = 1590.0
+STEP_BYTES = 3_221_487_624          # full sum + row sum + row mean, per rank
+
+
+def config_of(world: int) -> dict:
+    """The workload description, identical in both arms' JSON lines."""
+    return {"workload": WORKLOAD, "step": "one pass of the three reductions",
+            "per_rank_bytes_per_step": STEP_BYTES,
+            "l2": "each input is 1 GiB > 126 MB L2; no flush needed",
+            "parallelism": f"weak scaling over {world} rank(s); full sum finished by "
+                           "NCCL all-reduce"}
 
 
 def peaks() -> tuple[float, str]:
@@ -134,6 +155,16 @@ def bytes_of(p) -> int:
     return synth.algorithmic_bytes(p)
 
 
+def bf16_peak() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_BF16, "fallback"
+
+
 # --------------------------------------------------------------------------
 # CPU evaluation (the reference's numpy expressions)
 # --------------------------------------------------------------------------
@@ -184,7 +215,7 @@ def run_reference(args, rank: int, world: int) -> None:
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "step": "one pass of the three reductions"},
+            "config": config_of(world),
             "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads,
                              "kind": "port",
                              "sample": "full workload (3 GiB read), numpy reductions split "
@@ -192,6 +223,204 @@ def run_reference(args, rank: int, world: int) -> None:
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def cpu_case(name: str) -> dict | None:
+    """The category's CPU baseline on a bounded sample of its BASELINE
+    workload, timed on this host (median of 3 after one warm pass): numpy
+    float32 expressions single-threaded for the pointwise add and the fused row
+    ops (the reference's refs.py forms), numpy/OpenBLAS float32 matmul on every
+    host core, torch CPU ``scaled_dot_product_attention`` in fp32 on every host
+    core.  Returns the metric of the category (GB/s or TFLOP/s)."""
+    import numpy as np
+    cores = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(0)
+
+    def timed(fn, reps=3):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    if name in ("vector_add", "vector_add_large"):
+        n = 1_048_576 if name == "vector_add" else 1 << 25
+        a = rng.uniform(-1, 1, n).astype(np.float32)
+        b = rng.uniform(-1, 1, n).astype(np.float32)
+        sec = timed(lambda: a + b, 20 if n < 1 << 22 else 3)
+        return {"value": round(12 * n / sec / 1e9, 2), "unit": "GB/s", "cores": 1, "kind": "port",
+                "sample": f"a + b over {n} f32 elements (numpy, one thread)"
+                          + ("" if name == "vector_add" else "; 1/8 of the 2^28-element case")}
+    if name in ("rmsnorm", "softmax", "l2norm"):
+        rows, cols = 4096, 4096
+        x = rng.standard_normal((rows, cols)).astype(np.float32)
+        w = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+        fn = {
+            "rmsnorm": lambda: x / np.sqrt((x * x).mean(-1, keepdims=True) + np.float32(1e-6)) * w,
+            "softmax": lambda: (lambda z: (lambda e: e / e.sum(-1, keepdims=True))(
+                np.exp(z - z.max(-1, keepdims=True))))(x * np.float32(4.0)),
+            "l2norm": lambda: x / np.maximum(np.sqrt((x * x).sum(-1, keepdims=True)),
+                                             np.float32(1e-12)),
+        }[name]
+        sec = timed(fn)
+        return {"value": round(8 * rows * cols / sec / 1e9, 2), "unit": "GB/s", "cores": 1,
+                "kind": "port",
+                "sample": f"{rows} of the 65536 rows x {cols} (1/16 of the workload), numpy "
+                          "float32, one thread"}
+    if name in ("matmul_bf16", "matmul_f32"):
+        from threadpoolctl import threadpool_limits
+        M, N, K = 2048, 8192, 4096
+        a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+        b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+        with threadpool_limits(limits=cores, user_api="blas"):
+            sec = timed(lambda: a @ b)
+        return {"value": round(2 * M * N * K / sec / 1e12, 3), "unit": "TFLOP/s", "cores": cores,
+                "kind": "port",
+                "sample": f"A[{M}, {K}] @ B[{K}, {N}] (1/8 of the M rows), numpy/OpenBLAS "
+                          f"float32 sgemm on {cores} threads"
+                          + (" (bf16 inputs held as float32)" if name == "matmul_bf16" else "")}
+    if name in ("attention", "attention_d64"):
+        import torch
+        D = 128 if name == "attention" else 64
+        H, S = 4, 4096
+        torch.set_num_threads(cores)
+        g = torch.Generator().manual_seed(0)
+        q, k, v = (torch.randn(1, H, S, D, generator=g) for _ in range(3))
+        sec = timed(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v))
+        return {"value": round(4 * H * S * S * D / sec / 1e12, 3), "unit": "TFLOP/s",
+                "cores": cores, "kind": "port",
+                "sample": f"{H} of the 256 (batch, head) pairs, S={S}, d={D}: torch CPU "
+                          f"scaled_dot_product_attention fp32 on {cores} threads"}
+    return None
+
+
+# --------------------------------------------------------------------------
+# same-run checks
+# --------------------------------------------------------------------------
+
+def read_status(kern) -> int | None:
+    """The module's ``__emmy_status`` word (nonzero once a bounded wait has
+    expired in any launch of the module); None for kernels without one."""
+    import torch
+    from emmy_b200 import native
+    try:
+        addr, _ = kern.module().global_addr("__emmy_status")
+    except native.EmmyError:
+        return None
+    st = torch.zeros(1, dtype=torch.int32)
+    native.check(native.lib().emmy_memcpy_dtoh_async(st.data_ptr(), addr, 4, None))
+    torch.cuda.synchronize()
+    return int(st[0])
+
+
+def _host(t, dt: str):
+    """A device tensor (slice) as the oracle takes it: bf16 as uint16 bits."""
+    import numpy as np
+    import torch
+    if dt == "bf16":
+        return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    return t.contiguous().cpu().numpy()
+
+
+def check_outputs(p, kern, bufs, stream, seed: int = 0) -> dict:
+    """Same-run correctness of a kernel that was just timed, outside the timed
+    region: one more launch on the timed buffers (outputs zeroed first, as
+    ``zero_outputs`` says), the module's status word, and sampled outputs
+    against the CPU oracle at the configuration's tolerance (bit-exact for the
+    pointwise add).  Samples: the whole output up to 4 Mi elements, else four
+    1 Mi-element windows (pointwise); the whole input (full sum); 64 rows (row
+    kernels); 16 rows of C (matmul); 2 (batch, head) pairs (attention)."""
+    import numpy as np
+    import torch
+    from emmy_b200 import native
+    sys.path.insert(0, str(REPO))
+    from oracle import expr
+
+    L = native.lib()
+    for z, nb in bufs.zero_list():
+        native.check(L.emmy_memset_async(z, 0, nb, stream))
+    kern.launch(bufs.ptrs(), stream)
+    torch.cuda.synchronize()
+    status = read_status(kern) if kern.kind != "ptx" else None
+    m = p.meta()
+    spec = m["oracle"]
+    fam, out = spec["family"], spec["output"]
+    args = bufs.args
+    rng = np.random.default_rng(seed)
+
+    def dev(name):
+        shape = args[name]["shape"]
+        return bufs.t[name].view(*shape) if shape else bufs.t[name]
+
+    def host(name, sel=None):
+        t = dev(name)
+        return _host(t if sel is None else t[sel], args[name]["dtype"])
+
+    names = list(spec["args"].values())
+    pairs = []                                   # (inputs, got) samples
+    if fam == "add":
+        n = args[out]["shape"][0]
+        if n <= 1 << 22:
+            sels, what = [slice(0, n)], f"all {n} elements"
+        else:
+            w = 1 << 20
+            starts = sorted(int(s) * w for s in rng.choice(n // w, 4, replace=False))
+            sels, what = [slice(s0, s0 + w) for s0 in starts], "4 windows of 2^20 elements"
+        for sl in sels:
+            pairs.append(({x: host(x, sl) for x in names}, host(out, sl)))
+    elif fam == "sum":
+        what = "the whole input"
+        pairs.append(({x: host(x) for x in names}, host(out)))
+    elif fam in ("row_sum", "row_mean", "rmsnorm", "softmax", "l2norm"):
+        R = args[out]["shape"][0]
+        k = min(64, R)
+        rows = np.sort(rng.choice(R, k, replace=False))
+        idx = torch.as_tensor(rows, device=bufs.t[out].device)
+        what = f"{k} sampled rows"
+        ins = {}
+        for x in names:
+            sh = args[x]["shape"]
+            ins[x] = host(x, idx) if len(sh) == 2 and sh[0] == R else host(x)
+        pairs.append((ins, host(out, idx)))
+    elif fam == "matmul":
+        Mr = args[out]["shape"][0]
+        k = min(16, Mr)
+        rows = np.sort(rng.choice(Mr, k, replace=False))
+        idx = torch.as_tensor(rows, device=bufs.t[out].device)
+        what = f"{k} sampled rows of C"
+        a, b = spec["args"]["a"], spec["args"]["b"]
+        pairs.append(({a: host(a, idx), b: host(b)}, host(out, idx)))
+    elif fam == "attention":
+        B, H = args[out]["shape"][:2]
+        flat = rng.choice(B * H, min(2, B * H), replace=False)
+        bh = [(int(f) // H, int(f) % H) for f in sorted(flat)]
+        what = f"(batch, head) pairs {bh}"
+        ins = {x: np.stack([host(x, (b_, h_)) for b_, h_ in bh]) for x in names}
+        pairs.append((ins, np.stack([host(out, (b_, h_)) for b_, h_ in bh])))
+    else:
+        return {"checked": False, "reason": f"no sampler for family {fam}"}
+    ok, err, scale = True, 0.0, 0.0
+    for ins, got in pairs:
+        ref = expr.evaluate_family(spec, ins)[out]
+        got = np.asarray(got).reshape(ref.shape)
+        rtol, atol = expr.tolerance(m, ref)
+        if rtol == 0 and atol == 0:
+            good = got.tobytes() == ref.tobytes()
+        else:
+            good = bool(np.allclose(got, ref, rtol=rtol, atol=atol))
+        ok = ok and good
+        d = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+        err = max(err, float(np.max(d)) if d.size else 0.0)
+        scale = max(scale, float(np.max(np.abs(ref))) if ref.size else 0.0)
+    if status not in (None, 0):
+        ok = False
+    res = {"checked": True, "ok": ok, "status": status, "max_abs_err": err,
+           "err_over_max_ref": err / scale if scale else 0.0, "sample": what,
+           "tolerance": "bit-exact" if not m.get("rtol") and not m.get("atol")
+           else f"rtol {m.get('rtol')}, atol {m.get('atol') if m.get('atol') is not None else 'rtol*max|ref|'}"}
+    return res
 
 
 # --------------------------------------------------------------------------
@@ -203,6 +432,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     import torch
     from emmy_b200 import dist as D
     from emmy_b200 import harness, native
+    sys.path.insert(0, str(REPO))
+    from oracle import expr
 
     torch.cuda.set_device(local)
     native.check(native.lib().emmy_device_init(local))
@@ -214,11 +445,13 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     kerns = {n: harness.CompiledKernel(*p.build()) for n, p in probs}
     nbytes = {n: bytes_of(p) for n, p in probs}
     step_bytes = sum(nbytes.values())
+    assert step_bytes == STEP_BYTES
 
     x_sum_h, x_rows_h = host_inputs(rank)
     x_sum_h, x_rows_h = x_sum_h.pin_memory(), x_rows_h.pin_memory()
     x_sum = x_sum_h.to(dev)
     x_rows = x_rows_h.to(dev)
+    x_sum_np, x_rows_np = x_sum_h.numpy(), x_rows_h.numpy()
     count = torch.tensor([8192.0], device=dev)
     out_sum = torch.zeros(1, device=dev)
     out_rs = torch.zeros(32768, device=dev)
@@ -248,15 +481,38 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             evs[3].record(stream)
         D.global_sum(out_sum)
 
+    # the oracle's float64 sum (``expr.full_sum`` before its float32 cast) of
+    # this rank's input, and of all ranks' inputs: each rank's float64
+    # partial, all-reduced in float64
+    own64 = float(np.sum(x_sum_np, dtype=np.float64))
+    part64 = torch.tensor([own64], dtype=torch.float64, device=dev)
+    D.global_sum(part64)
+    ref_total = float(part64.item())
+    sample_rows = np.sort(np.random.default_rng(5 + rank).choice(32768, 64, replace=False))
+    ref_rs = expr.row_sum(x_rows_np[sample_rows])
+    ref_rm = expr.row_mean(x_rows_np[sample_rows])
+
+    def check_headline(tag: str) -> dict:
+        """The step's three outputs against the oracle (the all-reduced full
+        sum against the sum of every rank's input)."""
+        got_sum = float(out_sum.item())
+        rs = out_rs.cpu().numpy()[sample_rows]
+        rm = out_rm.cpu().numpy()[sample_rows]
+        rel_sum = abs(got_sum - ref_total) / abs(ref_total)
+        ok_rs = np.allclose(rs, ref_rs, rtol=1e-4, atol=1e-4 * float(np.abs(ref_rs).max()))
+        ok_rm = np.allclose(rm, ref_rm, rtol=1e-4, atol=1e-4 * float(np.abs(ref_rm).max()))
+        res = {"checked": True, "ok": bool(rel_sum <= 1e-4 and ok_rs and ok_rm),
+               "full_sum_rel_err": rel_sum,
+               "row_sum_max_abs_err": float(np.abs(rs - ref_rs).max()),
+               "row_mean_max_abs_err": float(np.abs(rm - ref_rm).max()),
+               "sample": f"full sum of all {world} rank(s)' inputs; 64 sampled rows of the "
+                         "row kernels", "tolerance": "rtol 1e-4"}
+        assert res["ok"], (tag, res)
+        return res
+
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    # correctness spot check of this rank's results (cheap, outside timing)
-    ref_sum = float(x_sum.double().sum())
-    if world == 1:
-        assert abs(float(out_sum) - ref_sum) <= 1e-4 * abs(ref_sum), (float(out_sum), ref_sum)
-    ref_rs = x_rows.double().sum(-1)
-    assert torch.allclose(out_rs.double(), ref_rs, rtol=1e-4, atol=1e-4 * float(ref_rs.abs().max()))
 
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -274,11 +530,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
            for i, n in enumerate(order)}
     ms_max = D.max_over_ranks(ms, device=dev)
     value = step_bytes * world * args.steps / (ms_max / 1e3) / 1e9
+    # the last timed step's outputs (the all-reduced sum included)
+    headline_check = check_headline("headline")
 
     # e2e through the C ABI with host buffers: copies in, launch, result out
     host_out = {"full_sum": np.zeros(1, np.float32), "row_sum": np.zeros(32768, np.float32),
                 "row_mean": np.zeros(32768, np.float32)}
-    x_sum_np, x_rows_np = x_sum_h.numpy(), x_rows_h.numpy()
     host = {
         "full_sum": {"x": x_sum_np, "sum_1": host_out["full_sum"]},
         "row_sum": {"x": x_rows_np, "sum_1": host_out["row_sum"]},
@@ -290,7 +547,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         "row_sum": {"x": x_rows, "sum_1": out_rs},
         "row_mean": {"mean_count": count, "x": x_rows, "mean": out_rm},
     }
-    e2e_steps = max(1, min(args.steps, 5))
+    e2e_steps = args.steps
     # a step's inputs cross PCIe once: x_rows feeds both row kernels, so the
     # second call finds it resident (copied earlier in the same step)
     from emmy_b200.data import nbytes as nb
@@ -322,26 +579,29 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     torch.cuda.synchronize()
     e2e_ms = D.max_over_ranks(e0.elapsed_time(e1), device=dev)
     e2e_val = step_bytes * world * e2e_steps / (e2e_ms / 1e3) / 1e9
-    # the host outputs of the end-to-end path are right (row kernels on the
-    # input the step copied once), checked on a few rows outside the timing
-    chk = x_rows_np[:16].astype(np.float64)
-    assert np.allclose(host_out["row_sum"][:16], chk.sum(1), rtol=1e-4, atol=1e-3)
-    assert np.allclose(host_out["row_mean"][:16], chk.mean(1), rtol=1e-4, atol=1e-4)
+    # the host outputs of the end-to-end path against the oracle (row kernels
+    # on the input the step copied once; the per-rank sum before its
+    # all-reduce, which runs on the device copy)
+    e2e_ok = (np.allclose(host_out["row_sum"][sample_rows], ref_rs, rtol=1e-4,
+                          atol=1e-4 * float(np.abs(ref_rs).max()))
+              and np.allclose(host_out["row_mean"][sample_rows], ref_rm, rtol=1e-4,
+                              atol=1e-4 * float(np.abs(ref_rm).max()))
+              and abs(float(host_out["full_sum"][0]) - own64) <= 1e-4 * abs(own64))
+    assert e2e_ok, "end-to-end outputs differ from the oracle"
 
-    # reference compiler's PTX for the same IRs, JIT-run on this GPU
-    ref_ptx = {}
+    # reference compiler's PTX for the same IRs, JIT-run on this GPU, each
+    # checked against the oracle after its timing
+    ref_ptx, ref_ok = {}, {}
     for n in order:
         f = REPO / "oracle" / "_ref" / f"{n}.ptx"
         if not f.exists():
             continue
-        img = native.Image(f.read_text())
-        mod = native.Module(img.data)
-        kh = mod.kernel("ref_" + kerns[n].entry)
-        k = kerns[n]
-        arr, keep = k.params(ptrs[n])
-        zero = [(out_sum.data_ptr(), 4)] if n == "full_sum" else []
-        from emmy_b200 import harness as H  # noqa: F401
         import ctypes
+        k = kerns[n]
+        ref = harness.CompiledKernel.from_ptx(f.read_text(), dict(k.info, entry="ref_" + k.entry))
+        kh = ref.kernel()
+        arr, keep = ref.params(ptrs[n])
+        zero = [(out_sum.data_ptr(), 4)] if n == "full_sum" else []
         it = 10
         outbuf = (ctypes.c_float * it)()
         zd = (ctypes.c_uint64 * 1)(*([z[0] for z in zero] or [0]))
@@ -349,8 +609,18 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         native.check(L.emmy_time_launches(kh.h, native.u32x3(k.grid), native.u32x3(k.block),
                                           k.smem, None, arr, sh, 2, it, 0, 0, zd, zb,
                                           len(zero), outbuf))
-        ref_ptx[n] = statistics.median(list(outbuf))
-    # our kernels under the same protocol as the reference PTX (median of 10)
+        torch.cuda.synchronize()
+        if n == "full_sum":
+            good = abs(float(out_sum.item()) - own64) <= 1e-4 * abs(own64)
+        else:
+            got = (out_rs if n == "row_sum" else out_rm).cpu().numpy()[sample_rows]
+            want = ref_rs if n == "row_sum" else ref_rm
+            good = bool(np.allclose(got, want, rtol=1e-4, atol=1e-4 * float(np.abs(want).max())))
+        ref_ok[n] = good
+        if good:
+            ref_ptx[n] = statistics.median(list(outbuf))
+        ref._module.unload()
+        del keep
     ours_med = {n: statistics.median(per[n]) for n in order}
 
     hbm, src = peaks()
@@ -366,17 +636,18 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         if n in ref_ptx:
             cats[n]["reference_ptx_ms"] = round(ref_ptx[n], 4)
             cats[n]["speedup_vs_reference_ptx"] = round(ref_ptx[n] / ours_med[n], 2)
+        if n in ref_ok:
+            cats[n]["reference_ptx_checked"] = ref_ok[n]
     cpu = None
     if rank == 0 and world == 1:
-        xs, xr = x_sum_np, x_rows_np
-        cpu_reductions(xs, xr, 1)
-        ts = [cpu_reductions(xs, xr, 1) for _ in range(3)]
+        cpu_reductions(x_sum_np, x_rows_np, 1)
+        ts = [cpu_reductions(x_sum_np, x_rows_np, 1) for _ in range(3)]
         sec = statistics.median(ts)
         cpu = {"value": round(step_bytes / sec / 1e9, 3), "unit": "GB/s", "cores": 1,
                "kind": "port",
                "sample": "full workload once per run (median of 3), numpy float32 reductions "
                          "as the reference's refs.py, single thread"}
-    categories = None
+    categories = cat_clocks = None
     if world == 1 and not args.no_categories:
         # every other category's kernel at its BASELINE size (own buffers;
         # the reductions inputs are released first)
@@ -384,85 +655,213 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
         categories = {}
-        for nm in CATEGORY_CASES:
-            try:
-                # 10 launches as a burst, comparable with the burst peaks (longer
-                # runs of the contractions settle at the power-capped clock); the
-                # microsecond-scale vector add takes 50 for a stable median
-                r = measure_case(nm, {}, 50 if nm == "vector_add" else 10, 3)
-            except Exception as e:  # report, keep the headline line
-                categories[nm] = {"error": f"{type(e).__name__}: {e}"[:200]}
-                continue
-            categories[nm] = {kk: r[kk] for kk in ("template", "ms_median", "GB/s", "TFLOP/s",
-                                                   "frac", "reference_ptx_ms",
-                                                   "speedup_vs_reference_ptx") if kk in r}
+        with Clocks(local) as cclk:
+            for nm in CATEGORY_CASES:
+                try:
+                    # 10 launches as a burst, comparable with the burst peaks
+                    # (longer runs of the contractions settle at the
+                    # power-capped clock); the microsecond-scale vector add
+                    # takes 50 for a stable median
+                    r = measure_case(nm, {}, 50 if nm == "vector_add" else 10, 3,
+                                     extras=nm == "vector_add")
+                except Exception as e:  # report, keep the headline line
+                    categories[nm] = {"error": f"{type(e).__name__}: {e}"[:300]}
+                    continue
+                categories[nm] = {kk: r[kk] for kk in (
+                    "template", "ms_median", "GB/s", "TFLOP/s", "frac", "peak_basis",
+                    "reference_ptx_ms", "speedup_vs_reference_ptx", "reference_ptx_check",
+                    "check", "back_to_back", "wide_launch") if kk in r}
+        cat_clocks = cclk.summary()
+        if rank == 0:
+            for nm in CATEGORY_CASES:
+                try:
+                    categories[nm]["cpu_baseline"] = cpu_case(nm)
+                except Exception as e:
+                    categories[nm]["cpu_baseline"] = {"error": f"{type(e).__name__}: {e}"[:200]}
     shards = None
     if world > 1 and not args.no_categories:
-        # the configurations that shard without an exchange, strong scaling:
-        # each rank times its shard of the BASELINE problem; the job's time
-        # is the max over ranks
         del x_sum, x_rows, devt, host, ptrs, params
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
-        from emmy_b200 import synth
-        shards = {}
-        for nm in D.SHARDED:
-            kw = D.shard_kwargs(nm, rank, world)
-            try:
-                r = measure_case(nm, kw, 10, 3)
-                ms_r, err = r["ms_median"], None
-            except Exception as e:  # every rank still joins the max below
-                ms_r, err = float("inf"), f"{type(e).__name__}: {e}"[:200]
-            ms_all = D.max_over_ranks(ms_r, device=dev)
-            full = synth.config(nm)
-            flops = synth.algorithmic_flops(full)
-            shards[nm] = {"partition": D.SHARDED[nm][0], "rank0_shard": D.shard_kwargs(nm, 0, world),
-                          "ms_max_over_ranks": round(ms_all, 5),
-                          "TFLOP/s": round(flops / (ms_all / 1e3) / 1e12, 1) if ms_all < 1e30 else None,
-                          "scaling": "strong"}
-            if err:
-                shards[nm]["error"] = err
+        shards = run_shards(rank, world, dev)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (torch.Generator seeds 1000*rank+{0,1}; BASELINE distributions)",
-            "config": {"workload": WORKLOAD, "per_rank_bytes_per_step": step_bytes,
-                       "l2": "each input is 1 GiB > 126 MB L2; no flush needed",
-                       "parallelism": f"weak scaling over {world} rank(s); full sum "
-                                      "finished by NCCL all-reduce"},
+            "config": config_of(world),
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                          "peak": hbm, "peak_source": src, "unit": "GB/s",
                          "frac": round(achieved / hbm, 3), "traffic": traffic,
                          "algorithmic_bytes": nbytes[dom]},
+            "check": headline_check,
             "kernels": cats,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps, "checked": True,
                     "path": "emmy_run_host (C ABI) from pinned host memory"},
             "gpu_launches": 3 * args.steps,
             "clocks": clk.summary(),
             "categories": categories,
+            "categories_clocks": cat_clocks,
             "shards": shards,
         }
         print(json.dumps(line), flush=True)
 
 
-def measure_case(name: str, kw: dict, steps: int, warmup: int) -> dict:
+def run_shards(rank: int, world: int, dev) -> dict:
+    """Every configuration at N > 1 as strong scaling of its BASELINE problem:
+    each rank times its shard (10 launches, median), the job's time is the
+    max over ranks, and each rank checks its shard's outputs against the
+    oracle; a shard that fails on any rank reports no number."""
+    import torch
+    from emmy_b200 import dist as D
+    from emmy_b200 import synth
+    hbm, _ = peaks()
+    bf, _ = bf16_peak()
+    shards = {}
+    for nm in D.SHARDED:
+        kw = D.shard_kwargs(nm, rank, world)
+        try:
+            if nm == "full_sum":
+                r = measure_full_sum_strong(kw, 10, 3, dev, rank)
+            else:
+                r = measure_case(nm, kw, 10, 3, seed=rank)
+            ms_r, err = r["ms_median"], None
+            ok_r = bool(r["check"]["ok"])
+            e_r = float(r["check"]["err_over_max_ref"])
+        except Exception as e:  # every rank still joins the reductions below
+            r, ms_r, err, ok_r, e_r = None, float("inf"), f"{type(e).__name__}: {e}"[:300], \
+                False, float("inf")
+        ms_all = D.max_over_ranks(ms_r, device=dev)
+        ok_all = D.max_over_ranks(0.0 if ok_r else 1.0, device=dev) == 0.0
+        err_all = D.max_over_ranks(e_r, device=dev)
+        full = synth.config(nm)
+        flops = synth.algorithmic_flops(full)
+        d = {"partition": D.SHARDED[nm][0], "rank0_shard": D.shard_kwargs(nm, 0, world),
+             "ms_max_over_ranks": round(ms_all, 5) if ok_all else None, "scaling": "strong",
+             "check": {"checked": True, "ok_all_ranks": ok_all, "err_over_max_ref_max": err_all,
+                       "sample": r["check"]["sample"] if r else None}}
+        if ok_all and ms_all < 1e30:
+            if flops:
+                tf = flops / (ms_all / 1e3) / 1e12
+                peak = bf / 6 if nm == "matmul_f32" else bf
+                d.update({"TFLOP/s": round(tf, 1), "frac_of_n_peaks": round(tf / (world * peak), 3)})
+            else:
+                gbs = synth.algorithmic_bytes(full) / (ms_all / 1e3) / 1e9
+                d.update({"GB/s": round(gbs, 1), "frac_of_n_peaks": round(gbs / (world * hbm), 3)})
+        if err:
+            d["error"] = err
+        if nm == "full_sum":
+            d["collective"] = "NCCL all-reduce of the per-rank partial, inside each timed launch"
+        shards[nm] = d
+    return shards
+
+
+def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -> dict:
+    """The strong-scaled full sum: each rank sums its CTA slices of the global
+    input, then one NCCL all-reduce finishes the sum; both are inside each
+    timed step (CUDA events on the launching stream, which the all-reduce
+    joins).  Checked against the float64 sum of all ranks' slices."""
+    import numpy as np
+    import torch
+    from emmy_b200 import dist as D
+    from emmy_b200 import harness, native, synth
+    p = synth.config("full_sum", **kw)
+    kern = harness.CompiledKernel(*p.build())
+    bufs = harness.Buffers.random(kern, seed=rank)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    out = bufs.t["sum_1"]
+    L = native.lib()
+    k = kern.kernel()
+    arr, keep = kern.params(bufs.ptrs())
+
+    def step():
+        native.check(L.emmy_memset_async(out.data_ptr(), 0, 4, sh))
+        native.check(L.emmy_launch(k.h, native.u32x3(kern.grid), native.u32x3(kern.block),
+                                   kern.smem, kern._cluster_arg(), arr, sh))
+        D.global_sum(out)
+
+    for _ in range(warmup):
+        step()
+    D.barrier()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    got = float(out.item())
+    part = torch.tensor([float(np.sum(bufs.t["x"].cpu().numpy(), dtype=np.float64))],
+                        dtype=torch.float64, device=dev)
+    D.global_sum(part)
+    want = float(part.item())
+    rel = abs(got - want) / abs(want)
+    del keep
+    return {"ms_median": float(np.median(ms)),
+            "check": {"checked": True, "ok": rel <= 1e-4, "status": None, "rel_err": rel,
+                      "err_over_max_ref": rel,
+                      "sample": "the all-reduced sum against the float64 sum of every rank's "
+                                "slices"}}
+
+
+def back_to_back(kern, ptrs: dict, n: int = 100, reps: int = 5) -> float:
+    """Per-launch time of ``n`` launches captured back to back in one CUDA
+    graph (no flush, no events between them): the device-side rate of a
+    launch-latency-bound kernel."""
+    import torch
+    from emmy_b200 import native
+    L = native.lib()
+    k = kern.kernel()
+    arr, keep = kern.params(ptrs)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        native.check(L.emmy_launch(k.h, native.u32x3(kern.grid), native.u32x3(kern.block),
+                                   kern.smem, kern._cluster_arg(), arr, s.cuda_stream))
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(n):
+            native.check(L.emmy_launch(k.h, native.u32x3(kern.grid), native.u32x3(kern.block),
+                                       kern.smem, kern._cluster_arg(), arr, s.cuda_stream))
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    e0.record(cur)
+    for _ in range(reps):
+        g.replay()
+    e1.record(cur)
+    torch.cuda.synchronize()
+    del g, keep
+    return e0.elapsed_time(e1) / (n * reps)
+
+
+def measure_case(name: str, kw: dict, steps: int, warmup: int, seed: int = 0,
+                 extras: bool = False) -> dict:
     """Time one synthesised configuration: ``steps`` launches through the C ABI,
     each bracketed by CUDA events on the launching stream; L2 flushed between
-    launches when the inputs would fit in it.  Includes the reference
-    compiler's PTX for the same IR (``oracle/_ref``) when it exists."""
+    launches when the inputs would fit in it.  Then, outside the timing, the
+    outputs are checked (``check_outputs``); a failed check drops the numbers.
+    Includes the reference compiler's PTX for the same IR (``oracle/_ref``)
+    when it exists, checked the same way.  ``extras`` (the vector add): the
+    same kernel back to back in a CUDA graph, and a wider launch of the same
+    IR (one 32-byte vector per thread)."""
     import numpy as np
     import torch
 
-    from emmy_b200 import harness, native, synth
+    from emmy_b200 import harness, synth
 
     p = synth.config(name, **kw)
     g, m = p.build()
     kern = harness.CompiledKernel(g, m)
-    bufs = harness.Buffers.random(kern, seed=0)
+    bufs = harness.Buffers.random(kern, seed=seed)
     stream = torch.cuda.current_stream().cuda_stream
     in_bytes = sum(t.numel() * t.element_size() for n, t in bufs.t.items()
                    if not bufs.args[n].get("output"))
@@ -472,6 +871,7 @@ def measure_case(name: str, kw: dict, steps: int, warmup: int) -> dict:
         flush = (fb.data_ptr(), fb.numel())
     ms = kern.time(bufs.ptrs(), warmup=warmup, iters=steps, stream=stream,
                    flush=flush, zero=bufs.zero_list())
+    chk = check_outputs(p, kern, bufs, stream, seed=seed)
     med = float(np.median(ms))
     hbm, src = peaks()
     nb = synth.algorithmic_bytes(p)
@@ -479,22 +879,40 @@ def measure_case(name: str, kw: dict, steps: int, warmup: int) -> dict:
     line = {"case": name, "size": kw, "template": kern.kind, "entry": kern.entry,
             "ms_median": round(med, 5), "ms_min": round(float(np.min(ms)), 5),
             "launches": steps, "l2_flush": flush is not None,
-            "regs": kern.image.registers().get(kern.entry)}
+            "regs": kern.image.registers().get(kern.entry), "check": chk}
     if flops:
         tf = flops / (med / 1e3) / 1e12
-        mp = REPO / "MEASURED_PEAKS.json"
-        peak = float(json.loads(mp.read_text())["bf16_tflops"]) if mp.exists() else 1590.0
-        basis = "measured bf16 peak"
+        peak, psrc = bf16_peak()
+        basis = f"{psrc} bf16 peak"
         if kern.kind == "gemm" and getattr(kern.compiler.template, "mode", "") == "tf32x3":
             # fp32 through 3xTF32: tf32 runs at half the bf16 rate and every
             # product costs three tf32 MMAs
-            peak, basis = peak / 2 / 3, "3xTF32 effective = measured bf16 peak / 2 / 3"
+            peak, basis = peak / 2 / 3, f"3xTF32 effective = {psrc} bf16 peak / 2 / 3"
         line.update({"TFLOP/s": round(tf, 1), "peak": round(peak, 1), "peak_basis": basis,
                      "frac": round(tf / peak, 3), "flops": flops})
     else:
         gbs = nb / (med / 1e3) / 1e9
         line.update({"GB/s": round(gbs, 1), "peak": hbm, "peak_source": src,
                      "frac": round(gbs / hbm, 3), "algorithmic_bytes": nb})
+    if extras and kern.kind == "pointwise":
+        t = back_to_back(kern, bufs.ptrs())
+        line["back_to_back"] = {"us_per_launch": round(t * 1e3, 3),
+                                "GB/s": round(nb / (t / 1e3) / 1e9, 1),
+                                "note": "100 launches in one CUDA graph, no L2 flush: the "
+                                        "8 MiB of inputs stay in L2 between launches"}
+        n = p.meta()["kernels"][0]["args"][0]["shape"][0]
+        wide = synth.config(name, **{**kw, "threads": max(256, n // 8)})
+        wk = harness.CompiledKernel(*wide.build())
+        wb = harness.Buffers.random(wk, seed=seed)
+        wms = wk.time(wb.ptrs(), warmup=warmup, iters=steps, stream=stream, flush=flush,
+                      zero=wb.zero_list())
+        wchk = check_outputs(wide, wk, wb, stream, seed=seed)
+        wmed = float(np.median(wms))
+        line["wide_launch"] = {"grid": list(wk.grid), "block": list(wk.block),
+                               "ms_median": round(wmed, 5),
+                               "GB/s": round(nb / (wmed / 1e3) / 1e9, 1) if wchk["ok"] else None,
+                               "check": wchk}
+        del wb
     f = REPO / "oracle" / "_ref" / f"{name}.ptx"
     if f.exists() and not kw:
         # the reference compiler's PTX for the same IR, launched under the same
@@ -504,17 +922,24 @@ def measure_case(name: str, kw: dict, steps: int, warmup: int) -> dict:
                                               dict(kern.info, entry="ref_" + kern.entry))
         rms = ref.time(bufs.ptrs(), warmup=2, iters=min(steps, 10), stream=stream,
                        flush=flush, zero=bufs.zero_list())
-        line["reference_ptx_ms"] = round(float(np.median(rms)), 5)
-        line["speedup_vs_reference_ptx"] = round(float(np.median(rms)) / med, 2)
+        rchk = check_outputs(p, ref, bufs, stream, seed=seed)
+        line["reference_ptx_check"] = {"ok": rchk["ok"], "max_abs_err": rchk["max_abs_err"]}
+        if rchk["ok"]:
+            line["reference_ptx_ms"] = round(float(np.median(rms)), 5)
+            line["speedup_vs_reference_ptx"] = round(float(np.median(rms)) / med, 2)
         ref._module.unload()
+    if not chk["ok"]:
+        for key in ("TFLOP/s", "GB/s", "frac", "speedup_vs_reference_ptx"):
+            line.pop(key, None)
+        line["error"] = "output check failed: numbers withheld"
     del bufs, fb
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return line
 
 
-CATEGORY_CASES = ["vector_add", "vector_add_large", "rmsnorm", "softmax", "l2norm", "matmul_bf16", "matmul_f32",
-                  "attention", "attention_d64"]
+CATEGORY_CASES = ["vector_add", "vector_add_large", "rmsnorm", "softmax", "l2norm", "matmul_bf16",
+                  "matmul_f32", "attention", "attention_d64"]
 
 
 def run_case(args) -> None:

@@ -70,24 +70,48 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
     return start, start + q + (1 if rank < r else 0)
 
 
-# the configurations whose work shards across GPUs without an exchange, with
-# their BASELINE sizes: matmul by 256-row bands of A and C (B replicated),
-# attention by (batch, head) pairs
-SHARDED = {"matmul_bf16": ("M", 16384, 256), "matmul_f32": ("M", 16384, 256),
-           "attention": ("heads", 8 * 32, 1), "attention_d64": ("heads", 8 * 32, 1)}
+# the configurations measured at N > 1 as strong scaling of the BASELINE
+# problem: (partition, number of units, unit size).  Rows for the row
+# reductions and fused row ops, 2048-element chunks for the pointwise add,
+# 256-row bands of A and C for matmul (B replicated), (batch, head) pairs for
+# attention -- none of them exchanges data -- and for the full sum whole CTA
+# slices (131,072 elements each, one CTA of the one-GPU launch), whose
+# per-rank partial sums are finished by one all-reduce.
+SUM_SLICE = 268_435_456 // 2048
+SHARDED = {
+    "vector_add": ("elements", 1_048_576 // 2048, 2048),
+    "full_sum": ("slices", 2048, SUM_SLICE),
+    "row_sum": ("rows", 32768, 1), "row_mean": ("rows", 32768, 1),
+    "rmsnorm": ("rows", 65536, 1), "softmax": ("rows", 65536, 1), "l2norm": ("rows", 65536, 1),
+    "matmul_bf16": ("M", 16384 // 256, 256), "matmul_f32": ("M", 16384 // 256, 256),
+    "attention": ("heads", 8 * 32, 1), "attention_d64": ("heads", 8 * 32, 1),
+}
 
 
 def shard_kwargs(name: str, rank: int, world: int) -> dict:
     """Size overrides of ``synth.config(name)`` for ``rank``'s shard of the
     BASELINE problem (strong scaling: the shards of all ranks together are
-    the single-GPU problem).  Matmul: a contiguous range of 256-row bands
-    (the CTA-pair tiles' rows); attention: a contiguous range of the
-    B x H = 256 (batch, head) pairs, synthesised as B=1, H=count."""
+    the single-GPU problem): a contiguous range of the configuration's units
+    (``SHARDED``).  Attention shards are synthesised as B=1, H=pairs."""
     dim, total, unit = SHARDED[name]
-    lo, hi = shard_range(total // unit, rank, world)
+    lo, hi = shard_range(total, rank, world)
+    k = hi - lo
+    if dim == "rows":
+        return {"rows": k}
+    if dim == "elements":
+        return {"n": k * unit}
+    if dim == "slices":
+        return {"n": k * unit, "ctas": k}
     if dim == "M":
-        return {"M": (hi - lo) * unit}
-    return {"B": 1, "H": hi - lo}
+        return {"M": k * unit}
+    return {"B": 1, "H": k}
+
+
+def shard_offset(name: str, rank: int, world: int) -> int:
+    """Index of ``rank``'s first row / element / (batch, head) pair in the
+    BASELINE problem."""
+    _, total, unit = SHARDED[name]
+    return shard_range(total, rank, world)[0] * unit
 
 
 def global_sum(partial) -> None:

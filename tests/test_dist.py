@@ -85,19 +85,28 @@ def test_shard_ranges_cover(n, world):
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
 def test_shard_kwargs_cover_the_problem(world):
-    """The per-rank shards of the matmul (256-row bands) and attention
-    ((batch, head) pairs) configurations add up to the BASELINE problem,
-    and every shard's IR is one the tensor-core templates accept."""
+    """The per-rank shards of every strong-scaled configuration add up to the
+    BASELINE problem, back to back from each rank's offset, and every shard's
+    IR is one the templates accept (rows, pointwise, tensor-core kernels)."""
     from emmy_b200 import synth
     from emmy_b200.compiler import compile_graph
-    for name in D.SHARDED:
+    size = {"vector_add": ("n", 1_048_576), "full_sum": ("n", 268_435_456),
+            "row_sum": ("rows", 32768), "row_mean": ("rows", 32768), "rmsnorm": ("rows", 65536),
+            "softmax": ("rows", 65536), "l2norm": ("rows", 65536), "matmul_bf16": ("M", 16384),
+            "matmul_f32": ("M", 16384), "attention": ("H", 256), "attention_d64": ("H", 256)}
+    assert set(size) == set(D.SHARDED)
+    for name, (key, total) in size.items():
         parts = [D.shard_kwargs(name, r, world) for r in range(world)]
+        offs = [D.shard_offset(name, r, world) for r in range(world)]
+        assert sum(p[key] for p in parts) == total
+        assert offs == [sum(p[key] for p in parts[:r]) for r in range(world)]
         if name.startswith("matmul"):
-            assert sum(p["M"] for p in parts) == 16384
             assert all(p["M"] % 256 == 0 for p in parts)
-        else:
-            assert sum(p["B"] * p["H"] for p in parts) == 8 * 32
-    for name in ("matmul_bf16", "attention_d64"):
+        if name == "full_sum":
+            assert all(p["n"] == p["ctas"] * D.SUM_SLICE for p in parts)
+    want = {"vector_add": "pointwise", "full_sum": "rows", "row_mean": "rows", "softmax": "rows",
+            "matmul_bf16": "gemm", "attention_d64": "attention"}
+    for name, kind in want.items():
         kw = D.shard_kwargs(name, world - 1, world)
         g, m = synth.config(name, **kw).build()
-        assert compile_graph(g, m).kind in ("gemm", "attention")
+        assert compile_graph(g, m).kind == kind, name
