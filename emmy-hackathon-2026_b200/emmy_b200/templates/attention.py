@@ -71,6 +71,15 @@ class AttentionTemplate:
     PIPE = (1, 2)
     # wait for the next K block at the top of the MMA thread's block loop
     EARLY_K = True
+    # head dims whose P gets TMEM columns of its own (S_t at 128 t, P_t at
+    # 256 + 64 t, O_t at 384 + D t: 512 columns at D = 64 with two tiles;
+    # correct, measured 679 against 703 TFLOP/s at D = 64, so off by default).
+    # Then each tile's scores are released as soon as the softmax warps hold
+    # them in registers, the next Q K^T runs while the softmax works, and the
+    # softmax of block j+1 starts right after that of block j; P V of block
+    # j overlaps it.  At D = 128 the columns do not fit: P overwrites S and
+    # the tile's next Q K^T waits for its P V.
+    SPLIT_P = {64: False, 128: False}
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -161,6 +170,7 @@ class AttentionTemplate:
         if n < 4:
             raise TemplateMismatch("meta smem_bytes too small for 2+2 K/V stages")
         self.SK, self.SV = (n + 1) // 2, n // 2
+        self.split_p = bool(cls.SPLIT_P.get(D, False)) and self.NT * (128 + 64 + D) <= 512
         return self
 
     # ------------------------------------------------------------------- emit
@@ -224,9 +234,12 @@ class AttentionTemplate:
         V_FULL, V_EMPTY = 1 + 2 * SK, 1 + 2 * SK + SV
         S_FULL = V_EMPTY + SV          # [NT]: scores of tile t ready (tcgen05.commit)
         P_READY = S_FULL + NT          # [NT]: the 4 softmax warps wrote P of tile t
-        FINAL = P_READY + NT           # [NT]: last P V of tile t done
-        DRAIN = FINAL + NT             # the MMA thread's own ops in flight at exit
+        FINAL = P_READY + NT           # [NT]: last P V of tile t done (split P: every
+        #                                P V of tile t done, so its P columns are free)
+        S_FREE = FINAL + NT            # [NT] (split P): the 4 softmax warps read S of tile t
+        DRAIN = S_FREE + NT            # the MMA thread's own ops in flight at exit
         NSLOT = DRAIN + 1
+        split = self.split_p
         assert NSLOT * 8 + 4 <= 512
         tslot = k.reg("r")
         k(f"add.u32 {tslot}, {bars}, {NSLOT * 8};")
@@ -237,7 +250,7 @@ class AttentionTemplate:
         skip = k.label("SKIP_INIT")
         k(f"@!{p0} bra {skip};")
         for slot in range(NSLOT):
-            cnt = 4 if P_READY <= slot < P_READY + NT else 1
+            cnt = 4 if P_READY <= slot < P_READY + NT or S_FREE <= slot < S_FREE + NT else 1
             k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * slot}], {cnt};")
         k("fence.mbarrier_init.release.cluster;")
         for r in (tq, tk, tv):
@@ -396,23 +409,30 @@ class AttentionTemplate:
             k.comment(f"@trace {3 * t} {jreg}")
 
         def issue_pv(t, dv, pacc):
-            """O_t += P_t V (P: the first 64 columns of the score buffer)."""
+            """O_t += P_t V (P: the tile's own 64 columns with split P, else the
+            first 64 columns of the score buffer)."""
             for kk in range(8):                     # 128 keys, K=16 per MMA
                 a = k.reg("r")
-                k(f"add.u32 {a}, {s_tm[t]}, {8 * kk};")  # 16 bf16 = 8 TMEM columns
+                k(f"add.u32 {a}, {p_tm[t]}, {8 * kk};")  # 16 bf16 = 8 TMEM columns
                 bd = k.reg("rd")
                 k(f"add.s64 {bd}, {dv}, {kk * 128};")   # +16 key rows * 128 B
                 k(f"tcgen05.mma.cta_group::1.kind::f16 [{o_tm[t]}], [{a}], {bd}, {ipv}, "
                   f"{pacc if kk == 0 else ptrue};")
 
-        s_tm, o_tm = [], []
+        s_tm, o_tm, p_tm = [], [], []
         for t in range(NT):
             r1 = k.reg("r")
             k(f"add.u32 {r1}, {tmem}, {128 * t};")
             s_tm.append(r1)
             r2 = k.reg("r")
-            k(f"add.u32 {r2}, {tmem}, {256 + D * t};")
+            k(f"add.u32 {r2}, {tmem}, {(128 + 64) * NT + D * t if split else 256 + D * t};")
             o_tm.append(r2)
+            if split:
+                r3 = k.reg("r")
+                k(f"add.u32 {r3}, {tmem}, {128 * NT + 64 * t};")
+                p_tm.append(r3)
+            else:
+                p_tm.append(r1)
         # block 0 scores of every tile
         k(f"mov.u32 {j}, 0;")
         dk0, kst0 = k_ready(j)
@@ -460,6 +480,40 @@ class AttentionTemplate:
             if not last:
                 commit(bar(K_EMPTY, kst))
 
+        def block_split(last: bool):
+            """Split P: the scores of block j+1 for every tile as soon as its
+            softmax warps have read S of block j (they then work from
+            registers), then P V of block j for every tile as its P lands;
+            each P V's commit frees the tile's P columns (and its O) again."""
+            k(f"and.b32 {par}, {j}, 1;")
+            if not last:
+                k(f"add.u32 {jn}, {j}, 1;")
+                dk, kst = k_ready(jn)
+                k.comment(f"@trace 9 {jn}")
+                for t in range(NT):
+                    wait(k, bar(S_FREE + t), par, status, 2, end_mma)
+                    k("tcgen05.fence::after_thread_sync;")
+                    issue_qk(t, dk, jn)
+                commit(bar(K_EMPTY, kst))
+            vst, vph = ring_slot(j, SV)
+            wait(k, bar(V_FULL, vst), vph, status, 2, end_mma)
+            k.comment(f"@trace 8 {j}")
+            k("tcgen05.fence::after_thread_sync;")
+            vad = k.reg("r")
+            k(f"mad.lo.u32 {vad}, {vst}, {TB}, {vring};")
+            dv = GemmTemplate._desc(k, vad, hiV)
+            k(f"setp.ne.u32 {pacc}, {j}, 0;")
+            for t in range(NT):
+                wait(k, bar(P_READY + t), par, status, 2, end_mma)
+                k.comment(f"@trace {3 * t + 1} {j}")
+                k("tcgen05.fence::after_thread_sync;")
+                issue_pv(t, dv, pacc)
+                k.comment(f"@trace {3 * t + 2} {j}")
+                commit(bar(FINAL + t))
+            commit(bar(V_EMPTY, vst))
+
+        if split:
+            block = block_split  # noqa: F811
         if NB > 1:
             top2 = k.label("MMA")
             k.mark(top2)
@@ -495,13 +549,20 @@ class AttentionTemplate:
         k(f"mad.lo.u32 {srow}, {tt}, 128, {trow};")
         orow_tm = k.reg("r")
         k(f"mad.lo.u32 {orow_tm}, {tt}, {D}, {trow};")
-        k(f"add.u32 {orow_tm}, {orow_tm}, 256;")
+        k(f"add.u32 {orow_tm}, {orow_tm}, {(128 + 64) * NT if split else 256};")
+        prow = srow
+        if split:
+            prow = k.reg("r")
+            k(f"mad.lo.u32 {prow}, {tt}, 64, {trow};")
+            k(f"add.u32 {prow}, {prow}, {128 * NT};")
         sfull = k.reg("r")
         k(f"mad.lo.u32 {sfull}, {tt}, 8, {bars};")
         pready = k.reg("r")
         k(f"add.u32 {pready}, {sfull}, {8 * P_READY};")
         fin = k.reg("r")
         k(f"add.u32 {fin}, {sfull}, {8 * FINAL};")
+        sfree = k.reg("r")
+        k(f"add.u32 {sfree}, {sfull}, {8 * S_FREE};")
         k(f"add.u32 {sfull}, {sfull}, {8 * S_FULL};")
         sc = k.reg("f")
         k(f"ld.global.nc.f32 {sc}, [{sbuf}];")
@@ -571,7 +632,7 @@ class AttentionTemplate:
             return packed
 
         def st16(col, pk):
-            k(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{srow}+{col}], {{{', '.join(pk)}}};")
+            k(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{prow}+{col}], {{{', '.join(pk)}}};")
 
         def rescale_o(factor):
             """O row *= factor in TMEM (32 columns at a time)."""
@@ -603,131 +664,143 @@ class AttentionTemplate:
             k(f"add.rn.f32 {s0}, {s0}, {s1};")
             return s0
 
-        # the row's 128 scores stay in registers for the whole block
-        sv = ld32(0) + ld32(32) + ld32(64) + ld32(96)
-        wait_ld()
-        k.comment(f"@trace 12 {j}")
-        ps2 = [k.reg("rd") for _ in range(4)]      # row-sum partials, f32 pairs
-        negm = k.reg("f")
-        negm2 = k.reg("rd")
-        mx = [k.reg("f") for _ in range(8)]
+        if split:
+            self._softmax_split(k, dict(
+                ld32=ld32, wait_ld=wait_ld, st16=st16, rescale_o=rescale_o,
+                p_ready_arrive=p_ready_arrive, row_sum=row_sum, max_into=max_into, sc=sc,
+                sc2=sc2, cst=cst, poly=poly, m=m, lsum=lsum, j=j, top3=top3, sfree=sfree,
+                fin=fin, pl0=pl0, NB=NB, status=status, fail=soft_teardown, wait=wait))
+        else:
+            # the row's 128 scores stay in registers for the whole block
+            sv = ld32(0) + ld32(32) + ld32(64) + ld32(96)
+            wait_ld()
+            k.comment(f"@trace 12 {j}")
+            ps2 = [k.reg("rd") for _ in range(4)]      # row-sum partials, f32 pairs
+            negm = k.reg("f")
+            negm2 = k.reg("rd")
+            mx = [k.reg("f") for _ in range(8)]
 
-        def p_pass(base, fold_max):
-            """P = 2^(s*c - base) of the 128 scores over S columns 0..63 (P of
-            32-column chunk c at 16c), summed into ``ps2``; with ``fold_max``
-            the row max is folded into ``mx`` on the way (it does not feed the
-            exponentials).  One software-pipelined stream over the 64 column
-            pairs: step s issues the scale of pair s+1, the exponentials of
-            pair s, the sum and bf16 pack of pair s-2 and one max, so the FMA
-            and ALU work issues while the MUFU works through the ex2s."""
-            k(f"neg.f32 {negm}, {base};")
-            k(f"mov.b64 {negm2}, {{{negm}, {negm}}};")
-            for r in ps2:
-                k(f"mov.b64 {r}, 0;")
-            LEAD, LAG = self.PIPE
-            t2, es = {}, {}
-            packed = {}
-            maxops = []
-            if fold_max:
-                for i in range(8):
-                    maxops.append((mx[i], sv[i], sv[i + 8], sv[i + 16]))
-                rest = sv[24:]
-                for i in range(0, len(rest), 2):
-                    slot = mx[(i // 2) % 8]
-                    maxops.append((slot, slot, rest[i], rest[i + 1]))
+            def p_pass(base, fold_max):
+                """P = 2^(s*c - base) of the 128 scores over S columns 0..63 (P of
+                32-column chunk c at 16c), summed into ``ps2``; with ``fold_max``
+                the row max is folded into ``mx`` on the way (it does not feed the
+                exponentials).  One software-pipelined stream over the 64 column
+                pairs: step s issues the scale of pair s+1, the exponentials of
+                pair s, the sum and bf16 pack of pair s-2 and one max, so the FMA
+                and ALU work issues while the MUFU works through the ex2s."""
+                k(f"neg.f32 {negm}, {base};")
+                k(f"mov.b64 {negm2}, {{{negm}, {negm}}};")
+                for r in ps2:
+                    k(f"mov.b64 {r}, 0;")
+                LEAD, LAG = self.PIPE
+                t2, es = {}, {}
+                packed = {}
+                maxops = []
+                if fold_max:
+                    for i in range(8):
+                        maxops.append((mx[i], sv[i], sv[i + 8], sv[i + 16]))
+                    rest = sv[24:]
+                    for i in range(0, len(rest), 2):
+                        slot = mx[(i // 2) % 8]
+                        maxops.append((slot, slot, rest[i], rest[i + 1]))
 
-            def stage_a(q):
-                x2 = k.reg("rd")
-                k(f"mov.b64 {x2}, {{{sv[2 * q]}, {sv[2 * q + 1]}}};")
-                k(f"fma.rn.f32x2 {x2}, {x2}, {sc2}, {negm2};")
-                t2[q] = x2
+                def stage_a(q):
+                    x2 = k.reg("rd")
+                    k(f"mov.b64 {x2}, {{{sv[2 * q]}, {sv[2 * q + 1]}}};")
+                    k(f"fma.rn.f32x2 {x2}, {x2}, {sc2}, {negm2};")
+                    t2[q] = x2
 
-            def stage_b(q):
-                e0, e1 = k.reg("f"), k.reg("f")
-                if q % 16 in poly:
-                    self._exp2_poly(k, t2.pop(q), e0, e1, cst)
-                else:
-                    a0, a1 = k.reg("f"), k.reg("f")
-                    k(f"mov.b64 {{{a0}, {a1}}}, {t2.pop(q)};")
-                    k(f"ex2.approx.ftz.f32 {e0}, {a0};")
-                    k(f"ex2.approx.ftz.f32 {e1}, {a1};")
-                es[q] = (e0, e1)
+                def stage_b(q):
+                    e0, e1 = k.reg("f"), k.reg("f")
+                    if q % 16 in poly:
+                        self._exp2_poly(k, t2.pop(q), e0, e1, cst)
+                    else:
+                        a0, a1 = k.reg("f"), k.reg("f")
+                        k(f"mov.b64 {{{a0}, {a1}}}, {t2.pop(q)};")
+                        k(f"ex2.approx.ftz.f32 {e0}, {a0};")
+                        k(f"ex2.approx.ftz.f32 {e1}, {a1};")
+                    es[q] = (e0, e1)
 
-            def stage_c(q):
-                e0, e1 = es.pop(q)
-                e2 = k.reg("rd")
-                k(f"mov.b64 {e2}, {{{e0}, {e1}}};")
-                k(f"add.rn.f32x2 {ps2[q % 4]}, {ps2[q % 4]}, {e2};")
-                c, pi = divmod(q, 16)
-                if pi == 0:
-                    packed[c] = k.regs("r", 16)
-                k(f"cvt.rn.bf16x2.f32 {packed[c][pi]}, {e1}, {e0};")
-                if pi == 15:
-                    st16(16 * c, packed.pop(c))
+                def stage_c(q):
+                    e0, e1 = es.pop(q)
+                    e2 = k.reg("rd")
+                    k(f"mov.b64 {e2}, {{{e0}, {e1}}};")
+                    k(f"add.rn.f32x2 {ps2[q % 4]}, {ps2[q % 4]}, {e2};")
+                    c, pi = divmod(q, 16)
+                    if pi == 0:
+                        packed[c] = k.regs("r", 16)
+                    k(f"cvt.rn.bf16x2.f32 {packed[c][pi]}, {e1}, {e0};")
+                    if pi == 15:
+                        st16(16 * c, packed.pop(c))
 
-            for q in range(LEAD):
-                stage_a(q)
-            for st_ in range(64 + LAG):
-                if st_ + LEAD < 64:
-                    stage_a(st_ + LEAD)
-                if st_ < 64:
-                    stage_b(st_)
-                if st_ - LAG >= 0:
-                    stage_c(st_ - LAG)
-                if maxops:
-                    d_, a_, b_, c_ = maxops.pop(0)
-                    k(f"max.f32 {d_}, {a_}, {b_}, {c_};")
-            assert not maxops and not t2 and not es and not packed
+                for q in range(LEAD):
+                    stage_a(q)
+                for st_ in range(64 + LAG):
+                    if st_ + LEAD < 64:
+                        stage_a(st_ + LEAD)
+                    if st_ < 64:
+                        stage_b(st_)
+                    if st_ - LAG >= 0:
+                        stage_c(st_ - LAG)
+                    if maxops:
+                        d_, a_, b_, c_ = maxops.pop(0)
+                        k(f"max.f32 {d_}, {a_}, {b_}, {c_};")
+                assert not maxops and not t2 and not es and not packed
 
-        # speculative pass against the current base m; it stands unless a row
-        # max grew by more than 2^8 (lazy rescaling: p stays <= 256, and the
-        # final 1/l uses the same base, so this is exact)
-        p_pass(m, True)
-        k(f"max.f32 {mx[0]}, {mx[0]}, {mx[1]}, {mx[2]};")
-        k(f"max.f32 {mx[3]}, {mx[3]}, {mx[4]}, {mx[5]};")
-        k(f"max.f32 {mx[6]}, {mx[6]}, {mx[7]}, {mx[0]};")
-        k(f"max.f32 {mx[0]}, {mx[3]}, {mx[6]};")
-        cand = k.reg("f")
-        k(f"mul.rn.f32 {cand}, {mx[0]}, {sc};")
-        thr = k.reg("f")
-        k(f"add.rn.f32 {thr}, {m}, 0f41000000;")         # m + 8
-        need = k.reg("p")
-        k(f"setp.gt.f32 {need}, {cand}, {thr};")
-        anyw = k.reg("p")
-        k(f"vote.sync.any.pred {anyw}, {need}, 0xffffffff;")
-        fast = k.label("P_FAST")
-        k(f"@!{anyw} bra {fast};")
-        # slow path (always on the first block): new base, P again from the
-        # scores in registers, l and this warp's running O rows rescaled by
-        # 2^(m_old - m_new) (the tile's previous P V completed before its
-        # scores were released; the first block's O is not yet written)
-        meff = k.reg("f")
-        k(f"selp.f32 {meff}, {cand}, {m}, {need};")
-        alpha = k.reg("f")
-        dlt = k.reg("f")
-        k(f"sub.rn.f32 {dlt}, {m}, {meff};")
-        k(f"ex2.approx.ftz.f32 {alpha}, {dlt};")
-        k(f"@!{need} mov.f32 {alpha}, 0f3F800000;")
-        p_pass(meff, False)
-        skip_rs = k.label("NO_RESCALE")
-        pj0 = k.reg("p")
-        k(f"setp.eq.u32 {pj0}, {j}, 0;")
-        k(f"@{pj0} bra {skip_rs};")
-        rescale_o(alpha)
-        k.mark(skip_rs)
-        k(f"mul.rn.f32 {lsum}, {lsum}, {alpha};")
-        k(f"mov.f32 {m}, {meff};")
-        k.mark(fast)
-        p_ready_arrive()
-        k.comment(f"@trace 7 {j}")
-        rsum = row_sum(ps2)
-        k(f"add.rn.f32 {lsum}, {lsum}, {rsum};")
-        k(f"add.u32 {j}, {j}, 1;")
-        pl3 = k.reg("p")
-        k(f"setp.lt.u32 {pl3}, {j}, {NB};")
-        k(f"@{pl3} bra {top3};")
+            # speculative pass against the current base m; it stands unless a row
+            # max grew by more than 2^8 (lazy rescaling: p stays <= 256, and the
+            # final 1/l uses the same base, so this is exact)
+            p_pass(m, True)
+            k(f"max.f32 {mx[0]}, {mx[0]}, {mx[1]}, {mx[2]};")
+            k(f"max.f32 {mx[3]}, {mx[3]}, {mx[4]}, {mx[5]};")
+            k(f"max.f32 {mx[6]}, {mx[6]}, {mx[7]}, {mx[0]};")
+            k(f"max.f32 {mx[0]}, {mx[3]}, {mx[6]};")
+            cand = k.reg("f")
+            k(f"mul.rn.f32 {cand}, {mx[0]}, {sc};")
+            thr = k.reg("f")
+            k(f"add.rn.f32 {thr}, {m}, 0f41000000;")         # m + 8
+            need = k.reg("p")
+            k(f"setp.gt.f32 {need}, {cand}, {thr};")
+            anyw = k.reg("p")
+            k(f"vote.sync.any.pred {anyw}, {need}, 0xffffffff;")
+            fast = k.label("P_FAST")
+            k(f"@!{anyw} bra {fast};")
+            # slow path (always on the first block): new base, P again from the
+            # scores in registers, l and this warp's running O rows rescaled by
+            # 2^(m_old - m_new) (the tile's previous P V completed before its
+            # scores were released; the first block's O is not yet written)
+            meff = k.reg("f")
+            k(f"selp.f32 {meff}, {cand}, {m}, {need};")
+            alpha = k.reg("f")
+            dlt = k.reg("f")
+            k(f"sub.rn.f32 {dlt}, {m}, {meff};")
+            k(f"ex2.approx.ftz.f32 {alpha}, {dlt};")
+            k(f"@!{need} mov.f32 {alpha}, 0f3F800000;")
+            p_pass(meff, False)
+            skip_rs = k.label("NO_RESCALE")
+            pj0 = k.reg("p")
+            k(f"setp.eq.u32 {pj0}, {j}, 0;")
+            k(f"@{pj0} bra {skip_rs};")
+            rescale_o(alpha)
+            k.mark(skip_rs)
+            k(f"mul.rn.f32 {lsum}, {lsum}, {alpha};")
+            k(f"mov.f32 {m}, {meff};")
+            k.mark(fast)
+            p_ready_arrive()
+            k.comment(f"@trace 7 {j}")
+            rsum = row_sum(ps2)
+            k(f"add.rn.f32 {lsum}, {lsum}, {rsum};")
+            k(f"add.u32 {j}, {j}, 1;")
+            pl3 = k.reg("p")
+            k(f"setp.lt.u32 {pl3}, {j}, {NB};")
+            k(f"@{pl3} bra {top3};")
         # epilogue: O row * (1 / l) -> global
-        wait(k, fin, self._zero(k), status, 3, soft_teardown)
+        if split:
+            # the tile's P_FREE barrier completes once per block: the last
+            # completion is the last P V
+            wait(k, fin, (NB - 1) & 1, status, 3, soft_teardown)
+        else:
+            wait(k, fin, self._zero(k), status, 3, soft_teardown)
         k("tcgen05.fence::after_thread_sync;")
         inv = k.reg("f")
         k(f"rcp.rn.f32 {inv}, {lsum};")
@@ -766,6 +839,130 @@ class AttentionTemplate:
         k.mark(end)
         k("ret;")
         return k.render()
+
+    def _softmax_split(self, k, e):
+        """The softmax warps' block body with split P (one thread per query
+        row; S of block j already waited for):
+
+        * the row's 128 scores are read from TMEM into registers and S is
+          released at once (one arrival per warp on the tile's S_FREE), so the
+          next block's Q K^T runs while this block's softmax works;
+        * the row max, then the exponent base: it moves to the new max only
+          when that exceeds it by more than 2^8 (lazy rescaling; always on the
+          first block), with ``alpha = 2^(m_old - m_new)`` (exactly 1 for rows
+          that keep their base);
+        * ``p = 2^(s*c - m)`` of all 128 scores into 64 packed bf16 pairs held
+          in registers, summed on the way;
+        * the tile's previous P V must be complete before its P columns and O
+          rows are touched (the tile's P_FREE barrier, one completion per
+          block); then the O rows are rescaled by alpha if any row of the warp
+          moved its base (never on the first block, before any P V), P is
+          stored and the warp arrives on P_READY;
+        * l = l * alpha + the row sum."""
+        j, m, lsum = e["j"], e["m"], e["lsum"]
+        sv = e["ld32"](0) + e["ld32"](32) + e["ld32"](64) + e["ld32"](96)
+        e["wait_ld"]()
+        k("tcgen05.fence::before_thread_sync;")
+        k("bar.warp.sync 0xffffffff;")
+        k(f"@{e['pl0']} mbarrier.arrive.shared::cta.b64 _, [{e['sfree']}];")
+        k.comment(f"@trace 12 {j}")
+        # row max: eight partial maxima (3-input max), then folded
+        mx = [k.reg("f") for _ in range(8)]
+        e["max_into"](mx, sv, True)
+        k(f"max.f32 {mx[0]}, {mx[0]}, {mx[1]}, {mx[2]};")
+        k(f"max.f32 {mx[3]}, {mx[3]}, {mx[4]}, {mx[5]};")
+        k(f"max.f32 {mx[6]}, {mx[6]}, {mx[7]}, {mx[0]};")
+        k(f"max.f32 {mx[0]}, {mx[3]}, {mx[6]};")
+        k.comment(f"@trace 13 {j}")
+        cand = k.reg("f")
+        k(f"mul.rn.f32 {cand}, {mx[0]}, {e['sc']};")
+        thr = k.reg("f")
+        k(f"add.rn.f32 {thr}, {m}, 0f41000000;")         # m + 8
+        need = k.reg("p")
+        k(f"setp.gt.f32 {need}, {cand}, {thr};")
+        anyw = k.reg("p")
+        k(f"vote.sync.any.pred {anyw}, {need}, 0xffffffff;")
+        meff = k.reg("f")
+        k(f"selp.f32 {meff}, {cand}, {m}, {need};")
+        alpha = k.reg("f")
+        dlt = k.reg("f")
+        k(f"sub.rn.f32 {dlt}, {m}, {meff};")           # 0 for rows that keep m
+        k(f"ex2.approx.ftz.f32 {alpha}, {dlt};")
+        k(f"mov.f32 {m}, {meff};")
+        negm = k.reg("f")
+        k(f"neg.f32 {negm}, {m};")
+        negm2 = k.reg("rd")
+        k(f"mov.b64 {negm2}, {{{negm}, {negm}}};")
+        ps2 = [k.reg("rd") for _ in range(4)]      # row-sum partials, f32 pairs
+        for r in ps2:
+            k(f"mov.b64 {r}, 0;")
+        LEAD, LAG = self.PIPE
+        poly, cst, sc2 = e["poly"], e["cst"], e["sc2"]
+        t2, es, packed = {}, {}, []
+
+        def stage_a(q):
+            x2 = k.reg("rd")
+            k(f"mov.b64 {x2}, {{{sv[2 * q]}, {sv[2 * q + 1]}}};")
+            k(f"fma.rn.f32x2 {x2}, {x2}, {sc2}, {negm2};")
+            t2[q] = x2
+
+        def stage_b(q):
+            e0, e1 = k.reg("f"), k.reg("f")
+            if q % 16 in poly:
+                self._exp2_poly(k, t2.pop(q), e0, e1, cst)
+            else:
+                a0, a1 = k.reg("f"), k.reg("f")
+                k(f"mov.b64 {{{a0}, {a1}}}, {t2.pop(q)};")
+                k(f"ex2.approx.ftz.f32 {e0}, {a0};")
+                k(f"ex2.approx.ftz.f32 {e1}, {a1};")
+            es[q] = (e0, e1)
+
+        def stage_c(q):
+            e0, e1 = es.pop(q)
+            e2 = k.reg("rd")
+            k(f"mov.b64 {e2}, {{{e0}, {e1}}};")
+            k(f"add.rn.f32x2 {ps2[q % 4]}, {ps2[q % 4]}, {e2};")
+            pk = k.reg("r")
+            k(f"cvt.rn.bf16x2.f32 {pk}, {e1}, {e0};")
+            packed.append(pk)
+
+        for q in range(LEAD):
+            stage_a(q)
+        for st_ in range(64 + LAG):
+            if st_ + LEAD < 64:
+                stage_a(st_ + LEAD)
+            if st_ < 64:
+                stage_b(st_)
+            if st_ - LAG >= 0:
+                stage_c(st_ - LAG)
+        assert not t2 and not es and len(packed) == 64
+        k.comment(f"@trace 14 {j}")
+        # the tile's previous P V is done: its P columns and O rows are free
+        skip_w = k.label("FIRST_BLOCK")
+        pj0 = k.reg("p")
+        k(f"setp.eq.u32 {pj0}, {j}, 0;")
+        k(f"@{pj0} bra {skip_w};")
+        fpar = k.reg("r")
+        k(f"add.u32 {fpar}, {j}, 1;")               # completion j-1: parity (j-1) & 1
+        k(f"and.b32 {fpar}, {fpar}, 1;")
+        e["wait"](k, e["fin"], fpar, e["status"], 3, e["fail"])
+        k("tcgen05.fence::after_thread_sync;")
+        no_rs = k.label("NO_RESCALE")
+        k(f"@!{anyw} bra {no_rs};")
+        e["rescale_o"](alpha)
+        k.mark(no_rs)
+        k.mark(skip_w)
+        k.comment(f"@trace 15 {j}")
+        for c in range(4):
+            e["st16"](16 * c, packed[16 * c:16 * c + 16])
+        e["p_ready_arrive"]()
+        k.comment(f"@trace 7 {j}")
+        rsum = e["row_sum"](ps2)
+        k(f"fma.rn.f32 {lsum}, {lsum}, {alpha}, {rsum};")
+        k(f"add.u32 {j}, {j}, 1;")
+        pl3 = k.reg("p")
+        k(f"setp.lt.u32 {pl3}, {j}, {e['NB']};")
+        k(f"@{pl3} bra {e['top3']};")
 
     def poly_pairs(self) -> set:
         """Which of the 16 column pairs of a 32-column chunk take the FMA-pipe
