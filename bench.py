@@ -942,6 +942,55 @@ CATEGORY_CASES = ["vector_add", "vector_add_large", "rmsnorm", "softmax", "l2nor
                   "matmul_f32", "attention", "attention_d64"]
 
 
+# the reference's own published kernel times for its open problems (H200,
+# docs/ATTRIBUTION_PLAYBOOK.md:271-274 of the reference), for comparison only
+PUBLISHED_H200_US = {"m01_matmul_512": 15.04, "a01_attention": 47.78, "r03_mean": 6.848,
+                     "r02_big_sum": 15.73}
+
+
+def run_problems(args) -> None:
+    """``--problems``: the reference's 15 open problems (their own IRs, meta
+    and expected.npz) through this build's compiler and through the
+    reference compiler's PTX for the same IRs (``oracle/_ref/problems``),
+    both on this GPU: every kernel checked against expected.npz within the
+    problem's rtol/atol, then timed (``--steps`` launches back to back, CUDA
+    events around each, median).  One JSON line."""
+    import torch
+    from emmy_b200 import native, problem
+    torch.cuda.set_device(0)
+    native.check(native.lib().emmy_device_init(0))
+    rows = {}
+    root = REPO / "tests" / "golden" / "problems"
+    for folder in sorted(p for p in root.iterdir() if (p / "meta.json").exists()):
+        pid = folder.name
+        row = {}
+        for arm in ("ours", "reference_ptx"):
+            if arm == "ours":
+                rep = problem.run_problem(folder, out=lambda s_: None, time_launches=True,
+                                          iters=args.steps)
+            else:
+                rdir = REPO / "oracle" / "_ref" / "problems" / pid
+                if not rdir.exists():
+                    continue
+                rep = problem.run_problem(
+                    folder, ptx_for=lambda k_, ir_: (rdir / f"{k_['entry']}.ptx").read_text(),
+                    out=lambda s_: None, time_launches=True, iters=args.steps)
+            ks = rep["kernels"]
+            row[arm] = {"ok": bool(rep["ok"]),
+                        "kernels": [{"entry": k_["entry"], "kind": k_["kind"],
+                                     "us": round(k_["us"], 3) if k_["us"] else None} for k_ in ks],
+                        "us": round(sum(k_["us"] or 0 for k_ in ks), 3) if rep["ok"] else None}
+        if row.get("ours", {}).get("us") and row.get("reference_ptx", {}).get("us"):
+            row["speedup_vs_reference_ptx"] = round(row["reference_ptx"]["us"] / row["ours"]["us"], 2)
+        if pid in PUBLISHED_H200_US:
+            row["reference_published_h200_us"] = PUBLISHED_H200_US[pid]
+        rows[pid] = row
+    print(json.dumps({"problems": rows, "launches_timed": args.steps,
+                      "protocol": "inputs resident; one checked launch, then back-to-back "
+                                  "launches with CUDA events around each, no L2 flush "
+                                  "(the inputs are at most 1 MiB)"}), flush=True)
+
+
 def run_case(args) -> None:
     """``--case`` (sizes from ``--size k=v,..``): one JSON line for one
     configuration (per-category numbers; small ncu captures)."""
@@ -968,6 +1017,8 @@ def main():
     ap.add_argument("--size", default=None, help="size overrides for --case, k=v,k=v")
     ap.add_argument("--no-categories", action="store_true",
                     help="skip the per-category kernels after the headline workload")
+    ap.add_argument("--problems", action="store_true",
+                    help="time the reference's 15 open problems, ours and the reference PTX")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -976,6 +1027,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.case:
         run_case(args)
+        return
+    if args.problems:
+        run_problems(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

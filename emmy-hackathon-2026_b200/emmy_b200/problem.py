@@ -74,13 +74,15 @@ def not_ptx(ptx: str) -> str | None:
 
 
 def run_problem(folder, ptx_for=None, out=print, time_launches: bool = False,
-                device: str = "cuda") -> dict:
+                device: str = "cuda", iters: int = 5) -> dict:
     """Run every kernel of the problem in ``folder`` once, in meta order.
 
     ``ptx_for(kernel_info, ir_path) -> str`` supplies each kernel's PTX; by
     default the kernels are compiled in-process.  Returns ``{"ok": bool,
     "kernels": [...], "outputs": {name: ndarray}}``; ``out`` receives one line
-    per checked output (``[entry] PASS name: max abs err ...``)."""
+    per checked output (``[entry] PASS name: max abs err ...``).  With
+    ``time_launches`` each kernel is also timed, ``iters`` launches back to
+    back (CUDA events around each, median), after the checked launch."""
     import torch
     folder = Path(folder)
     meta = json.loads((folder / "meta.json").read_text())
@@ -142,7 +144,7 @@ def run_problem(folder, ptx_for=None, out=print, time_launches: bool = False,
         torch.cuda.synchronize()
         us = None
         if time_launches:
-            ms = kern.time(ptrs, warmup=1, iters=5, stream=stream, zero=zero)
+            ms = kern.time(ptrs, warmup=1, iters=iters, stream=stream, zero=zero)
             us = float(np.median(ms)) * 1e3
         report["kernels"].append({"entry": entry, "kind": kern.kind, "us": us})
         for a in k["args"]:

@@ -122,3 +122,24 @@ def emit_reference_ptx(name: str, graph_dict: dict, meta: dict) -> Path:
     out = REF_OUT / f"{name}.ptx"
     out.write_bytes(reference_ptx(g, m).encode())
     return out
+
+
+def emit_problem_ptx(folder) -> list:
+    """Write the reference's PTX for every kernel of a problem folder (IR
+    files named ``<entry>.ir.json`` or ``kernel.ir.json``, ``meta.json``
+    beside them) to ``oracle/_ref/problems/<problem>/<entry>.ptx``, entry
+    names unchanged (so the PTX launches under the problem's own meta)."""
+    folder = Path(folder)
+    meta = json.loads((folder / "meta.json").read_text())
+    out_dir = REF_OUT / "problems" / folder.name
+    out_dir.mkdir(parents=True, exist_ok=True)
+    written = []
+    for kinfo in meta["kernels"]:
+        ir_path = folder / f"{kinfo['entry']}.ir.json"
+        if not ir_path.exists():
+            ir_path = folder / "kernel.ir.json"
+        ptx = reference_ptx(json.loads(ir_path.read_text()), meta)
+        out = out_dir / f"{kinfo['entry']}.ptx"
+        out.write_bytes(ptx.encode())
+        written.append(out)
+    return written
