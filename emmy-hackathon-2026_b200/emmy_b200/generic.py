@@ -20,8 +20,12 @@ IR order, one PTX sequence per statement, with the reference's semantics:
 * ``Sync``: barrier 0 is CTA-wide (its count is ignored, as Emmy renders
   ``__syncthreads()``), named barriers take their count, ``warp`` syncs the warp.
 
-It emits plain loops (no unrolling) and scalar memory accesses: correctness
-first; the templates are the fast paths.
+Loops with a static trip count of at most ``UNROLL_CAP`` and no nested loop
+are unrolled, the loop variable bound to each constant in turn, and an f32
+``multiply`` whose only use is the next statement's ``Accum`` add becomes one
+``fma.rn.f32`` -- the reference's own two speed rules (``compile.py:1882-1928``,
+``2244-2264``); every other loop stays a plain loop, and memory accesses are
+scalar: correctness first; the templates are the fast paths.
 """
 from __future__ import annotations
 
@@ -443,8 +447,68 @@ class GenericLowering:
 
     # --------------------------------------------------------- statements
     def body(self, stmts):
-        for s in stmts:
+        stmts = list(stmts)
+        uses = self._uses(stmts)
+        i = 0
+        while i < len(stmts):
+            s = stmts[i]
+            nxt = stmts[i + 1] if i + 1 < len(stmts) else None
+            if (kind(s) == "Assign" and s.op.name == "multiply" and len(s.args) == 2
+                    and uses.get(s.name, 0) == 1 and nxt is not None
+                    and kind(nxt) == "Accum" and nxt.value == s.name and nxt.op.name == "add"
+                    and (nxt.dtype is None or nxt.dtype.name == "f32")
+                    and all(self.vals.get(a, (None, ""))[1] == "f32" for a in s.args)):
+                # acc = acc + a*b in one rounding, as the reference contracts it
+                reg, ty = self.accum_reg(nxt)
+                if ty == "f32":
+                    left = self.vals[nxt.base][0] if nxt.base else reg
+                    a, b = (self.vals[x][0] for x in s.args)
+                    self.k(f"fma.rn.f32 {reg}, {a}, {b}, {left};")
+                    self.vals[nxt.name] = (reg, ty)
+                    i += 2
+                    continue
             getattr(self, "s_" + kind(s), self.s_unsupported)(s)
+            i += 1
+
+    @staticmethod
+    def _uses(stmts) -> dict:
+        """How often each name is read in ``stmts`` (nested bodies included):
+        operand names of statements and variables of their expressions
+        (conditions, indices, loop bounds)."""
+        out: dict = {}
+
+        def count(n):
+            out[n] = out.get(n, 0) + 1
+
+        def expr(e):
+            if e is None or isinstance(e, (int, float)):
+                return
+            if isinstance(e, tuple):
+                for x in e:
+                    expr(x)
+                return
+            fv = getattr(e, "free_vars", None)
+            if fv is not None:
+                for n in fv():
+                    count(n)
+        for st in walk(stmts):
+            for a in getattr(st, "args", ()) or ():
+                if isinstance(a, str):
+                    count(a)
+                else:
+                    expr(a)
+            for f in ("value", "base"):
+                v = getattr(st, f, None)
+                if isinstance(v, str):
+                    count(v)
+                else:
+                    expr(v)
+            for v in getattr(st, "values", ()) or ():
+                if isinstance(v, str):
+                    count(v)
+            for f in ("cond", "index", "src_index", "smem_index", "start", "step", "end"):
+                expr(getattr(st, f, None))
+        return out
 
     def s_unsupported(self, s):
         raise NotImplementedError(f"statement {kind(s)}")
@@ -652,12 +716,37 @@ class GenericLowering:
                     if sub:
                         self.init_accumulators(sub)
 
+    UNROLL_CAP = 128
+
     def _loop(self, axis, start, step, end, body, seed):
         k = self.k
         if seed:
             self.init_accumulators(body)
         name = axis.name
         saved = self.ints.get(name)
+        if _is_imm(start) and _is_imm(step) and _is_imm(end) and int(step) > 0:
+            trip = max(0, -(-(int(end) - int(start)) // int(step)))
+            if 1 < trip <= self.UNROLL_CAP and not any(
+                    kind(x) in ("Loop", "StridedLoop") for x in walk(body)):
+                # one copy of the body per iteration, the axis a constant.
+                # Each copy starts from the bindings the loop form's body
+                # sees on every iteration (those made before the loop), so
+                # what the loop form re-executes per iteration (lazily
+                # initialised accumulators, rebindings) is re-executed by
+                # every copy; accumulators keep their registers, so their
+                # state carries from copy to copy as from iteration to
+                # iteration, and after the loop the last copy's bindings hold
+                before_v, before_i = dict(self.vals), dict(self.ints)
+                for it in range(trip):
+                    self.vals = dict(before_v)
+                    self.ints = dict(before_i)
+                    self.ints[name] = str(int(start) + it * int(step))
+                    self.body(body)
+                if saved is None:
+                    self.ints.pop(name, None)
+                else:
+                    self.ints[name] = saved
+                return
         v = k.reg("r")
         k(f"mov.u32 {v}, {start};")
         top, out = k.label("LOOP"), k.label("ENDLOOP")

@@ -72,14 +72,17 @@ class AttentionTemplate:
     # wait for the next K block at the top of the MMA thread's block loop
     EARLY_K = True
     # head dims whose P gets TMEM columns of its own (S_t at 128 t, P_t at
-    # 256 + 64 t, O_t at 384 + D t: 512 columns at D = 64 with two tiles;
-    # correct, measured 679 against 703 TFLOP/s at D = 64, so off by default).
+    # 256 + 64 t, O_t at 384 + D t: 512 columns at D = 64 with two tiles).
+    # The tiles then share their barriers and the MMA thread commits twice
+    # per block (a commit costs the issuing thread about 100 cycles): at
+    # D = 64 712 TFLOP/s against 703 with P over S (with per-tile barriers
+    # and six commits per block the same split measured 679).
     # Then each tile's scores are released as soon as the softmax warps hold
     # them in registers, the next Q K^T runs while the softmax works, and the
     # softmax of block j+1 starts right after that of block j; P V of block
     # j overlaps it.  At D = 128 the columns do not fit: P overwrites S and
     # the tile's next Q K^T waits for its P V.
-    SPLIT_P = {64: False, 128: False}
+    SPLIT_P = {64: True, 128: False}
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -234,12 +237,20 @@ class AttentionTemplate:
         V_FULL, V_EMPTY = 1 + 2 * SK, 1 + 2 * SK + SV
         S_FULL = V_EMPTY + SV          # [NT]: scores of tile t ready (tcgen05.commit)
         P_READY = S_FULL + NT          # [NT]: the 4 softmax warps wrote P of tile t
-        FINAL = P_READY + NT           # [NT]: last P V of tile t done (split P: every
-        #                                P V of tile t done, so its P columns are free)
-        S_FREE = FINAL + NT            # [NT] (split P): the 4 softmax warps read S of tile t
-        DRAIN = S_FREE + NT            # the MMA thread's own ops in flight at exit
-        NSLOT = DRAIN + 1
+        FINAL = P_READY + NT           # [NT]: last P V of tile t done
         split = self.split_p
+        # split P: the tiles share S_FULL, P_READY (4 NT arrivals) and S_FREE
+        # (4 NT arrivals: every softmax warp has read its S), and one commit
+        # per block on DONE[j % R] marks block j's P V (and, MMAs completing in
+        # order, the Q K^T of block j+1 before it) complete: the K and V
+        # producers, the softmax's reuse of P and O and the epilogue all wait
+        # on that ring (R >= each ring's depth keeps their waits within one
+        # phase of the barrier they read)
+        S_FREE = FINAL + NT
+        R = max(SK, SV)
+        DONE = S_FREE + NT
+        DRAIN = DONE + (R if split else 0)   # the MMA thread's own ops in flight at exit
+        NSLOT = DRAIN + 1
         assert NSLOT * 8 + 4 <= 512
         tslot = k.reg("r")
         k(f"add.u32 {tslot}, {bars}, {NSLOT * 8};")
@@ -250,7 +261,11 @@ class AttentionTemplate:
         skip = k.label("SKIP_INIT")
         k(f"@!{p0} bra {skip};")
         for slot in range(NSLOT):
-            cnt = 4 if P_READY <= slot < P_READY + NT or S_FREE <= slot < S_FREE + NT else 1
+            if split:
+                cnt = 4 * NT if slot in (P_READY, S_FREE) else 1
+            else:
+                cnt = 4 if P_READY <= slot < P_READY + NT else 1
+
             k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * slot}], {cnt};")
         k("fence.mbarrier_init.release.cluster;")
         for r in (tq, tk, tv):
@@ -337,9 +352,24 @@ class AttentionTemplate:
             top = k.label(f"PROD_{which}")
             k.mark(top)
             st_, ph_ = ring_slot(j, depth)
-            par = k.reg("r")
-            k(f"xor.b32 {par}, {ph_}, 1;")
-            wait(k, bar(empty, st_), par, status, 1, end_p)
+            if split:
+                # the stage's previous block b = j - depth is free once the
+                # P V iteration that last read it is done: V(b) -> DONE(b);
+                # K(b) (read by the Q K^T of iteration b-1) -> DONE(max(b-1, 0))
+                nowait = k.label(f"NOWAIT_{which}")
+                pf = k.reg("p")
+                k(f"setp.lt.u32 {pf}, {j}, {depth};")
+                k(f"@{pf} bra {nowait};")
+                n_ = k.reg("r")
+                k(f"sub.u32 {n_}, {j}, {depth + (1 if which == 'K' else 0)};")
+                k(f"max.s32 {n_}, {n_}, 0;")
+                ds, dph = ring_slot(n_, R)
+                wait(k, bar(DONE, ds), dph, status, 1, end_p)
+                k.mark(nowait)
+            else:
+                par = k.reg("r")
+                k(f"xor.b32 {par}, {ph_}, 1;")
+                wait(k, bar(empty, st_), par, status, 1, end_p)
             kr = k.reg("r")
             k(f"mad.lo.u32 {kr}, {j}, 128, {krow0};")
             dst = k.reg("r")
@@ -395,7 +425,7 @@ class AttentionTemplate:
             k(f"mad.lo.u32 {kad}, {kst}, {TB}, {kring};")
             return GemmTemplate._desc(k, kad, hiK), kst
 
-        def issue_qk(t, dk, jreg):
+        def issue_qk(t, dk, jreg, do_commit=True):
             """S_t = Q_t K^T (overwrites the tile's score buffer)."""
             for kk in range(D // 16):
                 off = (kk % 4) * 2 + (kk // 4) * 1024
@@ -405,7 +435,8 @@ class AttentionTemplate:
                 k(f"add.s64 {bd}, {dk}, {off};")
                 k(f"tcgen05.mma.cta_group::1.kind::f16 [{s_tm[t]}], {a}, {bd}, {iqk}, "
                   f"{pfalse if kk == 0 else ptrue};")
-            commit(bar(S_FULL + t))
+            if do_commit:
+                commit(bar(S_FULL + t))
             k.comment(f"@trace {3 * t} {jreg}")
 
         def issue_pv(t, dv, pacc):
@@ -437,8 +468,11 @@ class AttentionTemplate:
         k(f"mov.u32 {j}, 0;")
         dk0, kst0 = k_ready(j)
         for t in range(NT):
-            issue_qk(t, dk0, j)
-        commit(bar(K_EMPTY, kst0))
+            issue_qk(t, dk0, j, not split)
+        if split:
+            commit(bar(S_FULL))
+        else:
+            commit(bar(K_EMPTY, kst0))
         jn = k.reg("r")
         pacc = k.reg("p")
         par = k.reg("r")
@@ -481,36 +515,37 @@ class AttentionTemplate:
                 commit(bar(K_EMPTY, kst))
 
         def block_split(last: bool):
-            """Split P: the scores of block j+1 for every tile as soon as its
-            softmax warps have read S of block j (they then work from
-            registers), then P V of block j for every tile as its P lands;
-            each P V's commit frees the tile's P columns (and its O) again."""
+            """Split P: once every softmax warp has read S of block j, the
+            scores of block j+1 for both tiles (one commit on the shared
+            S_FULL); once every softmax warp has stored P of block j, P V of
+            block j for both tiles and one commit on DONE[j % R]."""
             k(f"and.b32 {par}, {j}, 1;")
             if not last:
                 k(f"add.u32 {jn}, {j}, 1;")
                 dk, kst = k_ready(jn)
                 k.comment(f"@trace 9 {jn}")
+                wait(k, bar(S_FREE), par, status, 2, end_mma)
+                k("tcgen05.fence::after_thread_sync;")
                 for t in range(NT):
-                    wait(k, bar(S_FREE + t), par, status, 2, end_mma)
-                    k("tcgen05.fence::after_thread_sync;")
-                    issue_qk(t, dk, jn)
-                commit(bar(K_EMPTY, kst))
+                    issue_qk(t, dk, jn, False)
+                k.comment(f"@trace 0 {jn}")
+                commit(bar(S_FULL))
             vst, vph = ring_slot(j, SV)
             wait(k, bar(V_FULL, vst), vph, status, 2, end_mma)
             k.comment(f"@trace 8 {j}")
-            k("tcgen05.fence::after_thread_sync;")
             vad = k.reg("r")
             k(f"mad.lo.u32 {vad}, {vst}, {TB}, {vring};")
             dv = GemmTemplate._desc(k, vad, hiV)
             k(f"setp.ne.u32 {pacc}, {j}, 0;")
+            wait(k, bar(P_READY), par, status, 2, end_mma)
+            k.comment(f"@trace 1 {j}")
+            k("tcgen05.fence::after_thread_sync;")
             for t in range(NT):
-                wait(k, bar(P_READY + t), par, status, 2, end_mma)
-                k.comment(f"@trace {3 * t + 1} {j}")
-                k("tcgen05.fence::after_thread_sync;")
                 issue_pv(t, dv, pacc)
-                k.comment(f"@trace {3 * t + 2} {j}")
-                commit(bar(FINAL + t))
-            commit(bar(V_EMPTY, vst))
+            k.comment(f"@trace 2 {j}")
+            ds_ = k.reg("r")
+            k(f"rem.u32 {ds_}, {j}, {R};")
+            commit(bar(DONE, ds_))
 
         if split:
             block = block_split  # noqa: F811
@@ -564,6 +599,11 @@ class AttentionTemplate:
         sfree = k.reg("r")
         k(f"add.u32 {sfree}, {sfull}, {8 * S_FREE};")
         k(f"add.u32 {sfull}, {sfull}, {8 * S_FULL};")
+        if split:     # barriers shared by the tiles; fin = the DONE ring
+            k(f"add.u32 {pready}, {bars}, {8 * P_READY};")
+            k(f"add.u32 {sfree}, {bars}, {8 * S_FREE};")
+            k(f"add.u32 {sfull}, {bars}, {8 * S_FULL};")
+            k(f"add.u32 {fin}, {bars}, {8 * DONE};")
         sc = k.reg("f")
         k(f"ld.global.nc.f32 {sc}, [{sbuf}];")
         k(f"rcp.rn.f32 {sc}, {sc};")
@@ -669,7 +709,7 @@ class AttentionTemplate:
                 ld32=ld32, wait_ld=wait_ld, st16=st16, rescale_o=rescale_o,
                 p_ready_arrive=p_ready_arrive, row_sum=row_sum, max_into=max_into, sc=sc,
                 sc2=sc2, cst=cst, poly=poly, m=m, lsum=lsum, j=j, top3=top3, sfree=sfree,
-                fin=fin, pl0=pl0, NB=NB, status=status, fail=soft_teardown, wait=wait))
+                fin=fin, pl0=pl0, NB=NB, R=R, status=status, fail=soft_teardown, wait=wait))
         else:
             # the row's 128 scores stay in registers for the whole block
             sv = ld32(0) + ld32(32) + ld32(64) + ld32(96)
@@ -796,9 +836,10 @@ class AttentionTemplate:
             k(f"@{pl3} bra {top3};")
         # epilogue: O row * (1 / l) -> global
         if split:
-            # the tile's P_FREE barrier completes once per block: the last
-            # completion is the last P V
-            wait(k, fin, (NB - 1) & 1, status, 3, soft_teardown)
+            # the last block's P V: DONE[(NB-1) % R], its ((NB-1) // R)-th completion
+            fl = k.reg("r")
+            k(f"add.u32 {fl}, {fin}, {8 * ((NB - 1) % R)};")
+            wait(k, fl, ((NB - 1) // R) & 1, status, 3, soft_teardown)
         else:
             wait(k, fin, self._zero(k), status, 3, soft_teardown)
         k("tcgen05.fence::after_thread_sync;")
@@ -942,10 +983,16 @@ class AttentionTemplate:
         pj0 = k.reg("p")
         k(f"setp.eq.u32 {pj0}, {j}, 0;")
         k(f"@{pj0} bra {skip_w};")
+        jp = k.reg("r")
+        k(f"sub.u32 {jp}, {j}, 1;")                  # DONE of block j-1
+        ds = k.reg("r")
+        k(f"rem.u32 {ds}, {jp}, {e['R']};")
         fpar = k.reg("r")
-        k(f"add.u32 {fpar}, {j}, 1;")               # completion j-1: parity (j-1) & 1
+        k(f"div.u32 {fpar}, {jp}, {e['R']};")
         k(f"and.b32 {fpar}, {fpar}, 1;")
-        e["wait"](k, e["fin"], fpar, e["status"], 3, e["fail"])
+        fa = k.reg("r")
+        k(f"mad.lo.u32 {fa}, {ds}, 8, {e['fin']};")
+        e["wait"](k, fa, fpar, e["status"], 3, e["fail"])
         k("tcgen05.fence::after_thread_sync;")
         no_rs = k.label("NO_RESCALE")
         k(f"@!{anyw} bra {no_rs};")

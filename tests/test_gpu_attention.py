@@ -81,12 +81,14 @@ def test_attention_growing_scores(kw):
                                 dict(B=2, H=1, S=1024, D=64)],
                          ids=["d64_bm256", "d64_bm128", "d64_long"])
 @pytest.mark.parametrize("ramp", [False, True], ids=["plain", "growing"])
-def test_attention_split_p(kw, ramp, monkeypatch):
-    """P in TMEM columns of its own (scores released as soon as the softmax
-    warps hold them; the next Q K^T overlaps the softmax; each P V's commit
-    frees the tile's P columns and O rows): the same oracle bounds, also when
-    the exponent base moves inside blocks (O rescaled after the previous P V
-    completed)."""
+@pytest.mark.parametrize("split", [True, False], ids=["split", "p_over_s"])
+def test_attention_split_p(kw, ramp, split, monkeypatch):
+    """Both d=64 forms: P in TMEM columns of its own (scores released as soon
+    as the softmax warps hold them, the next Q K^T overlapping the softmax,
+    one commit per block freeing P, O and the K/V stages), and P over S.
+    The same oracle bounds, also when the exponent base moves inside blocks
+    (O rescaled after the previous P V completed)."""
     from emmy_b200.templates import attention
-    monkeypatch.setattr(attention.AttentionTemplate, "SPLIT_P", {64: True, 128: False})
+    monkeypatch.setattr(attention.AttentionTemplate, "SPLIT_P", {64: split, 128: False})
     _run(synth.attention(**kw), transform=_key_ramp if ramp else None)
+
