@@ -2,10 +2,11 @@
 from .attention import AttentionTemplate
 from .common import TemplateMismatch
 from .gemm import GemmTemplate
+from .gemm_small import GemmSmallTemplate
 from .pointwise import PointwiseTemplate
 from .rows import RowsTemplate
 
-TEMPLATES = [PointwiseTemplate, RowsTemplate, GemmTemplate, AttentionTemplate]
+TEMPLATES = [PointwiseTemplate, RowsTemplate, GemmTemplate, GemmSmallTemplate, AttentionTemplate]
 
 __all__ = ["TEMPLATES", "TemplateMismatch", "PointwiseTemplate", "RowsTemplate", "GemmTemplate",
-           "AttentionTemplate"]
+           "AttentionTemplate", "GemmSmallTemplate"]

@@ -87,6 +87,9 @@ class AttentionTemplate:
     # ------------------------------------------------------------------ match
     @classmethod
     def match(cls, ctx) -> "AttentionTemplate":
+        from .gemm_small import meta_only
+        if meta_only():
+            raise TemplateMismatch("meta-only launch requested (EMMY_META_ONLY): no tensor maps")
         tile = ctx.tile
         if tile is None:
             raise TemplateMismatch("no single top-level Tile")

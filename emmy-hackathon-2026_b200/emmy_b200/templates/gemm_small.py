@@ -1,0 +1,671 @@
+"""Matmul template with a meta-only launch: tcgen05 tiles fed by the CTA's own
+threads instead of tensor maps.
+
+The TMA kernels of :mod:`.gemm` take host-built tensor maps after the meta
+``arg_order`` parameters; a launcher that passes exactly ``arg_order`` (the
+reference's runner and its ctypes harness, ``tools/harness/gpu_run.py:82-89``)
+cannot supply them.  This template's PTX takes the meta parameters and nothing
+else, so it runs under any launcher of the reference's contract.  It accepts
+Emmy's own matmul schedules -- the m01/m02 open problems and the corpus
+``mm*`` IRs (reference ``problems/m01_matmul_512/*.ir.txt:1-37``): any CTA
+tile up to 128 x 256, any CTA size from 32 threads, tiles cut off by the
+matrix edge (``Cond(row < M)`` around ``% M`` stores) and split-K over a
+leading Tile axis with atomic stores (``red.global.add``, the output zeroed
+by ``zero_outputs``) -- and, when ``EMMY_META_ONLY=1`` makes the TMA
+template decline, the benchmark's own matmul IRs.
+
+Per CTA (the IR's CTA -> (k chunk, M tile, N tile) assignment, row-major over
+the Tile's block axes):
+
+* every thread stages 16-byte chunks of the A rows (K-major, as stored) and
+  of the B columns (transposed on the way into K-major, four or eight
+  scalar loads of a column per chunk, coalesced across the threads) into
+  shared memory in the UMMA 128-byte-swizzle layout (the 16-byte chunk c of
+  row r of an 8-row atom at chunk c ^ r), zero outside the matrix and past
+  the CTA's K range; for fp32 operands the same threads also write the
+  low tf32 parts lo = x - (x with its 13 low mantissa bits cleared) beside
+  them (3xTF32, as :func:`.gemm.tf32_lo_trunc`);
+* one thread issues ``tcgen05.mma.cta_group::1`` (M = 128, N = the tile
+  width rounded up to 16; ``kind::tf32`` lo*hi, hi*lo, hi*hi or
+  ``kind::f16``) into a TMEM accumulator and commits to the slab's
+  mbarrier; two slab buffers alternate, so the threads stage slab s+1 while
+  the tensor core works on slab s;
+* the warps read the accumulator back with ``tcgen05.ld.32x32b`` (warp w:
+  TMEM lanes 32 (w % 4) ..; warps with the same w % 4 split the columns)
+  and store the CTA's in-bounds outputs (plain or atomic, as the IR writes).
+
+Rows of the A operand beyond the tile (up to the MMA's 128) and columns beyond the tile
+width only produce accumulator rows and columns that are never stored.
+Every mbarrier wait is bounded by ``%globaltimer`` and reports through
+``__emmy_status``.
+"""
+from __future__ import annotations
+
+import os
+
+from ..analysis import NotAffine, affine, kind, walk
+from ..ir import dim
+from ..ptx import Kernel
+from .common import TemplateMismatch
+from .gemm import GemmTemplate, _desc_hi, idesc_mma
+
+STATIC_MAX = 48 * 1024 - 256      # static shared memory a kernel may declare
+SMEM_LIMIT = 227 * 1024
+
+
+def meta_only() -> bool:
+    """``EMMY_META_ONLY=1``: emit only kernels whose parameters are exactly
+    the meta ``arg_order`` (no trailing tensor maps)."""
+    return os.environ.get("EMMY_META_ONLY", "") not in ("", "0")
+
+
+def _strip_mod(e, extent):
+    """``(x) % extent`` -> (x, True); anything else -> (e, False)."""
+    if kind(e) == "BinaryExpr" and e.op == "%" and kind(e.right) == "Literal" \
+            and e.right.value == extent:
+        return e.left, True
+    return e, False
+
+
+def _guard_bounds(cond) -> list:
+    """The ``x < c`` terms of a guard (``&&`` of comparisons) as (affine x, c)."""
+    if kind(cond) == "BinaryExpr" and cond.op in ("&&", "and"):
+        return _guard_bounds(cond.left) + _guard_bounds(cond.right)
+    if kind(cond) == "BinaryExpr" and cond.op == "<" and kind(cond.right) == "Literal":
+        return [(affine(cond.left), int(cond.right.value))]
+    raise NotAffine("guard")
+
+
+class GemmSmallTemplate:
+    name = "gemm"
+
+    # ------------------------------------------------------------------ match
+    @classmethod
+    def match(cls, ctx) -> "GemmSmallTemplate":
+        tile = ctx.tile
+        if tile is None:
+            raise TemplateMismatch("no single top-level Tile")
+        # grouped rasterisation remaps CTAs only with a group of 2 or more
+        # (reference compile.py:2403-2415); auxiliary threads change the decode
+        if (getattr(tile, "raster_group", None) or 0) > 1 and getattr(tile, "raster_axes", None) \
+                or getattr(tile, "aux_threads", 0):
+            raise TemplateMismatch("rasterised or auxiliary-thread tile")
+        axes = ctx.tile_axes()
+        names = [a for a, _ in axes]
+        if names[-4:] != ["a0_b", "a1_b", "a0_u", "a1_u"] or len(names) not in (4, 5):
+            raise TemplateMismatch("not a matmul tile (..., a0_b, a1_b, a0_u, a1_u)")
+        ext = dict(axes)
+        ks_axis = names[0] if len(names) == 5 else None
+        T = ext["a0_u"] * ext["a1_u"]
+        bt = getattr(tile, "block_threads", None)
+        if ctx.block != (T, 1, 1) or (bt not in (None, T)) or T % 32 or T > 1024:
+            raise TemplateMismatch("CTA is not the a0_u x a1_u thread block")
+        nblk = ext["a0_b"] * ext["a1_b"] * (ext[ks_axis] if ks_axis else 1)
+        if ctx.grid[0] * ctx.grid[1] * ctx.grid[2] != nblk:
+            raise TemplateMismatch("grid is not one CTA per (k chunk, tile)")
+        body = list(walk(tile.body))
+        smems = {s.name for s in body if kind(s) == "Smem"}
+        copies = [s for s in body if kind(s) == "CpAsyncCopy"]
+        inits = {s.name for s in body if kind(s) == "Init"}
+        if len(smems) != 2 or not copies or not inits:
+            raise TemplateMismatch("matmul statements missing")
+        if any(float(s.identity) != 0.0 for s in body if kind(s) == "Init"):
+            raise TemplateMismatch("accumulator not zero-initialised")
+        src_of = {}
+        for c in copies:
+            if src_of.setdefault(c.smem, c.src) != c.src:
+                raise TemplateMismatch("smem filled from two buffers")
+        loops = [s for s in body if kind(s) == "Loop"]
+        if len(loops) != 1:
+            raise TemplateMismatch("expected one inner k loop")
+        role, defs, pairs = {}, {}, set()
+        for s in loops[0].body:
+            k_ = kind(s)
+            if k_ == "Load":
+                if s.input not in smems:
+                    raise TemplateMismatch("inner loop reads global memory")
+                defs[s.names[0]] = ("load", s.input)
+                fv = set()
+                for ix in s.index:
+                    fv |= ix.free_vars() if hasattr(ix, "free_vars") else set()
+                r = "A" if "a0_u" in fv and "a1_u" not in fv else \
+                    "B" if "a1_u" in fv and "a0_u" not in fv else None
+                if r is None or role.setdefault(s.input, r) != r:
+                    raise TemplateMismatch("operand tile indexing")
+            elif k_ == "Assign":
+                if s.op.name != "multiply" or len(s.args) != 2:
+                    raise TemplateMismatch(f"inner op {s.op.name}")
+                a, b = (defs.get(x) for x in s.args)
+                if not (a and b and a[0] == b[0] == "load" and a[1] != b[1]):
+                    raise TemplateMismatch("multiply of non-smem operands")
+                defs[s.name] = ("mul", frozenset((a[1], b[1])))
+            elif k_ == "Accum":
+                if s.name not in inits or s.op.name != "add" or s.base:
+                    raise TemplateMismatch("accumulate shape")
+                v = defs.get(s.value)
+                if not v or v[0] != "mul":
+                    raise TemplateMismatch("accumulate of a non-product")
+                pairs.add(v[1])
+            else:
+                raise TemplateMismatch(f"{k_} in the inner k loop")
+        if pairs != {frozenset(smems)}:
+            raise TemplateMismatch("products do not pair the two smem tiles")
+        inv = {v: s for s, v in role.items()}
+        if set(inv) != {"A", "B"}:
+            raise TemplateMismatch("operand roles")
+        A, B = src_of.get(inv["A"]), src_of.get(inv["B"])
+        bufs = ctx.bufs
+        # the stores: (row, col) of each value, possibly as (x % extent)
+        # under a Cond(x < extent) guard
+        writes = []
+
+        def collect(stmts, guards):
+            for s in stmts:
+                k_ = kind(s)
+                if k_ == "Write":
+                    writes.append((s, guards))
+                elif k_ == "Cond":
+                    if s.else_body:
+                        raise TemplateMismatch("store under if/else")
+                    try:
+                        g = _guard_bounds(s.cond)
+                    except NotAffine as e:
+                        raise TemplateMismatch(f"store guard: {e}")
+                    collect(s.body, guards + g)
+                elif k_ in ("Loop", "StridedLoop"):
+                    if any(kind(x) == "Write" for x in walk(s.body)):
+                        raise TemplateMismatch("store inside a loop")
+        collect(tile.body, [])
+        if not writes:
+            raise TemplateMismatch("no stores")
+        outs = {w.output for w, _ in writes}
+        if len(outs) != 1:
+            raise TemplateMismatch("multiple outputs")
+        C = outs.pop()
+        if A is None or B is None or any(len(bufs.shapes.get(x, ())) != 2 for x in (A, B, C)):
+            raise TemplateMismatch("operand ranks")
+        M, K = bufs.shapes[A]
+        K2, N = bufs.shapes[B]
+        if K2 != K or tuple(bufs.shapes[C]) != (M, N) or bufs.dtypes.get(C) != "f32":
+            raise TemplateMismatch("operand shapes")
+        atomic = {w.atomic for w, _ in writes}
+        if len(atomic) != 1:
+            raise TemplateMismatch("mixed plain and atomic stores")
+        atomic = atomic.pop()
+        # atomic stores add the CTA's partial product to C, as the IR's own
+        # red.global.add does, whatever C held before (the runner zeroes it)
+        if not atomic and ks_axis is not None and ext[ks_axis] > 1:
+            raise TemplateMismatch("split K with plain stores")
+        BM = BN = mu = nu = None
+        cells = set()
+        for w, guards in writes:
+            if len(w.index) != 2:
+                raise TemplateMismatch("store rank")
+            try:
+                re_, rmod = _strip_mod(w.index[0], M)
+                ce_, cmod = _strip_mod(w.index[1], N)
+                r, c = affine(re_), affine(ce_)
+            except NotAffine as e:
+                raise TemplateMismatch(f"store index: {e}")
+            # a wrapped index is only the identity where a guard bounds it
+            for x, wrapped, bound in ((r, rmod, M), (c, cmod, N)):
+                if wrapped and not any(gx == x and gc <= bound for gx, gc in guards):
+                    raise TemplateMismatch("wrapped store index without its guard")
+            for gx, gc in guards:
+                if gx != r and gx != c:
+                    raise TemplateMismatch("guard on something else than the store index")
+            if r.vars() - {"a0_b", "a0_u"} or c.vars() - {"a1_b", "a1_u"}:
+                raise TemplateMismatch("store index variables")
+            bm, m_, bn, n_ = r.coef("a0_b"), r.coef("a0_u"), c.coef("a1_b"), c.coef("a1_u")
+            if BM is None:
+                BM, mu, BN, nu = bm, m_, bn, n_
+            if (bm, m_, bn, n_) != (BM, mu, BN, nu):
+                raise TemplateMismatch("stores disagree on the tile")
+            for j in range(len(w.values)):
+                cells.add((r.const, c.const + j))
+        if not mu or not nu or BM != ext["a0_u"] * mu or BN != ext["a1_u"] * nu:
+            raise TemplateMismatch("micro-tiles do not tile the CTA tile")
+        if cells != {(i, j) for i in range(mu) for j in range(nu)}:
+            raise TemplateMismatch("stores do not cover each micro-tile once")
+        # rows / columns past the matrix must be guarded, tiles must reach it
+        if ext["a0_b"] * BM < M or ext["a1_b"] * BN < N:
+            raise TemplateMismatch("tiles do not cover the output")
+        for w, guards in writes:
+            r = affine(_strip_mod(w.index[0], M)[0])
+            c = affine(_strip_mod(w.index[1], N)[0])
+            if ext["a0_b"] * BM > M and not any(gx == r for gx, _ in guards):
+                raise TemplateMismatch("rows past M stored unguarded")
+            if ext["a1_b"] * BN > N and not any(gx == c for gx, _ in guards):
+                raise TemplateMismatch("columns past N stored unguarded")
+        # the CTA's K range: the k-slab loop's extent; with split K the
+        # leading axis numbers the chunks
+        kl = [s for s in body if kind(s) == "StridedLoop" and
+              any(kind(x) == "Loop" for x in walk(s.body))]
+        if len(kl) != 1:
+            raise TemplateMismatch("expected one k-slab loop")
+        KC = dim(kl[0].axis.extent)
+        nks = ext[ks_axis] if ks_axis else 1
+        if KC * nks != K:
+            raise TemplateMismatch("k chunks do not cover K")
+        dts = {bufs.dtypes[A], bufs.dtypes[B]}
+        if dts == {"f32"}:
+            mode = "tf32x3"
+        elif dts == {"bf16"}:
+            mode = "bf16"
+        else:
+            raise TemplateMismatch(f"operand dtypes {dts}")
+        warps = T // 32
+        if BM > 128 or BM > 32 * min(4, warps) or BN > 256:
+            raise TemplateMismatch(f"tile {BM}x{BN} too large for {T} threads")
+        self = cls()
+        self.ctx, self.A, self.B, self.C = ctx, A, B, C
+        self.M, self.N, self.K, self.KC = M, N, K, KC
+        self.BM, self.BN, self.T = BM, BN, T
+        self.nb0, self.nb1, self.nks = ext["a0_b"], ext["a1_b"], nks
+        self.mode, self.atomic = mode, atomic
+        self.es = 4 if mode == "tf32x3" else 2
+        self.CE = 16 // self.es                 # elements per 16-byte chunk
+        self.KB = 128 // self.es                # k per 128-byte swizzle row (one slab)
+        self.BNp = -(-BN // 16) * 16
+        half = 2 if mode == "tf32x3" else 1     # raw + low parts
+        # per slab buffer: A (the tile's rows, in whole 8-row atoms) | A_lo |
+        # B (BNp rows) | B_lo, 128 bytes a row.  The MMA's A descriptor spans
+        # 128 rows (16 KiB) from A's base: rows past the tile read the bytes
+        # after it (garbage that only reaches accumulator rows never
+        # stored), so the allocation reaches 16 KiB past the last A base
+        self.sa = -(-BM // 8) * 1024
+        self.sb = self.BNp * 128
+        self.buf = (self.sa + self.sb) * half
+
+        def need(nbuf):
+            span = (nbuf - 1) * self.buf + (self.sa if half == 2 else 0) + 128 * 128
+            return max(nbuf * self.buf, span) + 1024 + 64
+        avail = min(ctx.smem_bytes, SMEM_LIMIT)
+        # static shared memory adds to the launch's dynamic bytes: a launcher
+        # raises the per-CTA limit above 48 KiB only for dynamic sizes above it
+        cap = SMEM_LIMIT if avail > 48 * 1024 else 48 * 1024
+        for nbuf in (2, 1):
+            if avail >= need(nbuf):
+                self.nbuf, self.dynamic = nbuf, True
+                break
+            if need(nbuf) <= STATIC_MAX and need(nbuf) + avail <= cap:
+                self.nbuf, self.dynamic = nbuf, False
+                break
+        else:
+            raise TemplateMismatch("shared memory for one slab")
+        self.smem_need = need(self.nbuf)
+        return self
+
+    # ------------------------------------------------------------------- emit
+    def emit(self) -> str:
+        ctx = self.ctx
+        T, BM, BN, BNp, KB, CE, es = self.T, self.BM, self.BN, self.BNp, self.KB, self.CE, self.es
+        M, N, K, KC = self.M, self.N, self.K, self.KC
+        tf32 = self.mode == "tf32x3"
+        KMMA = 32 // es                         # k per tcgen05.mma (32 bytes)
+        k = Kernel(ctx.entry, ctx.params())
+        k.maxntid = (T, 1, 1)
+        if self.dynamic:
+            k.decl(".extern .shared .align 1024 .b8 __emmy_smem[];")
+        else:
+            k.decl(f".shared .align 1024 .b8 __emmy_smem[{self.smem_need}];")
+        k.decl(".global .align 4 .u32 __emmy_status;")
+        k.comment(f"emmy-b200 template: tcgen05 gemm, meta-only launch (no tensor maps), "
+                  f"{self.mode} M={M} N={N} K={K}, CTA tile {BM}x{BN} over K chunks of {KC}, "
+                  f"{T} threads, {self.nbuf} slab buffer(s)")
+        abase, bbase, cbase = k.param_ptr(self.A), k.param_ptr(self.B), k.param_ptr(self.C)
+        tid = k.special("%tid.x")
+        warp = k.reg("r")
+        k(f"shr.u32 {warp}, {tid}, 5;")
+        lane = k.reg("r")
+        k(f"and.b32 {lane}, {tid}, 31;")
+        cta = k.special("%ctaid.x")
+        nb = k.reg("r")
+        k(f"rem.u32 {nb}, {cta}, {self.nb1};")
+        t_ = k.reg("r")
+        k(f"div.u32 {t_}, {cta}, {self.nb1};")
+        mb = k.reg("r")
+        k(f"rem.u32 {mb}, {t_}, {self.nb0};")
+        ks = k.reg("r")
+        k(f"div.u32 {ks}, {t_}, {self.nb0};")
+        r0 = k.reg("r")
+        k(f"mul.lo.u32 {r0}, {mb}, {BM};")
+        n0 = k.reg("r")
+        k(f"mul.lo.u32 {n0}, {nb}, {BN};")
+        k0 = k.reg("r")
+        k(f"mul.lo.u32 {k0}, {ks}, {KC};")
+        kend = k.reg("r")
+        k(f"add.u32 {kend}, {k0}, {KC};")
+        # shared memory: nbuf x [A | A_lo | B | B_lo], then barriers, tmem slot
+        raw = k.reg("r")
+        k(f"mov.u32 {raw}, __emmy_smem;")
+        sm = k.reg("r")
+        k(f"add.u32 {sm}, {raw}, 1023;")
+        k(f"and.b32 {sm}, {sm}, -1024;")
+        bars = k.reg("r")
+        k(f"add.u32 {bars}, {sm}, {self.smem_need - 1024 - 64};")
+        tslot = k.reg("r")
+        k(f"add.u32 {tslot}, {bars}, 16;")
+        status = k.reg("rd")
+        k(f"mov.u64 {status}, __emmy_status;")
+        p0 = k.reg("p")
+        k(f"setp.eq.u32 {p0}, {tid}, 0;")
+        skip = k.label("SKIP_INIT")
+        k(f"@!{p0} bra {skip};")
+        for b in range(self.nbuf):
+            k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * b}], 1;")
+        k("fence.mbarrier_init.release.cluster;")
+        k.mark(skip)
+        pw0 = k.reg("p")
+        k(f"setp.eq.u32 {pw0}, {warp}, 0;")
+        skip2 = k.label("SKIP_ALLOC")
+        ncols = max(32, 1 << (BNp - 1).bit_length())
+        k(f"@!{pw0} bra {skip2};")
+        k(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{tslot}], {ncols};")
+        k("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;")
+        k.mark(skip2)
+        k("tcgen05.fence::before_thread_sync;")
+        k("bar.sync 0;")
+        k("tcgen05.fence::after_thread_sync;")
+        tmem = k.reg("r")
+        k(f"ld.shared.u32 {tmem}, [{tslot}];")
+        teardown = k.label("TEARDOWN")
+        idesc = k.reg("r")
+        k(f"mov.u32 {idesc}, {idesc_mma(128, BNp, False, tf32)};")
+        hi = _desc_hi(16, 1024)
+        ptrue = k.reg("p")
+        k(f"setp.eq.u32 {ptrue}, 0, 0;")
+        wait = GemmTemplate._wait
+
+        def swz(row, ch):
+            """Byte offset of 16-byte chunk ``ch`` of row ``row`` in the
+            128-byte-swizzle K-major layout (8-row atoms of 1024 bytes)."""
+            o = k.reg("r")
+            k(f"and.b32 {o}, {row}, 7;")
+            x = k.reg("r")
+            k(f"xor.b32 {x}, {ch}, {o};")
+            k(f"shl.b32 {x}, {x}, 4;")
+            k(f"shl.b32 {o}, {o}, 7;")
+            k(f"add.u32 {x}, {x}, {o};")
+            a = k.reg("r")
+            k(f"shr.u32 {a}, {row}, 3;")
+            k(f"mad.lo.u32 {x}, {a}, 1024, {x};")
+            return x
+
+        def store_chunk(dst, off, vals, lo_off):
+            a = k.reg("r")
+            k(f"add.u32 {a}, {dst}, {off};")
+            k(f"st.shared.v4.b32 [{a}], {{{', '.join(vals)}}};")
+            if tf32:
+                lo = []
+                for v in vals:
+                    m_ = k.reg("r")
+                    k(f"and.b32 {m_}, {v}, -8192;")
+                    l_ = k.reg("r")
+                    k(f"sub.rn.f32 {l_}, {v}, {m_};")
+                    lo.append(l_)
+                k(f"st.shared.v4.b32 [{a}+{lo_off}], {{{', '.join(lo)}}};")
+
+        def zeros():
+            z = k.regs("r", 4)
+            for r_ in z:
+                k(f"mov.b32 {r_}, 0;")
+            return z
+
+        def load_elem(ptr_base, eidx, ok, dst):
+            """dst = element eidx of a global operand if ok, else 0."""
+            k(f"mov.b32 {dst}, 0;")
+            a = k.reg("rd")
+            k(f"mul.wide.u32 {a}, {eidx}, {es};")
+            k(f"add.s64 {a}, {a}, {ptr_base};")
+            if es == 4:
+                k(f"@{ok} ld.global.nc.b32 {dst}, [{a}];")
+            else:
+                h = k.reg("h")
+                k(f"mov.b16 {h}, 0;")
+                k(f"@{ok} ld.global.nc.b16 {h}, [{a}];")
+                k(f"cvt.u32.u16 {dst}, {h};")
+
+        def pack16(lo16, hi16):
+            r_ = k.reg("r")
+            k(f"shl.b32 {r_}, {hi16}, 16;")
+            k(f"or.b32 {r_}, {r_}, {lo16};")
+            return r_
+
+        def stage(slab, buf):
+            """Threads stage slab ``slab`` (k from k0 + slab*KB) into buffer
+            ``buf``: A rows (16-byte chunks along k), B columns (transposed)."""
+            base = k.reg("r")
+            k(f"mad.lo.u32 {base}, {buf}, {self.buf}, {sm};")
+            kb = k.reg("r")
+            k(f"mad.lo.u32 {kb}, {slab}, {KB}, {k0};")
+            # A: BM rows x 8 chunks
+            idx = k.reg("r")
+            k(f"mov.u32 {idx}, {tid};")
+            top, done = k.label("STA"), k.label("STA_END")
+            k.mark(top)
+            pe = k.reg("p")
+            k(f"setp.ge.u32 {pe}, {idx}, {BM * 8};")
+            k(f"@{pe} bra {done};")
+            row = k.reg("r")
+            k(f"shr.u32 {row}, {idx}, 3;")
+            ch = k.reg("r")
+            k(f"and.b32 {ch}, {idx}, 7;")
+            gr = k.reg("r")
+            k(f"add.u32 {gr}, {r0}, {row};")
+            kk = k.reg("r")
+            k(f"mad.lo.u32 {kk}, {ch}, {CE}, {kb};")
+            rowok = k.reg("p")
+            k(f"setp.lt.u32 {rowok}, {gr}, {M};")
+            vals = k.regs("r", 4)
+            words = []
+            elems = k.regs("r", CE)
+            for e in range(CE):
+                ke = k.reg("r")
+                k(f"add.u32 {ke}, {kk}, {e};")
+                ok = k.reg("p")
+                k(f"setp.lt.and.u32 {ok}, {ke}, {kend}, {rowok};")
+                ei = k.reg("r")
+                k(f"mad.lo.u32 {ei}, {gr}, {K}, {ke};")
+                load_elem(abase, ei, ok, elems[e])
+            if es == 4:
+                words = elems
+            else:
+                words = [pack16(elems[2 * w], elems[2 * w + 1]) for w in range(4)]
+            for v, w in zip(vals, words):
+                k(f"mov.b32 {v}, {w};")
+            off = swz(row, ch)
+            store_chunk(base, off, vals, self.sa)
+            k(f"add.u32 {idx}, {idx}, {T};")
+            k(f"bra {top};")
+            k.mark(done)
+            # B: BN columns (rows of the K-major copy) x 8 chunks, column
+            # fastest across threads (coalesced loads of a B row)
+            k(f"mov.u32 {idx}, {tid};")
+            top, done = k.label("STB"), k.label("STB_END")
+            k.mark(top)
+            k(f"setp.ge.u32 {pe}, {idx}, {BN * 8};")
+            k(f"@{pe} bra {done};")
+            n_ = k.reg("r")
+            k(f"rem.u32 {n_}, {idx}, {BN};")
+            ch2 = k.reg("r")
+            k(f"div.u32 {ch2}, {idx}, {BN};")
+            gn = k.reg("r")
+            k(f"add.u32 {gn}, {n0}, {n_};")
+            k(f"mad.lo.u32 {kk}, {ch2}, {CE}, {kb};")
+            colok = k.reg("p")
+            k(f"setp.lt.u32 {colok}, {gn}, {N};")
+            elems = k.regs("r", CE)
+            for e in range(CE):
+                ke = k.reg("r")
+                k(f"add.u32 {ke}, {kk}, {e};")
+                ok = k.reg("p")
+                k(f"setp.lt.and.u32 {ok}, {ke}, {kend}, {colok};")
+                ei = k.reg("r")
+                k(f"mad.lo.u32 {ei}, {ke}, {N}, {gn};")
+                load_elem(bbase, ei, ok, elems[e])
+            words = elems if es == 4 else [pack16(elems[2 * w], elems[2 * w + 1])
+                                           for w in range(4)]
+            vals = k.regs("r", 4)
+            for v, w in zip(vals, words):
+                k(f"mov.b32 {v}, {w};")
+            off = swz(n_, ch2)
+            k(f"add.u32 {off}, {off}, {self.sa * (2 if tf32 else 1)};")
+            store_chunk(base, off, vals, self.sb)
+            k(f"add.u32 {idx}, {idx}, {T};")
+            k(f"bra {top};")
+            k.mark(done)
+            k("fence.proxy.async.shared::cta;")
+
+        def mma(slab, buf, nsteps):
+            """Thread 0: the MMAs of one staged slab, then a commit."""
+            sk = k.label("NO_MMA")
+            k(f"@!{p0} bra {sk};")
+            k("tcgen05.fence::after_thread_sync;")
+            base = k.reg("r")
+            k(f"mad.lo.u32 {base}, {buf}, {self.buf}, {sm};")
+            da = GemmTemplate._desc(k, base, hi)
+            bb = k.reg("r")
+            k(f"add.u32 {bb}, {base}, {self.sa * (2 if tf32 else 1)};")
+            db = GemmTemplate._desc(k, bb, hi)
+            if tf32:
+                la = k.reg("r")
+                k(f"add.u32 {la}, {base}, {self.sa};")
+                dla = GemmTemplate._desc(k, la, hi)
+                lb = k.reg("r")
+                k(f"add.u32 {lb}, {base}, {2 * self.sa + self.sb};")
+                dlb = GemmTemplate._desc(k, lb, hi)
+            pacc = k.reg("p")
+            k(f"setp.ne.u32 {pacc}, {slab}, 0;")
+            first = True
+            for st in range(nsteps):
+                pairs = [(dla, db), (da, dlb), (da, db)] if tf32 else [(da, db)]
+                for x, y in pairs:
+                    ax = k.reg("rd")
+                    k(f"add.s64 {ax}, {x}, {2 * st};")
+                    by = k.reg("rd")
+                    k(f"add.s64 {by}, {y}, {2 * st};")
+                    kind_ = "tf32" if tf32 else "f16"
+                    k(f"tcgen05.mma.cta_group::1.kind::{kind_} [{tmem}], {ax}, {by}, {idesc}, "
+                      f"{pacc if first else ptrue};")
+                    first = False
+            bar = k.reg("r")
+            k(f"mad.lo.u32 {bar}, {buf}, 8, {bars};")
+            k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{bar}];")
+            k.mark(sk)
+
+        def wait_slab(slab):
+            """Wait for the MMAs of slab ``slab`` (its buffer's barrier,
+            completion number slab // nbuf)."""
+            b = k.reg("r")
+            k(f"rem.u32 {b}, {slab}, {self.nbuf};")
+            bar = k.reg("r")
+            k(f"mad.lo.u32 {bar}, {b}, 8, {bars};")
+            ph = k.reg("r")
+            k(f"div.u32 {ph}, {slab}, {self.nbuf};")
+            k(f"and.b32 {ph}, {ph}, 1;")
+            wait(k, bar, ph, status, 2, teardown)
+
+        nslab = -(-KC // KB)
+        full = KC // KB                       # slabs with KB k each
+        tail_k = KC - full * KB
+        s = k.reg("r")
+        bufr = k.reg("r")
+        k(f"mov.u32 {s}, 0;")
+        if full:
+            top = k.label("SLAB")
+            k.mark(top)
+            k(f"rem.u32 {bufr}, {s}, {self.nbuf};")
+            pw = k.reg("p")
+            k(f"setp.ge.u32 {pw}, {s}, {self.nbuf};")
+            skw = k.label("NO_WAIT")
+            k(f"@!{pw} bra {skw};")
+            prev = k.reg("r")
+            k(f"sub.u32 {prev}, {s}, {self.nbuf};")
+            wait_slab(prev)                   # the buffer's previous MMAs are done
+            k.mark(skw)
+            stage(s, bufr)
+            k("bar.sync 0;")
+            mma(s, bufr, KB // KMMA)
+            k(f"add.u32 {s}, {s}, 1;")
+            pl = k.reg("p")
+            k(f"setp.lt.u32 {pl}, {s}, {full};")
+            k(f"@{pl} bra {top};")
+        if tail_k:
+            k(f"rem.u32 {bufr}, {s}, {self.nbuf};")
+            if full >= self.nbuf:
+                prev = k.reg("r")
+                k(f"sub.u32 {prev}, {s}, {self.nbuf};")
+                wait_slab(prev)
+            stage(s, bufr)
+            k("bar.sync 0;")
+            mma(s, bufr, -(-tail_k // KMMA))
+        last = k.reg("r")
+        k(f"mov.u32 {last}, {nslab - 1};")
+        wait_slab(last)                       # MMAs complete in order: all done
+        k("tcgen05.fence::after_thread_sync;")
+        # ---------------- epilogue ----------------
+        warps = T // 32
+        groups = max(1, warps // 4)
+        q = k.reg("r")
+        k(f"and.b32 {q}, {warp}, 3;")
+        g_ = k.reg("r")
+        k(f"shr.u32 {g_}, {warp}, 2;")
+        skip_ep = k.label("NO_ROWS")
+        pq = k.reg("p")
+        k(f"setp.ge.u32 {pq}, {q}, {-(-BM // 32)};")       # no tile rows in this quarter
+        k(f"@{pq} bra {skip_ep};")
+        lrow = k.reg("r")
+        k(f"mad.lo.u32 {lrow}, {q}, 32, {lane};")
+        grow = k.reg("r")
+        k(f"add.u32 {grow}, {r0}, {lrow};")
+        rok = k.reg("p")
+        k(f"setp.lt.u32 {rok}, {grow}, {M};")
+        rok2 = k.reg("p")
+        k(f"setp.lt.and.u32 {rok2}, {lrow}, {BM}, {rok};")
+        crow = k.reg("rd")
+        k(f"mul.wide.u32 {crow}, {grow}, {N * 4};")
+        k(f"add.s64 {crow}, {crow}, {cbase};")
+        taddr = k.reg("r")
+        k(f"shl.b32 {taddr}, {q}, 21;")
+        k(f"add.u32 {taddr}, {taddr}, {tmem};")
+        chunks = list(range(0, BNp, 8))
+        for gi in range(groups):
+            mine = [c for i, c in enumerate(chunks) if i % groups == gi]
+            if not mine:
+                continue
+            skg = k.label("NOT_MY_COLS")
+            pg = k.reg("p")
+            k(f"setp.ne.u32 {pg}, {g_}, {gi};")
+            if groups > 1:
+                k(f"@{pg} bra {skg};")
+            for c in mine:
+                regs = k.regs("r", 8)
+                k(f"tcgen05.ld.sync.aligned.32x32b.x8.b32 {{{', '.join(regs)}}}, [{taddr}+{c}];")
+                k("tcgen05.wait::ld.sync.aligned;")
+                for e in range(8):
+                    if c + e >= BN:
+                        break
+                    gc = k.reg("r")
+                    k(f"add.u32 {gc}, {n0}, {c + e};")
+                    ok = k.reg("p")
+                    k(f"setp.lt.and.u32 {ok}, {gc}, {N}, {rok2};")
+                    a = k.reg("rd")
+                    k(f"mul.wide.u32 {a}, {gc}, 4;")
+                    k(f"add.s64 {a}, {a}, {crow};")
+                    op = "red.global.add.f32" if self.atomic else "st.global.f32"
+                    k(f"@{ok} {op} [{a}], {regs[e]};")
+            k.mark(skg)
+        k.mark(skip_ep)
+        # ---------------- teardown ----------------
+        k.mark(teardown)
+        k("tcgen05.fence::before_thread_sync;")
+        k("barrier.sync 0;")
+        end = k.label("END")
+        k(f"@!{pw0} bra {end};")
+        k("bar.warp.sync 0xffffffff;")
+        k("tcgen05.fence::after_thread_sync;")
+        k(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tmem}, {ncols};")
+        k.mark(end)
+        k("ret;")
+        return k.render()

@@ -345,3 +345,28 @@ def test_tf32_split_with_raw_high_part():
     ptx = compiler.compile_graph(g, m).render()
     assert "cvt.rna.tf32.f32" not in ptx
     assert "and.b32" in ptx and "-8192" in ptx
+
+
+def test_meta_only_gemm_takes_only_meta_parameters(monkeypatch):
+    """Emmy's own matmul IRs (m01, m02, corpus mm*) compile to the tcgen05
+    kernel whose parameters are exactly meta ``arg_order`` (no tensor-map
+    directives or trailing parameters); with EMMY_META_ONLY=1 the benchmark's
+    matmul IRs do too, and attention falls back to the generic lowering."""
+    import re
+    from conftest import GOLDEN
+    from emmy_b200 import synth
+    folders = [GOLDEN / "problems" / "m01_matmul_512", GOLDEN / "problems" / "m02_matmul_rect"] + \
+        [GOLDEN / "corpus" / n for n in ("mm128", "mm256", "mm512", "mm64a", "mm_rect2")]
+    cases = [(json.loads((f / "kernel.ir.json").read_text()),
+              json.loads((f / "meta.json").read_text())) for f in folders]
+    monkeypatch.setenv("EMMY_META_ONLY", "1")
+    cases += [synth.config(n).build() for n in ("matmul_bf16", "matmul_f32")]
+    for g, m in cases:
+        c = compile_graph(g, m)
+        ptx = c.render()
+        assert type(c.template).__name__ == "GemmSmallTemplate", c.rejections
+        assert "@emmy tmap" not in ptx and "tensormap" not in ptx
+        params = re.findall(r"\.param \.(\w+) param_(\w+)", ptx)
+        assert [n for _, n in params] == m["kernels"][0]["arg_order"]
+    g, m = synth.attention(B=1, H=1, S=256, D=64).build()
+    assert compile_graph(g, m).kind == "generic"
