@@ -406,12 +406,6 @@ class GemmSmallTemplate:
                     lo.append(l_)
                 k(f"st.shared.v4.b32 [{a}+{lo_off}], {{{', '.join(lo)}}};")
 
-        def zeros():
-            z = k.regs("r", 4)
-            for r_ in z:
-                k(f"mov.b32 {r_}, 0;")
-            return z
-
         def load_elem(ptr_base, eidx, ok, dst):
             """dst = element eidx of a global operand if ok, else 0."""
             k(f"mov.b32 {dst}, 0;")
@@ -432,89 +426,88 @@ class GemmSmallTemplate:
             k(f"or.b32 {r_}, {r_}, {lo16};")
             return r_
 
-        def stage(slab, buf):
-            """Threads stage slab ``slab`` (k from k0 + slab*KB) into buffer
-            ``buf``: A rows (16-byte chunks along k), B columns (transposed)."""
-            base = k.reg("r")
-            k(f"mad.lo.u32 {base}, {buf}, {self.buf}, {sm};")
+        nA, nB = -(-BM * 8 // T), -(-BN * 8 // T)     # 16-byte chunks per thread
+        vec_a = K % CE == 0 and KC % CE == 0            # a chunk is all in or all out
+
+        def fetch(slab, into=None):
+            """This thread's chunks of slab ``slab`` (k from k0 + slab*KB)
+            into registers: A rows as 16-byte loads (element loads at ragged
+            K), B columns as CE coalesced element loads each; zero outside
+            the matrix and past the CTA's K range.  The loads stay in flight
+            until ``put`` stores them.  ``into``: the registers of an earlier
+            fetch to load into (a loop-carried register set)."""
             kb = k.reg("r")
             k(f"mad.lo.u32 {kb}, {slab}, {KB}, {k0};")
-            # A: BM rows x 8 chunks
-            idx = k.reg("r")
-            k(f"mov.u32 {idx}, {tid};")
-            top, done = k.label("STA"), k.label("STA_END")
-            k.mark(top)
-            pe = k.reg("p")
-            k(f"setp.ge.u32 {pe}, {idx}, {BM * 8};")
-            k(f"@{pe} bra {done};")
-            row = k.reg("r")
-            k(f"shr.u32 {row}, {idx}, 3;")
-            ch = k.reg("r")
-            k(f"and.b32 {ch}, {idx}, 7;")
-            gr = k.reg("r")
-            k(f"add.u32 {gr}, {r0}, {row};")
-            kk = k.reg("r")
-            k(f"mad.lo.u32 {kk}, {ch}, {CE}, {kb};")
-            rowok = k.reg("p")
-            k(f"setp.lt.u32 {rowok}, {gr}, {M};")
-            vals = k.regs("r", 4)
-            words = []
-            elems = k.regs("r", CE)
-            for e in range(CE):
-                ke = k.reg("r")
-                k(f"add.u32 {ke}, {kk}, {e};")
-                ok = k.reg("p")
-                k(f"setp.lt.and.u32 {ok}, {ke}, {kend}, {rowok};")
-                ei = k.reg("r")
-                k(f"mad.lo.u32 {ei}, {gr}, {K}, {ke};")
-                load_elem(abase, ei, ok, elems[e])
-            if es == 4:
-                words = elems
-            else:
-                words = [pack16(elems[2 * w], elems[2 * w + 1]) for w in range(4)]
-            for v, w in zip(vals, words):
-                k(f"mov.b32 {v}, {w};")
-            off = swz(row, ch)
-            store_chunk(base, off, vals, self.sa)
-            k(f"add.u32 {idx}, {idx}, {T};")
-            k(f"bra {top};")
-            k.mark(done)
-            # B: BN columns (rows of the K-major copy) x 8 chunks, column
-            # fastest across threads (coalesced loads of a B row)
-            k(f"mov.u32 {idx}, {tid};")
-            top, done = k.label("STB"), k.label("STB_END")
-            k.mark(top)
-            k(f"setp.ge.u32 {pe}, {idx}, {BN * 8};")
-            k(f"@{pe} bra {done};")
-            n_ = k.reg("r")
-            k(f"rem.u32 {n_}, {idx}, {BN};")
-            ch2 = k.reg("r")
-            k(f"div.u32 {ch2}, {idx}, {BN};")
-            gn = k.reg("r")
-            k(f"add.u32 {gn}, {n0}, {n_};")
-            k(f"mad.lo.u32 {kk}, {ch2}, {CE}, {kb};")
-            colok = k.reg("p")
-            k(f"setp.lt.u32 {colok}, {gn}, {N};")
-            elems = k.regs("r", CE)
-            for e in range(CE):
-                ke = k.reg("r")
-                k(f"add.u32 {ke}, {kk}, {e};")
-                ok = k.reg("p")
-                k(f"setp.lt.and.u32 {ok}, {ke}, {kend}, {colok};")
-                ei = k.reg("r")
-                k(f"mad.lo.u32 {ei}, {ke}, {N}, {gn};")
-                load_elem(bbase, ei, ok, elems[e])
-            words = elems if es == 4 else [pack16(elems[2 * w], elems[2 * w + 1])
-                                           for w in range(4)]
-            vals = k.regs("r", 4)
-            for v, w in zip(vals, words):
-                k(f"mov.b32 {v}, {w};")
-            off = swz(n_, ch2)
-            k(f"add.u32 {off}, {off}, {self.sa * (2 if tf32 else 1)};")
-            store_chunk(base, off, vals, self.sb)
-            k(f"add.u32 {idx}, {idx}, {T};")
-            k(f"bra {top};")
-            k.mark(done)
+            out = []
+            slots = iter(into or [])
+            for which, nch, tot in (("A", nA, BM * 8), ("B", nB, BN * 8)):
+                for c in range(nch):
+                    prev = next(slots, None)
+                    idx = k.reg("r")
+                    k(f"add.u32 {idx}, {tid}, {c * T};")
+                    live = prev[3] if prev else k.reg("p")
+                    k(f"setp.lt.u32 {live}, {idx}, {tot};")
+                    row = prev[1] if prev else k.reg("r")
+                    ch = prev[2] if prev else k.reg("r")
+                    if which == "A":
+                        k(f"shr.u32 {row}, {idx}, 3;")
+                        k(f"and.b32 {ch}, {idx}, 7;")
+                        g = k.reg("r")
+                        k(f"add.u32 {g}, {r0}, {row};")
+                        k(f"setp.lt.and.u32 {live}, {g}, {M}, {live};")
+                    else:
+                        k(f"rem.u32 {row}, {idx}, {BN};")
+                        k(f"div.u32 {ch}, {idx}, {BN};")
+                        g = k.reg("r")
+                        k(f"add.u32 {g}, {n0}, {row};")
+                        k(f"setp.lt.and.u32 {live}, {g}, {N}, {live};")
+                    kk = k.reg("r")
+                    k(f"mad.lo.u32 {kk}, {ch}, {CE}, {kb};")
+                    w = prev[4] if prev else k.regs("r", 4)
+                    for r_ in w:
+                        k(f"mov.b32 {r_}, 0;")
+                    if which == "A" and vec_a:
+                        ok = k.reg("p")
+                        k(f"setp.lt.and.u32 {ok}, {kk}, {kend}, {live};")
+                        ei = k.reg("r")
+                        k(f"mad.lo.u32 {ei}, {g}, {K}, {kk};")
+                        a = k.reg("rd")
+                        k(f"mul.wide.u32 {a}, {ei}, {es};")
+                        k(f"add.s64 {a}, {a}, {abase};")
+                        k(f"@{ok} ld.global.nc.v4.b32 {{{', '.join(w)}}}, [{a}];")
+                    else:
+                        elems = k.regs("r", CE)
+                        for e in range(CE):
+                            ke = k.reg("r")
+                            k(f"add.u32 {ke}, {kk}, {e};")
+                            ok = k.reg("p")
+                            k(f"setp.lt.and.u32 {ok}, {ke}, {kend}, {live};")
+                            ei = k.reg("r")
+                            if which == "A":
+                                k(f"mad.lo.u32 {ei}, {g}, {K}, {ke};")
+                            else:
+                                k(f"mad.lo.u32 {ei}, {ke}, {N}, {g};")
+                            load_elem(abase if which == "A" else bbase, ei, ok, elems[e])
+                        words = elems if es == 4 else [pack16(elems[2 * x], elems[2 * x + 1])
+                                                       for x in range(4)]
+                        for r_, x in zip(w, words):
+                            k(f"mov.b32 {r_}, {x};")
+                    out.append((which, row, ch, live, w))
+            return out
+
+        def put(chunks, buf):
+            """Store fetched chunks into slab buffer ``buf`` (swizzled; with
+            their low tf32 parts for fp32 operands)."""
+            base = k.reg("r")
+            k(f"mad.lo.u32 {base}, {buf}, {self.buf}, {sm};")
+            for which, row, ch, live, w in chunks:
+                sk = k.label("NO_CHUNK")
+                k(f"@!{live} bra {sk};")
+                off = swz(row, ch)
+                if which == "B":
+                    k(f"add.u32 {off}, {off}, {self.sa * (2 if tf32 else 1)};")
+                store_chunk(base, off, w, self.sa if which == "A" else self.sb)
+                k.mark(sk)
             k("fence.proxy.async.shared::cta;")
 
         def mma(slab, buf, nsteps):
@@ -567,39 +560,34 @@ class GemmSmallTemplate:
             wait(k, bar, ph, status, 2, teardown)
 
         nslab = -(-KC // KB)
-        full = KC // KB                       # slabs with KB k each
-        tail_k = KC - full * KB
         s = k.reg("r")
         bufr = k.reg("r")
         k(f"mov.u32 {s}, 0;")
-        if full:
-            top = k.label("SLAB")
-            k.mark(top)
-            k(f"rem.u32 {bufr}, {s}, {self.nbuf};")
-            pw = k.reg("p")
-            k(f"setp.ge.u32 {pw}, {s}, {self.nbuf};")
-            skw = k.label("NO_WAIT")
-            k(f"@!{pw} bra {skw};")
-            prev = k.reg("r")
-            k(f"sub.u32 {prev}, {s}, {self.nbuf};")
-            wait_slab(prev)                   # the buffer's previous MMAs are done
-            k.mark(skw)
-            stage(s, bufr)
-            k("bar.sync 0;")
-            mma(s, bufr, KB // KMMA)
-            k(f"add.u32 {s}, {s}, 1;")
-            pl = k.reg("p")
-            k(f"setp.lt.u32 {pl}, {s}, {full};")
-            k(f"@{pl} bra {top};")
-        if tail_k:
-            k(f"rem.u32 {bufr}, {s}, {self.nbuf};")
-            if full >= self.nbuf:
-                prev = k.reg("r")
-                k(f"sub.u32 {prev}, {s}, {self.nbuf};")
-                wait_slab(prev)
-            stage(s, bufr)
-            k("bar.sync 0;")
-            mma(s, bufr, -(-tail_k // KMMA))
+        chunks = fetch(s)
+        top = k.label("SLAB")
+        k.mark(top)
+        k(f"rem.u32 {bufr}, {s}, {self.nbuf};")
+        pw = k.reg("p")
+        k(f"setp.ge.u32 {pw}, {s}, {self.nbuf};")
+        skw = k.label("NO_WAIT")
+        k(f"@!{pw} bra {skw};")
+        prev = k.reg("r")
+        k(f"sub.u32 {prev}, {s}, {self.nbuf};")
+        wait_slab(prev)                       # the buffer's previous MMAs are done
+        k.mark(skw)
+        put(chunks, bufr)
+        k("bar.sync 0;")
+        nxt = k.reg("r")
+        k(f"add.u32 {nxt}, {s}, 1;")
+        pn = k.reg("p")
+        k(f"setp.lt.u32 {pn}, {nxt}, {nslab};")
+        skf = k.label("NO_FETCH")
+        k(f"@!{pn} bra {skf};")
+        fetch(nxt, chunks)                    # in flight while the MMAs run
+        k.mark(skf)
+        mma(s, bufr, KB // KMMA)
+        k(f"mov.u32 {s}, {nxt};")
+        k(f"@{pn} bra {top};")
         last = k.reg("r")
         k(f"mov.u32 {last}, {nslab - 1};")
         wait_slab(last)                       # MMAs complete in order: all done
