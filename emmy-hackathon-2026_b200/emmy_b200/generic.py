@@ -115,6 +115,7 @@ class GenericLowering:
             else:
                 self.base[a] = k.param_ptr(a)
         self.tmaps = {}      # TmaDescriptor name -> (param address register, info)
+        self.cells = {}      # (carrier, index) -> [state register, next register, type]
         self._declare_mbarriers(ctx.tile)
         self.compile_tile(ctx.tile)
         k("ret;")
@@ -186,6 +187,7 @@ class GenericLowering:
             p = k.reg("p")
             k(f"setp.ge.u64 {p}, {gid64}, {ncells};")
             k(f"@{p} bra {done};")
+        self.gid64 = gid64
         self.decode(tile, gid64, extents)
         self.body(tile.body)
         k.mark(done)
@@ -467,7 +469,10 @@ class GenericLowering:
                     self.vals[nxt.name] = (reg, ty)
                     i += 2
                     continue
-            getattr(self, "s_" + kind(s), self.s_unsupported)(s)
+            if isinstance(s, _StepMark):
+                self._step(s.cells, s.begin)
+            else:
+                getattr(self, "s_" + kind(s), self.s_unsupported)(s)
             i += 1
 
     @staticmethod
@@ -718,10 +723,139 @@ class GenericLowering:
 
     UNROLL_CAP = 128
 
+    # ---------------------------------------------------------- carried state
+    # TASK.md's Carry / Pre (defined by the IR vocabulary, lowered by no
+    # reference code): a carried-state cell is named by its carrier and a
+    # literal index; its loop is the innermost loop around the Carry, whose
+    # iterations are the steps.  Each step starts with next = state (cells
+    # no Carry of the step sets keep their values), Carry sets next, Pre
+    # reads state (the previous step's value, the seed on the first step),
+    # and the step ends with state = next; after the loop Pre reads the final
+    # value.
+    def _cell_key(self, carrier, index):
+        key = []
+        for e in index or ():
+            v = self.ival(e)
+            if not _is_imm(v):
+                raise NotImplementedError("carried-state cell with a run-time index")
+            key.append(int(v))
+        return (carrier, tuple(key))
+
+    def _carries(self, body):
+        """Carry statements of this loop's steps (not of nested loops)."""
+        out = []
+        for st in body:
+            kd = kind(st)
+            if kd == "Carry":
+                out.append(st)
+            elif kd == "Cond":
+                out += self._carries(st.body) + self._carries(st.else_body or ())
+        return out
+
+    def _open_cells(self, body):
+        """Create (state = seed) the cells this loop carries; return them."""
+        k = self.k
+        cells = []
+        for st in self._carries(body):
+            key = self._cell_key(st.name, st.index)
+            if key not in self.cells:
+                ty = _calc_ty(st.dtype.name if st.dtype is not None else "f32")
+                state, nxt = k.reg(REG[ty]), k.reg(REG[ty])
+                lit = float(st.seed) if ty in ("f32", "f64") else int(st.seed)
+                if ty == "f32":
+                    k(f"mov.f32 {state}, {f32_hex(lit)};")
+                elif ty == "f64":
+                    k(f"mov.f64 {state}, {f64_hex(lit)};")
+                else:
+                    k(f"mov.{PTY[ty]} {state}, {lit};")
+                self.cells[key] = [state, nxt, ty]
+            if key not in cells:
+                cells.append(key)
+        return cells
+
+    def _step(self, cells, begin: bool):
+        for key in cells:
+            state, nxt, ty = self.cells[key]
+            mv = MOVTY[REG[ty]]
+            if begin:
+                self.k(f"mov.{mv} {nxt}, {state};")
+            else:
+                self.k(f"mov.{mv} {state}, {nxt};")
+
+    def s_Carry(self, s):
+        key = self._cell_key(s.name, s.index)
+        if key not in self.cells:        # a Carry outside any loop: one step
+            self._open_cells((s,))
+            self._step([key], True)
+        _, nxt, ty = self.cells[key]
+        v, vty = self.vals[s.value] if isinstance(s.value, str) else \
+            (f32_hex(float(s.value.value)), "f32")
+        v = self.convert(v, vty, ty)
+        self.k(f"mov.{MOVTY[REG[ty]]} {nxt}, {v};")
+
+    def s_Pre(self, s):
+        key = self._cell_key(s.carrier, s.index)
+        if key not in self.cells:
+            raise NotImplementedError(f"Pre of {s.carrier} before any Carry of it")
+        state, _, ty = self.cells[key]
+        r = self.k.reg(REG[ty])
+        self.k(f"mov.{MOVTY[REG[ty]]} {r}, {state};")
+        self.vals[s.name] = (r, ty)
+
+    def s_Select(self, s):
+        """``name`` = the value of the branch whose coordinate predicate holds
+        (TASK.md ``Select``: branches of (value, select)); evaluated as a
+        chain of selects from the last branch back, so the first branch
+        whose predicate holds wins."""
+        k = self.k
+        branches = [(b.value, b.select) if hasattr(b, "select") else (b[0], b[1])
+                    for b in s.branches]
+        if not branches:
+            raise NotImplementedError("Select without branches")
+        vals = []
+        for v, _ in branches:
+            if isinstance(v, str):
+                vals.append(self.vals[v])
+            else:
+                vals.append((self.fval(v, "f32"), "f32"))
+        ty = vals[0][1]
+        r = k.reg(REG[ty])
+        k(f"mov.{MOVTY[REG[ty]]} {r}, {self.convert(vals[-1][0], vals[-1][1], ty)};")
+        for (v, vty), (_, sel) in list(zip(vals, branches))[-2::-1]:
+            p = self.pred(sel)
+            k(f"selp.{'b32' if REG[ty] in ('f', 'r') else 'b64'} {r}, "
+              f"{self.convert(v, vty, ty)}, {r}, {p};")
+        self.vals[s.name] = (r, ty)
+
+    def s_ZeroPrologue(self, s):
+        """Zero ``words`` 32-bit words of buffer ``dst`` (another kernel's
+        atomic accumulator), every thread of the grid a strided share, in
+        place of a memset before that kernel (TASK.md ``ZeroPrologue``)."""
+        k = self.k
+        words = int(s.words.value if hasattr(s.words, "value") else s.words)
+        total = self.ctx.total_threads
+        i = k.reg("rd")
+        k(f"mov.u64 {i}, {self.gid64};")
+        top, out = k.label("ZERO"), k.label("ZERO_END")
+        k.mark(top)
+        p = k.reg("p")
+        k(f"setp.ge.u64 {p}, {i}, {words};")
+        k(f"@{p} bra {out};")
+        a = k.reg("rd")
+        k(f"shl.b64 {a}, {i}, 2;")
+        k(f"add.s64 {a}, {a}, {self.base[s.dst]};")
+        k(f"st.global.b32 [{a}], 0;")
+        k(f"add.s64 {i}, {i}, {total};")
+        k(f"bra {top};")
+        k.mark(out)
+
     def _loop(self, axis, start, step, end, body, seed):
         k = self.k
         if seed:
             self.init_accumulators(body)
+        cells = self._open_cells(body)
+        if cells:
+            body = (_StepMark(cells, True),) + tuple(body) + (_StepMark(cells, False),)
         name = axis.name
         saved = self.ints.get(name)
         if _is_imm(start) and _is_imm(step) and _is_imm(end) and int(step) > 0:
@@ -1415,6 +1549,13 @@ class GenericLowering:
 def I_Var(name):
     from .ir import NODE_CLASSES
     return NODE_CLASSES["Var"](name)
+
+
+class _StepMark:
+    """An internal statement at the start / end of a carrying loop's body."""
+
+    def __init__(self, cells, begin):
+        self.cells, self.begin = cells, begin
 
 
 def _is_imm(x) -> bool:

@@ -812,3 +812,66 @@ def mbarrier_timeout(n: int = 1024, block: int = 128) -> Problem:
     p.grid, p.block = (n // block, 1, 1), (block, 1, 1)
     p.rtol, p.atol = 0, 0
     return p
+
+
+# --------------------------------------------------------------------------
+# IR nodes the vocabulary defines but no reference IR uses (TASK.md rows
+# marked *): small IRs written from the table's own descriptions
+# --------------------------------------------------------------------------
+
+def carried_prefix(rows: int = 64, cols: int = 96, every: int = 1, block: int = 64) -> Problem:
+    """``Carry``/``Pre``: one thread per row steps through the columns with a
+    carried cell ``c`` (seed 0): each step reads the previous state, and on
+    steps where ``col % every == 0`` sets ``c = previous + x[row, col]``;
+    ``y[row, col]`` is the state the step read -- the sum of the earlier
+    columns that set it (other steps leave the cell as it was)."""
+    p = Problem(f"carry_{rows}x{cols}_{every}", "exclusive prefix sum over every-th column",
+                "k_carry", "y")
+    p.add_input("x", (rows, cols))
+    p.out = ("y", (rows, cols), "f32")
+    step = [load("xv", "x", V("a0"), V("j")),
+            I.Pre("prev", "c", ()),
+            I.Cond(eq(I.BinaryExpr("%", V("j"), Lit(every)), Lit(0)),
+                   (assign("nxt", "add", "prev", "xv"), I.Carry("c", "nxt", (), 0.0, F32)), ()),
+            I.Pre("seen", "c", ()),
+            write("y", (V("a0"), V("j")), ("seen",))]
+    p.body = tile([axis("a0", rows)], [I.Loop(axis("j", cols), tuple(step), False, False)])
+    p.grid, p.block = (-(-rows // block), 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 1e-5, 1e-5
+    p.oracle = {"family": "carried_prefix", "args": {"x": "x"}, "output": "y", "every": every}
+    return p
+
+
+def select_branches(n: int = 4096, split: int = 1000, block: int = 256) -> Problem:
+    """``Select``: y[i] = x[i] where i < split, else x[i] * x[i] -- the value
+    of the branch whose coordinate predicate holds."""
+    p = Problem(f"select_{n}", "where(i < split, x, x*x)", "k_select", "y")
+    p.add_input("x", (n,))
+    p.out = ("y", (n,), "f32")
+    lt = I.BinaryExpr("<", V("a0"), Lit(split))
+    ge = I.BinaryExpr(">=", V("a0"), Lit(split))
+    p.body = tile([axis("a0", n)], [load("xv", "x", V("a0")), assign("sq", "multiply", "xv", "xv"),
+                                    I.Select("v", (("xv", lt), ("sq", ge))),
+                                    write("y", (V("a0"),), ("v",))])
+    p.grid, p.block = (-(-n // block), 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 0, 0
+    p.oracle = {"family": "select", "args": {"x": "x"}, "output": "y", "split": split}
+    return p
+
+
+def zero_prologue(words: int = 100_000, n: int = 4096, block: int = 128) -> Problem:
+    """``ZeroPrologue``: the kernel zeroes the first ``words`` words of its
+    output ``acc`` (another kernel's atomic accumulator in the vocabulary's
+    use), every thread of the grid a strided share, and then adds x[i] into
+    acc[i] atomically for its own cell."""
+    p = Problem(f"zero_prologue_{words}", "acc[:words] = 0, then acc[:n] += x", "k_zero_pro",
+                "acc")
+    p.add_input("x", (n,))
+    p.out = ("acc", (max(words, n),), "f32")
+    p.body = tile([axis("a0", n)], [I.ZeroPrologue("acc", words), I.Sync(0, None, False),
+                                    load("xv", "x", V("a0")),
+                                    write("acc", (V("a0"),), ("xv",), atomic=True)])
+    p.grid, p.block = (-(-n // block), 1, 1), (block, 1, 1)
+    p.rtol, p.atol = 0, 0
+    p.oracle = {"family": "zero_prologue", "args": {"x": "x"}, "output": "acc", "words": words}
+    return p

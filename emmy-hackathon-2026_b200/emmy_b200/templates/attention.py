@@ -83,6 +83,13 @@ class AttentionTemplate:
     # j overlaps it.  At D = 128 the columns do not fit: P overwrites S and
     # the tile's next Q K^T waits for its P V.
     SPLIT_P = {64: True, 128: False}
+    # head dims whose CTAs run in pairs (a cluster of 2 over neighbouring
+    # 256-row query blocks of one (batch, head)): the leader's one thread
+    # issues tcgen05.mma.cta_group::2 (M = 256: each CTA's 128 rows of a tile
+    # in its own TMEM), each CTA loads half of every K block (64 keys) and
+    # half of every V block (D/2 columns), so per SM the MMA issue -- the
+    # measured limiter -- and the K/V shared-memory traffic halve
+    PAIR = {64: False, 128: True}
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -177,6 +184,12 @@ class AttentionTemplate:
             raise TemplateMismatch("meta smem_bytes too small for 2+2 K/V stages")
         self.SK, self.SV = (n + 1) // 2, n // 2
         self.split_p = bool(cls.SPLIT_P.get(D, False)) and self.NT * (128 + 64 + D) <= 512
+        self.pair = (bool(cls.PAIR.get(D, False)) and not self.split_p and self.NT == 2
+                     and (S // 256) % 2 == 0 and tuple(ctx.grid[1:]) == (1, 1))
+        if self.pair:
+            # K and V stages hold half a block each: twice as many fit
+            n = min(12, avail // (TB // 2))
+            self.SK, self.SV = (n + 1) // 2, n // 2
         return self
 
     # ------------------------------------------------------------------- emit
@@ -187,17 +200,25 @@ class AttentionTemplate:
         QB = S // (128 * NT)               # CTAs per (batch, head)
         TB = self.tile_bytes               # one 128 x D bf16 tile
         NBX = D // 64                      # 64-column boxes per tile
+        pair = self.pair
+        TBK = TB // 2 if pair else TB      # a K stage: 64 or 128 keys x D
+        TBV = TB // 2 if pair else TB      # a V stage: 128 keys x D/2 or D columns
+        KBOX = 64 * 128 if pair else 128 * 128   # bytes of one 64-column K box
         params = ctx.params() + [("tmapQ", ".align 64 .b8", "[128]"),
                                  ("tmapK", ".align 64 .b8", "[128]"),
                                  ("tmapV", ".align 64 .b8", "[128]")]
         k = Kernel(ctx.entry, params)
         k.maxntid = (512, 1, 1)
+        if pair:
+            k.reqnctapercluster = (2, 1, 1)
+            k.directive("cluster 2 1 1")
         k.decl(".extern .shared .align 1024 .b8 __emmy_smem[];")
         k.decl(".global .align 4 .u32 __emmy_status;")
         rows = self.B * self.H * S
         for nm, buf in (("tmapQ", self.q), ("tmapK", self.k), ("tmapV", self.v)):
+            bk = 64 if pair and nm == "tmapK" else 128
             k.directive(f"tmap {nm} buf={buf} dtype=9 dims={D},{rows} strides={D * 2} "
-                        f"box=64,128 swizzle=3")
+                        f"box=64,{bk} swizzle=3")
         k.comment(f"emmy-b200 template: tcgen05 flash attention B={self.B} H={self.H} S={S} "
                   f"D={D}, {NT} query tile(s) per CTA")
         obase = k.param_ptr(self.out)
@@ -221,6 +242,10 @@ class AttentionTemplate:
         qrow0 = k.reg("r")
         k(f"mad.lo.u32 {qrow0}, {qb}, {128 * NT}, {krow0};")
         SK, SV = self.SK, self.SV
+        if pair:
+            rank = k.special("%cluster_ctarank")
+            plead = k.reg("p")
+            k(f"setp.eq.u32 {plead}, {rank}, 0;")
         # shared memory: Q tiles | K ring (SK tiles) | V ring (SV tiles) |
         # barriers | tmem slot
         raw = k.reg("r")
@@ -231,9 +256,9 @@ class AttentionTemplate:
         kring = k.reg("r")
         k(f"add.u32 {kring}, {qs}, {NT * TB};")
         vring = k.reg("r")
-        k(f"add.u32 {vring}, {kring}, {SK * TB};")
+        k(f"add.u32 {vring}, {kring}, {SK * TBK};")
         bars = k.reg("r")
-        k(f"add.u32 {bars}, {vring}, {SV * TB};")
+        k(f"add.u32 {bars}, {vring}, {SV * TBV};")
         # barrier slots
         Q_FULL = 0
         K_FULL, K_EMPTY = 1, 1 + SK
@@ -267,7 +292,8 @@ class AttentionTemplate:
             if split:
                 cnt = 4 * NT if slot in (P_READY, S_FREE) else 1
             else:
-                cnt = 4 if P_READY <= slot < P_READY + NT else 1
+                # pair: the leader's P_READY counts both CTAs' softmax warps
+                cnt = (8 if pair else 4) if P_READY <= slot < P_READY + NT else 1
 
             k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * slot}], {cnt};")
         k("fence.mbarrier_init.release.cluster;")
@@ -278,11 +304,17 @@ class AttentionTemplate:
         k(f"setp.eq.u32 {pwm}, {warp}, {MMA_WARP};")
         skip2 = k.label("SKIP_ALLOC")
         k(f"@!{pwm} bra {skip2};")
-        k(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{tslot}], 512;")
-        k("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;")
+        cg = "cta_group::2" if pair else "cta_group::1"
+        # a pair allocates collectively: the same 512 columns in both CTAs
+        k(f"tcgen05.alloc.{cg}.sync.aligned.shared::cta.b32 [{tslot}], 512;")
+        k(f"tcgen05.relinquish_alloc_permit.{cg}.sync.aligned;")
         k.mark(skip2)
         k("tcgen05.fence::before_thread_sync;")
         k("bar.sync 0;")
+        if pair:
+            # both CTAs' barriers and tensor memory exist before any cross-CTA use
+            k("barrier.cluster.arrive.release.aligned;")
+            k("barrier.cluster.wait.acquire.aligned;")
         k("tcgen05.fence::after_thread_sync;")
         tmem = k.reg("r")
         k(f"ld.shared.u32 {tmem}, [{tslot}];")
@@ -330,8 +362,21 @@ class AttentionTemplate:
             k(f"and.b32 {ph_}, {ph_}, 1;")
             return st_, ph_
 
-        def commit(addr):
-            k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{addr}];")
+        if pair:
+            cmask = k.reg("h")
+            k(f"mov.b16 {cmask}, 3;")
+
+        def commit(addr, local=False):
+            """Arrive on ``addr`` once this thread's MMAs so far complete; a
+            pair's leader signals the barrier at that offset in both CTAs."""
+            if pair and not local:
+                k(f"tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster"
+                  f".multicast::cluster.b64 [{addr}], {cmask};")
+            elif pair:
+                k(f"tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [{addr}];")
+            else:
+                k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+                  f"[{addr}];")
 
         j = k.reg("r")
 
@@ -341,16 +386,30 @@ class AttentionTemplate:
             k(f"and.pred {pp}, {pp}, {pl0};")
             end_p = k.label(f"END_{which}")
             k(f"@!{pp} bra {end_p};")
+            # a pair's copies complete on the LEADER's barriers (mapa address),
+            # which the leader arms with both CTAs' bytes
+            cpy = ("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier"
+                   "::complete_tx::bytes" if pair else
+                   "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes")
+            arm = f"@{plead} " if pair else ""
+            ncta = 2 if pair else 1
+
+            def target(addr):
+                if not pair:
+                    return addr
+                r = k.reg("r")
+                k(f"mapa.shared::cluster.u32 {r}, {addr}, 0;")
+                return r
             if load_q:
                 qf = bar(Q_FULL)
-                k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qf}], {NT * TB};")
+                k(f"{arm}mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qf}], {ncta * NT * TB};")
+                qft = target(qf)
                 for t in range(NT):
                     qr = k.reg("r")
                     k(f"add.u32 {qr}, {qrow0}, {128 * t};")
                     for i in range(NBX):
-                        k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx"
-                          f"::bytes [{qs}+{t * TB + i * 16384}], [{tq}, {{{64 * i}, {qr}}}], "
-                          f"[{qf}];")
+                        k(f"{cpy} [{qs}+{t * TB + i * 16384}], [{tq}, {{{64 * i}, {qr}}}], "
+                          f"[{qft}];")
             k(f"mov.u32 {j}, 0;")
             top = k.label(f"PROD_{which}")
             k.mark(top)
@@ -375,13 +434,28 @@ class AttentionTemplate:
                 wait(k, bar(empty, st_), par, status, 1, end_p)
             kr = k.reg("r")
             k(f"mad.lo.u32 {kr}, {j}, 128, {krow0};")
+            stage = TBK if which == "K" else TBV
             dst = k.reg("r")
-            k(f"mad.lo.u32 {dst}, {st_}, {TB}, {ring};")
+            k(f"mad.lo.u32 {dst}, {st_}, {stage}, {ring};")
             fb = bar(full, st_)
-            k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {TB};")
-            for i in range(NBX):
-                k(f"cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-                  f"[{dst}+{i * 16384}], [{tmap}, {{{64 * i}, {kr}}}], [{fb}];")
+            k(f"{arm}mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {ncta * stage};")
+            fbt = target(fb)
+            if pair and which == "K":
+                # this CTA's 64 keys of the block, all D columns
+                k(f"mad.lo.u32 {kr}, {rank}, 64, {kr};")
+                for i in range(NBX):
+                    k(f"{cpy} [{dst}+{i * KBOX}], [{tmap}, {{{64 * i}, {kr}}}], [{fbt}];")
+            elif pair:
+                # all 128 keys of the block, this CTA's D/2 columns
+                c0 = k.reg("r")
+                k(f"mul.lo.u32 {c0}, {rank}, {D // 2};")
+                for i in range(NBX // 2):
+                    ci = k.reg("r")
+                    k(f"add.u32 {ci}, {c0}, {64 * i};")
+                    k(f"{cpy} [{dst}+{i * 16384}], [{tmap}, {{{ci}, {kr}}}], [{fbt}];")
+            else:
+                for i in range(NBX):
+                    k(f"{cpy} [{dst}+{i * 16384}], [{tmap}, {{{64 * i}, {kr}}}], [{fbt}];")
             k.comment(f"@trace {10 if load_q else 11} {j}")
             k(f"add.u32 {j}, {j}, 1;")
             pl = k.reg("p")
@@ -397,13 +471,16 @@ class AttentionTemplate:
         pm = k.reg("p")
         k(f"setp.eq.u32 {pm}, {warp}, {MMA_WARP};")
         k(f"and.pred {pm}, {pm}, {pl0};")
+        if pair:
+            k(f"and.pred {pm}, {pm}, {plead};")      # the leader's thread issues for both
         end_mma = k.label("END_MMA")
         skip_mma = k.label("SKIP_MMA")
         k(f"@!{pm} bra {skip_mma};")
+        MM = 256 if pair else 128                    # rows per MMA: a pair's both tiles
         iqk = k.reg("r")
-        k(f"mov.u32 {iqk}, {idesc_mma(128, 128, False)};")
+        k(f"mov.u32 {iqk}, {idesc_mma(MM, 128, False)};")
         ipv = k.reg("r")
-        k(f"mov.u32 {ipv}, {idesc_mma(128, D, True)};")
+        k(f"mov.u32 {ipv}, {idesc_mma(MM, D, True)};")
         hiK = _desc_hi(16, 1024)
         hiV = _desc_hi(16384, 1024)
         ptrue = k.reg("p")
@@ -425,18 +502,19 @@ class AttentionTemplate:
             wait(k, bar(K_FULL, kst), kph, status, 2, end_mma)
             k("tcgen05.fence::after_thread_sync;")
             kad = k.reg("r")
-            k(f"mad.lo.u32 {kad}, {kst}, {TB}, {kring};")
+            k(f"mad.lo.u32 {kad}, {kst}, {TBK}, {kring};")
             return GemmTemplate._desc(k, kad, hiK), kst
 
         def issue_qk(t, dk, jreg, do_commit=True):
             """S_t = Q_t K^T (overwrites the tile's score buffer)."""
             for kk in range(D // 16):
-                off = (kk % 4) * 2 + (kk // 4) * 1024
+                off = (kk % 4) * 2 + (kk // 4) * 1024        # +32 B along K; next box
+                offk = (kk % 4) * 2 + (kk // 4) * (KBOX // 16)
                 a = k.reg("rd")
                 k(f"add.s64 {a}, {dq[t]}, {off};")
                 bd = k.reg("rd")
-                k(f"add.s64 {bd}, {dk}, {off};")
-                k(f"tcgen05.mma.cta_group::1.kind::f16 [{s_tm[t]}], {a}, {bd}, {iqk}, "
+                k(f"add.s64 {bd}, {dk}, {offk};")
+                k(f"tcgen05.mma.{cg}.kind::f16 [{s_tm[t]}], {a}, {bd}, {iqk}, "
                   f"{pfalse if kk == 0 else ptrue};")
             if do_commit:
                 commit(bar(S_FULL + t))
@@ -450,7 +528,7 @@ class AttentionTemplate:
                 k(f"add.u32 {a}, {p_tm[t]}, {8 * kk};")  # 16 bf16 = 8 TMEM columns
                 bd = k.reg("rd")
                 k(f"add.s64 {bd}, {dv}, {kk * 128};")   # +16 key rows * 128 B
-                k(f"tcgen05.mma.cta_group::1.kind::f16 [{o_tm[t]}], [{a}], {bd}, {ipv}, "
+                k(f"tcgen05.mma.{cg}.kind::f16 [{o_tm[t]}], [{a}], {bd}, {ipv}, "
                   f"{pacc if kk == 0 else ptrue};")
 
         s_tm, o_tm, p_tm = [], [], []
@@ -488,7 +566,7 @@ class AttentionTemplate:
             k.comment(f"@trace 8 {j}")
             k("tcgen05.fence::after_thread_sync;")
             vad = k.reg("r")
-            k(f"mad.lo.u32 {vad}, {vst}, {TB}, {vring};")
+            k(f"mad.lo.u32 {vad}, {vst}, {TBV}, {vring};")
             dv = GemmTemplate._desc(k, vad, hiV)
             k(f"setp.ne.u32 {pacc}, {j}, 0;")
             k(f"and.b32 {par}, {j}, 1;")
@@ -500,7 +578,8 @@ class AttentionTemplate:
                 dk, kst = k_ready(jn)
                 k.comment(f"@trace 9 {jn}")
             for t in range(NT):
-                wait(k, bar(P_READY + t), par, status, 2, end_mma)
+                wait(k, bar(P_READY + t), par, status, 2, end_mma,
+                     ".acquire.cluster" if pair else "")
                 k.comment(f"@trace {3 * t + 1} {j}")
                 k("tcgen05.fence::after_thread_sync;")
                 issue_pv(t, dv, pacc)
@@ -537,7 +616,7 @@ class AttentionTemplate:
             wait(k, bar(V_FULL, vst), vph, status, 2, end_mma)
             k.comment(f"@trace 8 {j}")
             vad = k.reg("r")
-            k(f"mad.lo.u32 {vad}, {vst}, {TB}, {vring};")
+            k(f"mad.lo.u32 {vad}, {vst}, {TBV}, {vring};")
             dv = GemmTemplate._desc(k, vad, hiV)
             k(f"setp.ne.u32 {pacc}, {j}, 0;")
             wait(k, bar(P_READY), par, status, 2, end_mma)
@@ -565,7 +644,7 @@ class AttentionTemplate:
         k.mark(end_mma)
         # wait (bounded) for this thread's tensor-core operations still in
         # flight, so that no MMA outlives the TMEM allocation on an error path
-        commit(bar(DRAIN))
+        commit(bar(DRAIN), local=True)
         wait(k, bar(DRAIN), zero, status, 6, skip_mma)
         k.mark(skip_mma)
         k(f"bra {teardown};")
@@ -690,13 +769,23 @@ class AttentionTemplate:
                 k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{orow_tm}+{32 * c}], "
                   f"{{{', '.join(ov)}}};")
 
+        if pair:
+            # the P_READY the leader's issuing thread waits on
+            lpready = k.reg("r")
+            k(f"mapa.shared::cluster.u32 {lpready}, {pready}, 0;")
+
         def p_ready_arrive():
             """This warp's P (and O) stores are complete: one arrival per warp
-            on the tile's P_READY barrier (lane 0, after the warp converges)."""
+            on the tile's P_READY barrier (lane 0, after the warp converges);
+            in a pair, on the leader's, with release semantics for the
+            cluster (the leader's MMA reads this CTA's TMEM)."""
             k("tcgen05.wait::st.sync.aligned;")
             k("tcgen05.fence::before_thread_sync;")
             k("bar.warp.sync 0xffffffff;")
-            k(f"@{pl0} mbarrier.arrive.shared::cta.b64 _, [{pready}];")
+            if pair:
+                k(f"@{pl0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{lpready}];")
+            else:
+                k(f"@{pl0} mbarrier.arrive.shared::cta.b64 _, [{pready}];")
 
         def row_sum(ps2):
             k(f"add.rn.f32x2 {ps2[0]}, {ps2[0]}, {ps2[1]};")
@@ -869,17 +958,23 @@ class AttentionTemplate:
         k.mark(soft_teardown)
         k("tcgen05.fence::before_thread_sync;")
         k("barrier.sync 0;")
+        if pair:   # the peer may still use this CTA's memory until it arrives too
+            k("barrier.cluster.arrive.release;")
+            k("barrier.cluster.wait.acquire;")
         k("ret;")
 
         # ---------------- teardown of the other warps ----------------
         k.mark(teardown)
         k("tcgen05.fence::before_thread_sync;")
         k("barrier.sync 0;")
+        if pair:
+            k("barrier.cluster.arrive.release;")
+            k("barrier.cluster.wait.acquire;")
         end = k.label("END")
         k(f"@!{pwm} bra {end};")
         k("bar.warp.sync 0xffffffff;")
         k("tcgen05.fence::after_thread_sync;")
-        k(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tmem}, 512;")
+        k(f"tcgen05.dealloc.{cg}.sync.aligned.b32 {tmem}, 512;")
         k.mark(end)
         k("ret;")
         return k.render()

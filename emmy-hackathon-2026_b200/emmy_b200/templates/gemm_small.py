@@ -76,6 +76,213 @@ def _guard_bounds(cond) -> list:
     raise NotAffine("guard")
 
 
+def block_indices(k, cta, tile, block_axes) -> dict:
+    """Registers holding each block axis's index for CTA ``cta``, as the
+    reference decodes the flat thread index when the thread axes fill the CTA
+    (``compile.py:2385-2466``): row-major over the block axes, except that a
+    grouped rasterisation (``raster_group`` >= 2 over two adjacent axes whose
+    grouped one has an extent above 1) numbers ``g`` block rows of the
+    grouped axis fastest within each stripe of the other, with a short last
+    group when the extent is not a multiple of ``g``."""
+    names = [n for n, _ in block_axes]
+    ext = dict(block_axes)
+    out = {}
+    raster = None
+    rg, ra = getattr(tile, "raster_group", None), getattr(tile, "raster_axes", None)
+    if rg and ra and ra[0] in names and ra[1] in names:
+        mi, ni = names.index(ra[0]), names.index(ra[1])
+        if ni == mi + 1:
+            gi, oi = (mi, ni) if getattr(tile, "raster_orient", None) == "m" else (ni, mi)
+            g = min(rg, ext[names[gi]])
+            if ext[names[gi]] > 1 and g > 1:
+                raster = (gi, oi, g)
+
+    def after(i):
+        p = 1
+        for n in names[i + 1:]:
+            p *= ext[n]
+        return p
+    for i, n in enumerate(names):
+        if raster is not None and i in raster[:2]:
+            continue
+        r = k.reg("r")
+        if ext[n] == 1:
+            k(f"mov.u32 {r}, 0;")
+        else:
+            k(f"div.u32 {r}, {cta}, {after(i)};")
+            if i:
+                k(f"rem.u32 {r}, {r}, {ext[n]};")
+        out[n] = r
+    if raster is not None:
+        gi, oi, g = raster
+        ea, eb = ext[names[gi]], ext[names[oi]]
+        mi, ni = min(gi, oi), max(gi, oi)
+        sub = k.reg("r")
+        k(f"div.u32 {sub}, {cta}, {after(ni)};")
+        if mi != 0:
+            k(f"rem.u32 {sub}, {sub}, {ea * eb};")
+        a, b = k.reg("r"), k.reg("r")
+        if ea % g == 0:
+            t = k.reg("r")
+            k(f"div.u32 {t}, {sub}, {g * eb};")
+            k(f"rem.u32 {a}, {sub}, {g};")
+            k(f"mad.lo.u32 {a}, {t}, {g}, {a};")
+            k(f"rem.u32 {b}, {sub}, {g * eb};")
+            k(f"div.u32 {b}, {b}, {g};")
+        else:
+            grp, rem, rsz = k.reg("r"), k.reg("r"), k.reg("r")
+            k(f"div.u32 {grp}, {sub}, {g * eb};")
+            k(f"rem.u32 {rem}, {sub}, {g * eb};")
+            k(f"mul.lo.u32 {rsz}, {grp}, {g};")
+            k(f"sub.u32 {rsz}, {ea}, {rsz};")
+            k(f"min.u32 {rsz}, {rsz}, {g};")
+            k(f"rem.u32 {a}, {rem}, {rsz};")
+            k(f"mad.lo.u32 {a}, {grp}, {g}, {a};")
+            k(f"div.u32 {b}, {rem}, {rsz};")
+        out[names[gi]], out[names[oi]] = a, b
+    return out
+
+
+class Stager:
+    """A CTA's threads staging row-major global operands, 16 bytes at a time,
+    into the 128-byte-swizzle K-major layout a tcgen05 shared-memory
+    descriptor reads (8-row atoms of 1024 bytes; the 16-byte chunk c of row
+    r at chunk c ^ (r % 8)).  A slab is 128 bytes of K per row (32 fp32 or
+    64 bf16).  ``fetch`` issues one slab's loads into registers (they stay in
+    flight until ``put`` stores them); for fp32 operands ``put`` also writes
+    the low tf32 parts lo = x - (x with its 13 low mantissa bits cleared)
+    at ``lo_off`` bytes from each chunk (3xTF32)."""
+
+    def __init__(self, k, tid, T, es, tf32):
+        self.k, self.tid, self.T, self.es, self.tf32 = k, tid, T, es, tf32
+        self.CE = 16 // es               # elements per 16-byte chunk
+        self.KB = 128 // es              # k per slab
+
+    def swz(self, row, ch):
+        """Byte offset of 16-byte chunk ``ch`` of row ``row``."""
+        k = self.k
+        o = k.reg("r")
+        k(f"and.b32 {o}, {row}, 7;")
+        x = k.reg("r")
+        k(f"xor.b32 {x}, {ch}, {o};")
+        k(f"shl.b32 {x}, {x}, 4;")
+        k(f"shl.b32 {o}, {o}, 7;")
+        k(f"add.u32 {x}, {x}, {o};")
+        a = k.reg("r")
+        k(f"shr.u32 {a}, {row}, 3;")
+        k(f"mad.lo.u32 {x}, {a}, 1024, {x};")
+        return x
+
+    def store_chunk(self, dst, off, vals, lo_off):
+        k = self.k
+        a = k.reg("r")
+        k(f"add.u32 {a}, {dst}, {off};")
+        k(f"st.shared.v4.b32 [{a}], {{{', '.join(vals)}}};")
+        if self.tf32:
+            lo = []
+            for v in vals:
+                m_ = k.reg("r")
+                k(f"and.b32 {m_}, {v}, -8192;")
+                l_ = k.reg("r")
+                k(f"sub.rn.f32 {l_}, {v}, {m_};")
+                lo.append(l_)
+            k(f"st.shared.v4.b32 [{a}+{lo_off}], {{{', '.join(lo)}}};")
+
+    def load_elem(self, ptr_base, eidx, ok, dst):
+        """dst = element eidx of a global operand if ok, else 0."""
+        k, es = self.k, self.es
+        k(f"mov.b32 {dst}, 0;")
+        a = k.reg("rd")
+        k(f"mul.wide.u32 {a}, {eidx}, {es};")
+        k(f"add.s64 {a}, {a}, {ptr_base};")
+        if es == 4:
+            k(f"@{ok} ld.global.nc.b32 {dst}, [{a}];")
+        else:
+            h = k.reg("h")
+            k(f"mov.b16 {h}, 0;")
+            k(f"@{ok} ld.global.nc.b16 {h}, [{a}];")
+            k(f"cvt.u32.u16 {dst}, {h};")
+
+    def pack16(self, lo16, hi16):
+        k = self.k
+        r_ = k.reg("r")
+        k(f"shl.b32 {r_}, {hi16}, 16;")
+        k(f"or.b32 {r_}, {r_}, {lo16};")
+        return r_
+
+    def fetch(self, form, kb, base, count, bound, ptr, ld, kend, vec=False, into=None):
+        """This thread's chunks of one slab of ``count`` operand rows starting
+        at row ``base`` (rows >= ``bound`` and k >= ``kend`` read as 0), k
+        from ``kb``.  ``form`` "K": the operand is stored [row][k] (row
+        stride ``ld`` elements; ``vec``: a chunk is all in or all out of
+        range and 16-byte aligned, one vector load); "T": it is stored
+        [k][row] (stride ``ld``): CE loads of one column per chunk,
+        coalesced across the threads.  ``into``: the registers of an
+        earlier fetch to reuse (a loop-carried register set)."""
+        k, T, CE = self.k, self.T, self.CE
+        out = []
+        slots = iter(into or [])
+        for c in range(-(-count * 8 // T)):
+            prev = next(slots, None)
+            idx = k.reg("r")
+            k(f"add.u32 {idx}, {self.tid}, {c * T};")
+            live = prev[2] if prev else k.reg("p")
+            k(f"setp.lt.u32 {live}, {idx}, {count * 8};")
+            row = prev[0] if prev else k.reg("r")
+            ch = prev[1] if prev else k.reg("r")
+            if form == "K":
+                k(f"shr.u32 {row}, {idx}, 3;")
+                k(f"and.b32 {ch}, {idx}, 7;")
+            else:
+                k(f"rem.u32 {row}, {idx}, {count};")
+                k(f"div.u32 {ch}, {idx}, {count};")
+            g = k.reg("r")
+            k(f"add.u32 {g}, {base}, {row};")
+            k(f"setp.lt.and.u32 {live}, {g}, {bound}, {live};")
+            kk = k.reg("r")
+            k(f"mad.lo.u32 {kk}, {ch}, {CE}, {kb};")
+            w = prev[3] if prev else k.regs("r", 4)
+            for r_ in w:
+                k(f"mov.b32 {r_}, 0;")
+            if form == "K" and vec:
+                ok = k.reg("p")
+                k(f"setp.lt.and.u32 {ok}, {kk}, {kend}, {live};")
+                ei = k.reg("r")
+                k(f"mad.lo.u32 {ei}, {g}, {ld}, {kk};")
+                a = k.reg("rd")
+                k(f"mul.wide.u32 {a}, {ei}, {self.es};")
+                k(f"add.s64 {a}, {a}, {ptr};")
+                k(f"@{ok} ld.global.nc.v4.b32 {{{', '.join(w)}}}, [{a}];")
+            else:
+                elems = k.regs("r", CE)
+                for e in range(CE):
+                    ke = k.reg("r")
+                    k(f"add.u32 {ke}, {kk}, {e};")
+                    ok = k.reg("p")
+                    k(f"setp.lt.and.u32 {ok}, {ke}, {kend}, {live};")
+                    ei = k.reg("r")
+                    if form == "K":
+                        k(f"mad.lo.u32 {ei}, {g}, {ld}, {ke};")
+                    else:
+                        k(f"mad.lo.u32 {ei}, {ke}, {ld}, {g};")
+                    self.load_elem(ptr, ei, ok, elems[e])
+                words = elems if self.es == 4 else [self.pack16(elems[2 * x], elems[2 * x + 1])
+                                                    for x in range(4)]
+                for r_, x in zip(w, words):
+                    k(f"mov.b32 {r_}, {x};")
+            out.append((row, ch, live, w))
+        return out
+
+    def put(self, chunks, dst, lo_off):
+        """Store fetched chunks at buffer ``dst`` (a register)."""
+        k = self.k
+        for row, ch, live, w in chunks:
+            sk = k.label("NO_CHUNK")
+            k(f"@!{live} bra {sk};")
+            self.store_chunk(dst, self.swz(row, ch), w, lo_off)
+            k.mark(sk)
+
+
 class GemmSmallTemplate:
     name = "gemm"
 
@@ -85,11 +292,8 @@ class GemmSmallTemplate:
         tile = ctx.tile
         if tile is None:
             raise TemplateMismatch("no single top-level Tile")
-        # grouped rasterisation remaps CTAs only with a group of 2 or more
-        # (reference compile.py:2403-2415); auxiliary threads change the decode
-        if (getattr(tile, "raster_group", None) or 0) > 1 and getattr(tile, "raster_axes", None) \
-                or getattr(tile, "aux_threads", 0):
-            raise TemplateMismatch("rasterised or auxiliary-thread tile")
+        if getattr(tile, "aux_threads", 0):
+            raise TemplateMismatch("auxiliary-thread tile")
         axes = ctx.tile_axes()
         names = [a for a, _ in axes]
         if names[-4:] != ["a0_b", "a1_b", "a0_u", "a1_u"] or len(names) not in (4, 5):
@@ -262,6 +466,8 @@ class GemmSmallTemplate:
         self.M, self.N, self.K, self.KC = M, N, K, KC
         self.BM, self.BN, self.T = BM, BN, T
         self.nb0, self.nb1, self.nks = ext["a0_b"], ext["a1_b"], nks
+        self.ks_axis = ks_axis
+        self.block_axes = axes[:-2]
         self.mode, self.atomic = mode, atomic
         self.es = 4 if mode == "tf32x3" else 2
         self.CE = 16 // self.es                 # elements per 16-byte chunk
@@ -320,14 +526,11 @@ class GemmSmallTemplate:
         lane = k.reg("r")
         k(f"and.b32 {lane}, {tid}, 31;")
         cta = k.special("%ctaid.x")
-        nb = k.reg("r")
-        k(f"rem.u32 {nb}, {cta}, {self.nb1};")
-        t_ = k.reg("r")
-        k(f"div.u32 {t_}, {cta}, {self.nb1};")
-        mb = k.reg("r")
-        k(f"rem.u32 {mb}, {t_}, {self.nb0};")
-        ks = k.reg("r")
-        k(f"div.u32 {ks}, {t_}, {self.nb0};")
+        blk = block_indices(k, cta, ctx.tile, self.block_axes)
+        mb, nb = blk["a0_b"], blk["a1_b"]
+        ks = blk.get(self.ks_axis) if self.ks_axis else k.reg("r")
+        if not self.ks_axis:
+            k(f"mov.u32 {ks}, 0;")
         r0 = k.reg("r")
         k(f"mul.lo.u32 {r0}, {mb}, {BM};")
         n0 = k.reg("r")
@@ -377,137 +580,28 @@ class GemmSmallTemplate:
         k(f"setp.eq.u32 {ptrue}, 0, 0;")
         wait = GemmTemplate._wait
 
-        def swz(row, ch):
-            """Byte offset of 16-byte chunk ``ch`` of row ``row`` in the
-            128-byte-swizzle K-major layout (8-row atoms of 1024 bytes)."""
-            o = k.reg("r")
-            k(f"and.b32 {o}, {row}, 7;")
-            x = k.reg("r")
-            k(f"xor.b32 {x}, {ch}, {o};")
-            k(f"shl.b32 {x}, {x}, 4;")
-            k(f"shl.b32 {o}, {o}, 7;")
-            k(f"add.u32 {x}, {x}, {o};")
-            a = k.reg("r")
-            k(f"shr.u32 {a}, {row}, 3;")
-            k(f"mad.lo.u32 {x}, {a}, 1024, {x};")
-            return x
+        st = Stager(k, tid, T, es, tf32)
 
-        def store_chunk(dst, off, vals, lo_off):
-            a = k.reg("r")
-            k(f"add.u32 {a}, {dst}, {off};")
-            k(f"st.shared.v4.b32 [{a}], {{{', '.join(vals)}}};")
-            if tf32:
-                lo = []
-                for v in vals:
-                    m_ = k.reg("r")
-                    k(f"and.b32 {m_}, {v}, -8192;")
-                    l_ = k.reg("r")
-                    k(f"sub.rn.f32 {l_}, {v}, {m_};")
-                    lo.append(l_)
-                k(f"st.shared.v4.b32 [{a}+{lo_off}], {{{', '.join(lo)}}};")
-
-        def load_elem(ptr_base, eidx, ok, dst):
-            """dst = element eidx of a global operand if ok, else 0."""
-            k(f"mov.b32 {dst}, 0;")
-            a = k.reg("rd")
-            k(f"mul.wide.u32 {a}, {eidx}, {es};")
-            k(f"add.s64 {a}, {a}, {ptr_base};")
-            if es == 4:
-                k(f"@{ok} ld.global.nc.b32 {dst}, [{a}];")
-            else:
-                h = k.reg("h")
-                k(f"mov.b16 {h}, 0;")
-                k(f"@{ok} ld.global.nc.b16 {h}, [{a}];")
-                k(f"cvt.u32.u16 {dst}, {h};")
-
-        def pack16(lo16, hi16):
-            r_ = k.reg("r")
-            k(f"shl.b32 {r_}, {hi16}, 16;")
-            k(f"or.b32 {r_}, {r_}, {lo16};")
-            return r_
-
-        nA, nB = -(-BM * 8 // T), -(-BN * 8 // T)     # 16-byte chunks per thread
         vec_a = K % CE == 0 and KC % CE == 0            # a chunk is all in or all out
 
         def fetch(slab, into=None):
-            """This thread's chunks of slab ``slab`` (k from k0 + slab*KB)
-            into registers: A rows as 16-byte loads (element loads at ragged
-            K), B columns as CE coalesced element loads each; zero outside
-            the matrix and past the CTA's K range.  The loads stay in flight
-            until ``put`` stores them.  ``into``: the registers of an earlier
-            fetch to load into (a loop-carried register set)."""
+            """This thread's A and B chunks of slab ``slab`` (k from k0 + slab*KB)."""
             kb = k.reg("r")
             k(f"mad.lo.u32 {kb}, {slab}, {KB}, {k0};")
-            out = []
-            slots = iter(into or [])
-            for which, nch, tot in (("A", nA, BM * 8), ("B", nB, BN * 8)):
-                for c in range(nch):
-                    prev = next(slots, None)
-                    idx = k.reg("r")
-                    k(f"add.u32 {idx}, {tid}, {c * T};")
-                    live = prev[3] if prev else k.reg("p")
-                    k(f"setp.lt.u32 {live}, {idx}, {tot};")
-                    row = prev[1] if prev else k.reg("r")
-                    ch = prev[2] if prev else k.reg("r")
-                    if which == "A":
-                        k(f"shr.u32 {row}, {idx}, 3;")
-                        k(f"and.b32 {ch}, {idx}, 7;")
-                        g = k.reg("r")
-                        k(f"add.u32 {g}, {r0}, {row};")
-                        k(f"setp.lt.and.u32 {live}, {g}, {M}, {live};")
-                    else:
-                        k(f"rem.u32 {row}, {idx}, {BN};")
-                        k(f"div.u32 {ch}, {idx}, {BN};")
-                        g = k.reg("r")
-                        k(f"add.u32 {g}, {n0}, {row};")
-                        k(f"setp.lt.and.u32 {live}, {g}, {N}, {live};")
-                    kk = k.reg("r")
-                    k(f"mad.lo.u32 {kk}, {ch}, {CE}, {kb};")
-                    w = prev[4] if prev else k.regs("r", 4)
-                    for r_ in w:
-                        k(f"mov.b32 {r_}, 0;")
-                    if which == "A" and vec_a:
-                        ok = k.reg("p")
-                        k(f"setp.lt.and.u32 {ok}, {kk}, {kend}, {live};")
-                        ei = k.reg("r")
-                        k(f"mad.lo.u32 {ei}, {g}, {K}, {kk};")
-                        a = k.reg("rd")
-                        k(f"mul.wide.u32 {a}, {ei}, {es};")
-                        k(f"add.s64 {a}, {a}, {abase};")
-                        k(f"@{ok} ld.global.nc.v4.b32 {{{', '.join(w)}}}, [{a}];")
-                    else:
-                        elems = k.regs("r", CE)
-                        for e in range(CE):
-                            ke = k.reg("r")
-                            k(f"add.u32 {ke}, {kk}, {e};")
-                            ok = k.reg("p")
-                            k(f"setp.lt.and.u32 {ok}, {ke}, {kend}, {live};")
-                            ei = k.reg("r")
-                            if which == "A":
-                                k(f"mad.lo.u32 {ei}, {g}, {K}, {ke};")
-                            else:
-                                k(f"mad.lo.u32 {ei}, {ke}, {N}, {g};")
-                            load_elem(abase if which == "A" else bbase, ei, ok, elems[e])
-                        words = elems if es == 4 else [pack16(elems[2 * x], elems[2 * x + 1])
-                                                       for x in range(4)]
-                        for r_, x in zip(w, words):
-                            k(f"mov.b32 {r_}, {x};")
-                    out.append((which, row, ch, live, w))
-            return out
+            na = -(-BM * 8 // T)
+            a = st.fetch("K", kb, r0, BM, M, abase, K, kend, vec_a, into and into[:na])
+            b = st.fetch("T", kb, n0, BN, N, bbase, N, kend, False, into and into[na:])
+            return a + b, na
 
-        def put(chunks, buf):
-            """Store fetched chunks into slab buffer ``buf`` (swizzled; with
-            their low tf32 parts for fp32 operands)."""
+        def put(fetched, buf):
+            """Store a fetch into slab buffer ``buf``: A | A_lo | B | B_lo."""
+            chunks, na = fetched
             base = k.reg("r")
             k(f"mad.lo.u32 {base}, {buf}, {self.buf}, {sm};")
-            for which, row, ch, live, w in chunks:
-                sk = k.label("NO_CHUNK")
-                k(f"@!{live} bra {sk};")
-                off = swz(row, ch)
-                if which == "B":
-                    k(f"add.u32 {off}, {off}, {self.sa * (2 if tf32 else 1)};")
-                store_chunk(base, off, w, self.sa if which == "A" else self.sb)
-                k.mark(sk)
+            st.put(chunks[:na], base, self.sa)
+            bb = k.reg("r")
+            k(f"add.u32 {bb}, {base}, {self.sa * (2 if tf32 else 1)};")
+            st.put(chunks[na:], bb, self.sb)
             k("fence.proxy.async.shared::cta;")
 
         def mma(slab, buf, nsteps):
@@ -583,7 +677,7 @@ class GemmSmallTemplate:
         k(f"setp.lt.u32 {pn}, {nxt}, {nslab};")
         skf = k.label("NO_FETCH")
         k(f"@!{pn} bra {skf};")
-        fetch(nxt, chunks)                    # in flight while the MMAs run
+        fetch(nxt, chunks[0])                 # in flight while the MMAs run
         k.mark(skf)
         mma(s, bufr, KB // KMMA)
         k(f"mov.u32 {s}, {nxt};")

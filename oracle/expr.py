@@ -107,6 +107,43 @@ def attention(q, k, v, scale, k_transposed=False):
 
 
 # --------------------------------------------------------------------------
+# IR nodes the vocabulary defines and no reference IR uses, restated from
+# their descriptions in the reference's TASK.md (Pre / Carry, Select,
+# ZeroPrologue); the IRs are synth.carried_prefix / select_branches /
+# zero_prologue
+# --------------------------------------------------------------------------
+
+def carried_prefix(x, every):
+    """A carried cell stepped along each row: step j reads the previous state
+    (0 before the first step), and steps with j % every == 0 set it to that
+    state + x[j]; the output of step j is the state the step read."""
+    x = _d(x)
+    y = np.zeros_like(x)
+    state = np.zeros(x.shape[0])
+    for j in range(x.shape[1]):
+        y[:, j] = state
+        if j % every == 0:
+            state = state + x[:, j]
+    return y.astype(f32)
+
+
+def select_split(x, split):
+    """The value of the branch whose coordinate predicate holds: x[i] for
+    i < split, x[i] * x[i] (float32) otherwise."""
+    x = np.asarray(x, f32)
+    i = np.arange(x.shape[0])
+    return np.where(i < split, x, np.multiply(x, x, dtype=f32)).astype(f32)
+
+
+def zero_prologue(x, words):
+    """The first ``words`` words zeroed, then x added into the first n."""
+    x = np.asarray(x, f32)
+    out = np.zeros(max(words, x.shape[0]), f32)
+    out[:x.shape[0]] += x
+    return out
+
+
+# --------------------------------------------------------------------------
 # the reference's open problems (problems/*/meta.json "code")
 # --------------------------------------------------------------------------
 
@@ -172,6 +209,12 @@ def evaluate_family(spec: dict, inputs: dict) -> dict:
         r = matmul(v[a["a"]], v[a["b"]])
     elif fam == "attention":
         r = attention(v[a["q"]], v[a["k"]], v[a["v"]], spec["scale"])
+    elif fam == "carried_prefix":
+        r = carried_prefix(v[a["x"]], spec["every"])
+    elif fam == "select":
+        r = select_split(v[a["x"]], spec["split"])
+    elif fam == "zero_prologue":
+        r = zero_prologue(v[a["x"]], spec["words"])
     else:
         raise KeyError(fam)
     return {out: r}

@@ -370,3 +370,33 @@ def test_meta_only_gemm_takes_only_meta_parameters(monkeypatch):
         assert [n for _, n in params] == m["kernels"][0]["arg_order"]
     g, m = synth.attention(B=1, H=1, S=256, D=64).build()
     assert compile_graph(g, m).kind == "generic"
+    for name in ("a01_attention", "a02_attention_128"):
+        f = GOLDEN / "problems" / name
+        g, m = json.loads((f / "kernel.ir.json").read_text()), json.loads((f / "meta.json").read_text())
+        c = compile_graph(g, m)
+        assert type(c.template).__name__ == "AttentionSmallTemplate", c.rejections
+        params = re.findall(r"\.param \.(\w+) param_(\w+)", c.render())
+        assert [n for _, n in params] == m["kernels"][0]["arg_order"]
+
+
+def test_vocabulary_nodes_lower(native_lib):
+    """Pre/Carry, Select and ZeroPrologue (defined by the IR vocabulary,
+    lowered by no reference code) go through the statement-by-statement
+    lowering, assemble for sm_100a and pass the static checks; a Pre of a
+    cell no Carry sets, or a cell indexed at run time, is refused."""
+    from emmy_b200 import native, ptxcheck, synth
+    from emmy_b200 import ir as I
+    for p in (synth.carried_prefix(), synth.carried_prefix(cols=200, every=3),
+              synth.select_branches(), synth.zero_prologue()):
+        g, m = p.build()
+        c = compile_graph(g, m)
+        assert c.kind == "generic"
+        ptx = c.render()
+        native.Image(ptx)
+        assert not ptxcheck.check(ptx)
+    p = synth.carried_prefix()
+    p.body = synth.tile([synth.axis("a0", 64)], [I.Pre("v", "nothing", ()),
+                                               synth.write("y", (synth.V("a0"), synth.Lit(0)),
+                                                           ("v",))])
+    with pytest.raises(NotImplementedError):
+        compile_graph(*p.build()).render()

@@ -1,5 +1,7 @@
-"""The tcgen05 GEMM with a meta-only launch (``templates/gemm_small.py``) on
-the GPU: Emmy's own matmul IRs (the m01/m02 open problems, the corpus mm*
+"""The tcgen05 kernels with a meta-only launch (``templates/gemm_small.py``,
+``templates/attention_small.py``) on the GPU: Emmy's own matmul and attention
+IRs (the a01/a02 open problems and the corpus attn* IRs, fp32 with K
+pre-transposed, one-row to 32-row CTA blocks, grouped rasterisation) and matmul IRs (the m01/m02 open problems, the corpus mm*
 IRs: odd CTA tiles, edge guards, split K with atomic stores) against their
 golden outputs; the same kernels launched by a bare CUDA-driver launcher that
 passes exactly the meta ``arg_order`` (``cuModuleLoadData`` on the PTX text,
@@ -22,6 +24,8 @@ pytestmark = pytest.mark.gpu
 
 EMMY_MATMULS = [GOLDEN / "problems" / "m01_matmul_512", GOLDEN / "problems" / "m02_matmul_rect"] + \
     [GOLDEN / "corpus" / n for n in ("mm128", "mm256", "mm512", "mm64a", "mm_rect2")]
+EMMY_ATTENTION = [GOLDEN / "problems" / "a01_attention", GOLDEN / "problems" / "a02_attention_128"] + \
+    [GOLDEN / "corpus" / n for n in ("attn128b", "attn64b", "attn96")]
 
 
 def _status(kern):
@@ -46,6 +50,19 @@ def test_emmy_matmul_irs_on_tensor_cores(folder):
     _check_expected(folder, meta, outs)
 
 
+@pytest.mark.parametrize("folder", EMMY_ATTENTION, ids=lambda p: p.name)
+def test_emmy_attention_irs_on_tensor_cores(folder):
+    from emmy_b200 import harness
+    g = json.loads((folder / "kernel.ir.json").read_text())
+    meta = json.loads((folder / "meta.json").read_text())
+    outs, kern = harness.run(g, meta, folder=folder)
+    assert kern.kind == "attention" and \
+        type(kern.compiler.template).__name__ == "AttentionSmallTemplate"
+    assert not kern.tmaps
+    assert _status(kern) == 0
+    _check_expected(folder, meta, outs)
+
+
 def _check_expected(folder, meta, outs):
     """Golden outputs: an open problem's expected.npz is keyed by output name;
     a corpus case's holds ``val`` (and ``idx`` when sampled)."""
@@ -63,7 +80,7 @@ def _check_expected(folder, meta, outs):
         float(np.max(np.abs(got - ref)))
 
 
-@pytest.mark.parametrize("folder", EMMY_MATMULS[:3], ids=lambda p: p.name)
+@pytest.mark.parametrize("folder", EMMY_MATMULS[:3] + EMMY_ATTENTION[:2], ids=lambda p: p.name)
 def test_bare_driver_launch_with_meta_arguments(folder):
     """Load the PTX text with the CUDA driver and launch it with exactly the
     meta arguments: no tensor maps, no library of this build in the launch."""
