@@ -87,9 +87,12 @@ class AttentionTemplate:
     # 256-row query blocks of one (batch, head)): the leader's one thread
     # issues tcgen05.mma.cta_group::2 (M = 256: each CTA's 128 rows of a tile
     # in its own TMEM), each CTA loads half of every K block (64 keys) and
-    # half of every V block (D/2 columns), so per SM the MMA issue -- the
-    # measured limiter -- and the K/V shared-memory traffic halve
-    PAIR = {64: False, 128: True}
+    # half of every V block (D/2 columns), so per SM the MMA issue and the
+    # K/V shared-memory traffic halve.  Correct, and slower at D = 128 (933
+    # against 1178 TFLOP/s): a trace shows each tile's MMA chain shorter
+    # but the two tiles' softmax passes in phase, contending for the MUFU
+    # (3,200 cycles a pass instead of 1,750), a 4,570-cycle block period
+    PAIR = {64: False, 128: False}
 
     # ------------------------------------------------------------------ match
     @classmethod

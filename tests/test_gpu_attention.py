@@ -97,12 +97,15 @@ def test_attention_split_p(kw, ramp, split, monkeypatch):
 @pytest.mark.parametrize("kw", [dict(B=1, H=2, S=512, D=128), dict(B=2, H=1, S=1024, D=128)],
                          ids=["d128_s512", "d128_s1024"])
 @pytest.mark.parametrize("ramp", [False, True], ids=["plain", "growing"])
-def test_attention_cta_pairs(kw, ramp):
+def test_attention_cta_pairs(kw, ramp, monkeypatch):
     """d=128 on CTA pairs (cta_group::2: the leader issues M=256 MMAs for both
     CTAs' tiles; each CTA holds half of every K and V block; P_READY counts
-    both CTAs' softmax warps, the follower's arriving remotely): the same
-    oracle bounds, also when the exponent base moves inside blocks."""
+    both CTAs' softmax warps, the follower's arriving remotely; off by
+    default, measured slower): the same oracle bounds, also when the
+    exponent base moves inside blocks."""
     from emmy_b200.compiler import compile_graph
+    from emmy_b200.templates import attention
+    monkeypatch.setattr(attention.AttentionTemplate, "PAIR", {64: False, 128: True})
     p = synth.attention(**kw)
     g, m = p.build()
     assert compile_graph(g, m).template.pair
