@@ -40,6 +40,57 @@ WORKERS = 74                 # clusters of 2 CTAs: the 148 SMs of a B200
 PERSISTENT_MIN_STAGES = 4    # 4 x 32 KiB ring: one CTA per SM
 EPI_CHUNK = 16               # accumulator columns per tcgen05.ld in the epilogue
 GROUP_M = 16                 # 256-row bands per raster group (tiles run down a group's bands)
+TAIL_SPLIT = True            # leftover pair tiles of a partial last round run as 256 x 128 halves
+
+
+def schedule(tiles: int, workers: int = WORKERS):
+    """(W, NF, R, half): ``W`` worker clusters; every cluster runs ``NF``
+    full rounds of 256 x 256 pair tiles (cluster c: tiles c, c + W, ...);
+    ``R`` tiles are left over.  With ``half``, the leftover tiles are cut
+    into 256 x 128 halves and clusters 0 .. 2R-1 take one half each, so the
+    last round costs about half a round instead of a whole one (256 tiles
+    on 74 clusters: 3.5 rounds, not 4).  Without it (2R above W, where the
+    halves would need two half rounds anyway) clusters 0 .. R-1 take one
+    more whole tile."""
+    W = min(workers, tiles)
+    NF, R = divmod(tiles, W)
+    return W, NF, R, bool(TAIL_SPLIT and R and 2 * R <= W)
+
+
+def cluster_tiles(c: int, tiles: int, workers: int = WORKERS):
+    """The work list of cluster ``c`` under ``schedule``: (pair tile index
+    in raster order, column offset 0 or 128, width 256 or 128) per
+    iteration -- the order the kernel's producer, MMA and epilogue roles
+    walk."""
+    W, NF, R, half = schedule(tiles, workers)
+    out = [(c + W * i, 0, 256) for i in range(NF)]
+    if half:
+        if c < 2 * R:
+            out.append((NF * W + c // 2, 128 * (c % 2), 128))
+    elif c < R:
+        out.append((c + W * NF, 0, 256))
+    return out
+
+
+def tile_index(k, idx, clus, W, NF, half):
+    """Emitted form of ``cluster_tiles``: iteration ``idx`` of cluster
+    ``clus`` -> (pair tile register in raster order, half-tile predicate or
+    None, column offset register or None: 128 on the second half)."""
+    tt = k.reg("r")
+    k(f"mad.lo.u32 {tt}, {idx}, {W}, {clus};")
+    if not half:
+        return tt, None, None
+    ph_ = k.reg("p")
+    k(f"setp.ge.u32 {ph_}, {idx}, {NF};")
+    tail = k.reg("r")                             # tile NF*W + clus/2, half clus%2
+    k(f"shr.u32 {tail}, {clus}, 1;")
+    k(f"add.u32 {tail}, {tail}, {NF * W};")
+    k(f"selp.u32 {tt}, {tail}, {tt}, {ph_};")
+    hoff = k.reg("r")
+    k(f"and.b32 {hoff}, {clus}, 1;")
+    k(f"shl.b32 {hoff}, {hoff}, 7;")
+    k(f"selp.u32 {hoff}, {hoff}, 0, {ph_};")
+    return tt, ph_, hoff
 
 
 def raster(k, tt, MB, NB, group=None):
@@ -92,7 +143,7 @@ def emit_pair_persistent(t) -> str:
     NB = t.NB                        # 256-column tiles per row band
     MB = t.M // 256                  # 256-row bands
     TILES = MB * NB                  # pair tiles
-    W = min(WORKERS, TILES)
+    W, NF, R, HALF = schedule(TILES)
     params = ctx.params() + [("tmapA", ".align 64 .b8", "[128]"),
                              ("tmapB", ".align 64 .b8", "[128]")]
     k = Kernel(ctx.entry, params)
@@ -132,10 +183,12 @@ def emit_pair_persistent(t) -> str:
     rank = k.special("%cluster_ctarank")
     plead = k.reg("p")
     k(f"setp.eq.u32 {plead}, {rank}, 0;")
-    # this cluster's tile count: ceil((TILES - clus) / W)
+    # this cluster's tile count: NF full rounds, then one leftover tile (or
+    # one half of one) for the first clusters
     ntile = k.reg("r")
-    k(f"sub.u32 {ntile}, {TILES + W - 1}, {clus};")
-    k(f"div.u32 {ntile}, {ntile}, {W};")
+    ptl = k.reg("p")
+    k(f"setp.lt.u32 {ptl}, {clus}, {2 * R if HALF else R};")
+    k(f"selp.u32 {ntile}, {NF + 1}, {NF}, {ptl};")
     # shared memory: S stages, then the mbarriers full[S], empty[S],
     # conv[S] (3xTF32, used in the leader), acc[2], acc_empty[2] (leader),
     # and the tensor-memory slot
@@ -201,11 +254,19 @@ def emit_pair_persistent(t) -> str:
         k(f"mad.lo.u32 {r}, {stage_reg}, {STG}, {ring};")
         return r
 
+    def half_pred(idx):
+        """True on this cluster's 256 x 128 leftover half tile (None when the
+        schedule has none)."""
+        if not HALF:
+            return None
+        ph_ = k.reg("p")
+        k(f"setp.ge.u32 {ph_}, {idx}, {NF};")
+        return ph_
+
     def tile_coords(idx):
-        """(m0 of this CTA, n0 of the pair tile, this CTA's B columns) for
-        this cluster's tile iteration ``idx``."""
-        tt = k.reg("r")
-        k(f"mad.lo.u32 {tt}, {idx}, {W}, {clus};")
+        """(m0 of this CTA, n0 of the pair tile, this CTA's B columns, the
+        half-tile predicate) for this cluster's tile iteration ``idx``."""
+        tt, ph_, hoff = tile_index(k, idx, clus, W, NF, HALF)
         mp, nbk = raster(k, tt, MB, NB)
         m0 = k.reg("r")
         k(f"mad.lo.u32 {m0}, {mp}, 2, {rank};")
@@ -213,8 +274,14 @@ def emit_pair_persistent(t) -> str:
         n0 = k.reg("r")
         k(f"mul.lo.u32 {n0}, {nbk}, {BN};")
         nh = k.reg("r")
-        k(f"mad.lo.u32 {nh}, {rank}, 128, {n0};")
-        return m0, n0, nh
+        if HALF:
+            k(f"add.u32 {n0}, {n0}, {hoff};")
+            wcol = k.reg("r")                     # each CTA holds half of the tile's B
+            k(f"selp.u32 {wcol}, 64, 128, {ph_};")
+            k(f"mad.lo.u32 {nh}, {rank}, {wcol}, {n0};")
+        else:
+            k(f"mad.lo.u32 {nh}, {rank}, 128, {n0};")
+        return m0, n0, nh, ph_
 
     def tile_loop_head(label):
         k(f"mov.u32 {it}, 0;")
@@ -250,7 +317,14 @@ def emit_pair_persistent(t) -> str:
     k(f"mov.u32 {st}, 0;")
     k(f"mov.u32 {ph}, 0;")
     ptop = tile_loop_head("PTILE")
-    m0, n0, nh = tile_coords(it)
+    m0, n0, nh, phalf = tile_coords(it)
+    tx = k.reg("r")                               # bytes this CTA's copies deliver
+    if HALF:
+        k(f"selp.u32 {tx}, {SA + SBH // 2}, {RAW}, {phalf};")
+    else:
+        k(f"mov.u32 {tx}, {RAW};")
+    if not tf32:
+        k(f"shl.b32 {tx}, {tx}, 1;")              # the leader arms for both CTAs
     k(f"mov.u32 {kt}, 0;")
     pk = k.label("PK")
     k.mark(pk)
@@ -260,12 +334,12 @@ def emit_pair_persistent(t) -> str:
     own_fb = bar_addr(0, st)
     if tf32:
         fb = own_fb
-        k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{own_fb}], {RAW};")
+        k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{own_fb}], {tx};")
         copy = ("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes")
     else:
         fb = k.reg("r")
         k(f"mad.lo.u32 {fb}, {st}, 8, {lead_full};")
-        k(f"@{plead} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{own_fb}], {2 * RAW};")
+        k(f"@{plead} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{own_fb}], {tx};")
         copy = ("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::"
                 "complete_tx::bytes")
     kc = k.reg("r")
@@ -277,7 +351,8 @@ def emit_pair_persistent(t) -> str:
         k(f"add.u32 {nx}, {nh}, {BOXN * i};")
         db = k.reg("r")
         k(f"add.u32 {db}, {da}, {SA + i * BK * 128};")
-        k(f"{copy} [{db}], [{tb}, {{{nx}, {kc}}}], [{fb}];")
+        guard = f"@!{phalf} " if HALF and i >= 64 // BOXN else ""
+        k(f"{guard}{copy} [{db}], [{tb}, {{{nx}, {kc}}}], [{fb}];")
     k_loop_tail(pk)
     tile_loop_tail(ptop)
     k.mark(end_prod)
@@ -291,13 +366,19 @@ def emit_pair_persistent(t) -> str:
     k(f"@!{pmma} bra {end_mma};")
     mask = k.reg("h")
     k(f"mov.b16 {mask}, 3;")
-    idesc = k.reg("r")
-    k(f"mov.u32 {idesc}, {idesc_mma(2 * BM, BN, True, tf32)};")
+    idesc_full = idesc_mma(2 * BM, BN, True, tf32)
+    idesc_half = idesc_mma(2 * BM, BN // 2, True, tf32)
     hiA = _desc_hi(16, 1024)
     hiB = _desc_hi(BK * 128, 512, 1) if tf32 else _desc_hi(BK * 128, 1024)
     k(f"mov.u32 {st}, 0;")
     k(f"mov.u32 {ph}, 0;")
     mtop = tile_loop_head("MTILE")
+    idesc = k.reg("r")
+    mhalf = half_pred(it)
+    if HALF:                                      # N = 128: 64 B columns from each CTA
+        k(f"selp.u32 {idesc}, {idesc_half}, {idesc_full}, {mhalf};")
+    else:
+        k(f"mov.u32 {idesc}, {idesc_full};")
     buf = k.reg("r")
     k(f"and.b32 {buf}, {it}, 1;")
     aph = k.reg("r")                              # use count of this buffer, parity
@@ -384,7 +465,7 @@ def emit_pair_persistent(t) -> str:
         k(f"mad.lo.u32 {eaf}, {ebuf}, 8, {accb};")
         GemmTemplate._wait(k, eaf, eph, status, 3, teardown)
         k("tcgen05.fence::after_thread_sync;")
-        m0e, n0e, _ = tile_coords(idx)
+        m0e, n0e, _, ehalf = tile_coords(idx)
         row = k.reg("r")
         k(f"mad.lo.u32 {row}, {q}, 32, {lane};")
         k(f"add.u32 {row}, {row}, {m0e};")
@@ -398,7 +479,10 @@ def emit_pair_persistent(t) -> str:
         taddr = k.reg("r")
         k(f"mad.lo.u32 {taddr}, {ebuf}, {BN}, {tl};")
         CH = EPI_CHUNK
+        skip_half = k.label("EPI_HALF") if HALF else None
         for c in range(BN // CH):
+            if HALF and c == BN // 2 // CH:        # a half tile ends at column 128
+                k(f"@{ehalf} bra {skip_half};")
             regs = k.regs("r", CH)
             ta2 = k.reg("r")
             k(f"add.u32 {ta2}, {taddr}, {CH * c};")
@@ -407,6 +491,8 @@ def emit_pair_persistent(t) -> str:
             for v in range(CH // 8):
                 k(f"st.global.v8.b32 [{cptr}+{4 * CH * c + 32 * v}], "
                   f"{{{', '.join(regs[8 * v:8 * v + 8])}}};")
+        if HALF:
+            k.mark(skip_half)
         # this warp's reads of the buffer are complete: release it to the MMA
         k("tcgen05.fence::before_thread_sync;")
         k("bar.warp.sync 0xffffffff;")

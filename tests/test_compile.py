@@ -262,43 +262,71 @@ def test_rows_online_softmax_recognised():
     assert c.kind == "rows" and c.template.online is None
 
 
-@pytest.mark.parametrize("MB,NB", [(1, 1), (2, 3), (16, 32), (17, 5), (40, 7), (64, 32), (3, 100)])
+def _interpret(prog, env):
+    """Run straight-line integer PTX (the ops ``tile_index`` and ``raster``
+    emit, predicates included) over the register values in ``env``."""
+    ops = {"div": lambda a, b: a // b, "rem": lambda a, b: a % b,
+           "mul": lambda a, b: a * b, "sub": lambda a, b: a - b,
+           "add": lambda a, b: a + b, "min": min, "shr": lambda a, b: a >> b,
+           "shl": lambda a, b: a << b, "and": lambda a, b: a & b,
+           "mad": lambda a, b, c: a * b + c}
+    for ins in prog:
+        guard = None
+        if ins.startswith("@"):
+            guard, ins = ins.split(" ", 1)
+        op, args = ins.split(" ", 1)
+        d, *src = [a.strip() for a in args.split(",")]
+        v = [env[x] if x in env else int(x) for x in src]
+        if guard and not env[guard.lstrip("@!")] ^ guard.startswith("@!"):
+            continue
+        base, *mods = op.split(".")
+        if base == "setp":
+            env[d] = {"ge": v[0] >= v[1], "lt": v[0] < v[1]}[mods[0]]
+        elif base == "selp":
+            env[d] = v[0] if v[2] else v[1]
+        else:
+            env[d] = ops[base](*v)
+    return env
+
+
+@pytest.mark.parametrize("MB,NB", [(1, 1), (2, 3), (16, 32), (17, 5), (40, 7), (64, 32), (3, 100),
+                                   (8, 32), (4, 20)])
 @pytest.mark.parametrize("group", [1, 8, 16])
 def test_gemm_raster_is_a_bijection(MB, NB, group):
-    """The grouped tile order of the CTA-pair GEMMs (``gemm_persistent.raster``,
-    run here by interpreting its emitted integer PTX), together with the
-    persistent schedule (cluster c takes tiles c, c+W, ...), covers every
-    (row band, column block) pair exactly once -- including a last group
-    with fewer bands than the others."""
+    """The persistent CTA-pair GEMM's tile order (``gemm_persistent.tile_index``
+    then ``raster``, run here by interpreting their emitted integer PTX) walks
+    each cluster through the work list of ``cluster_tiles``: full rounds of
+    tiles c, c+W, ..., then a leftover tile or a 256 x 128 half of one.  Over
+    all clusters every column of every (row band, column block) is computed
+    exactly once -- including a last raster group with fewer bands and the
+    split tails (8 x 32 = 256 tiles, the matmul shard of one GPU in eight:
+    34 leftover tiles become 68 halves)."""
     from emmy_b200.ptx import Kernel
-    from emmy_b200.templates.gemm_persistent import WORKERS, raster
+    from emmy_b200.templates.gemm_persistent import (WORKERS, cluster_tiles, raster, schedule,
+                                                     tile_index)
+    tiles = MB * NB
+    W, NF, R, half = schedule(tiles)
+    assert half == ((MB, NB) in {(17, 5), (3, 100), (8, 32), (4, 20)})
     k = Kernel("t", [])
-    tt = k.reg("r")
+    idx, clus = k.reg("r"), k.reg("r")
+    tt, ph_, hoff = tile_index(k, idx, clus, W, NF, half)
     mp, nbk = raster(k, tt, MB, NB, group)
     prog = [ln.strip().rstrip(";") for ln in k.lines]
-
-    def run(t):
-        env = {tt: t}
-        for ins in prog:
-            op, args = ins.split(" ", 1)
-            d, *src = [a.strip() for a in args.split(",")]
-            v = [env[x] if x in env else int(x) for x in src]
-            base = op.split(".")[0]
-            env[d] = {"div": lambda a, b: a // b, "rem": lambda a, b: a % b,
-                      "mul": lambda a, b: a * b, "sub": lambda a, b: a - b,
-                      "add": lambda a, b: a + b, "min": min}[base](*v)
-        return env[mp], env[nbk]
-
-    tiles = MB * NB
-    W = min(WORKERS, tiles)
-    seen = set()
+    cover = {}
     for c in range(W):
-        ntile = (tiles + W - 1 - c) // W
-        for i in range(ntile):
-            band, blk = run(c + W * i)
+        work = cluster_tiles(c, tiles)
+        assert len(work) in (NF, NF + 1)
+        for i, (t, off, width) in enumerate(work):
+            env = _interpret(prog, {idx: i, clus: c})
+            assert env[tt] == t
+            assert (env[hoff] if half else 0) == off
+            if half:
+                assert env[ph_] == (width == 128)
+            band, blk = env[mp], env[nbk]
             assert 0 <= band < MB and 0 <= blk < NB
-            seen.add((band, blk))
-    assert len(seen) == tiles
+            for col in range(off, off + width, 64):
+                cover[(band, blk, col)] = cover.get((band, blk, col), 0) + 1
+    assert len(cover) == tiles * 4 and set(cover.values()) == {1}
 
 
 def test_pointwise_batch_follows_the_launch():

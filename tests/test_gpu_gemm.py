@@ -106,7 +106,8 @@ def test_gemm_pair_and_single(kw, pair, monkeypatch):
 
 PERSISTENT_CASES = [dict(M=256, N=256, K=64), dict(M=1024, N=768, K=512),
                     dict(M=512, N=512, K=1024), dict(M=4096, N=2048, K=512),
-                    dict(M=8192, N=4096, K=256)]
+                    dict(M=8192, N=4096, K=256), dict(M=2048, N=8192, K=256),
+                    dict(M=1024, N=5120, K=256)]
 
 
 @pytest.mark.parametrize("kw", PERSISTENT_CASES,
@@ -116,7 +117,9 @@ def test_gemm_persistent_pairs(kw):
     pair kernel: 74 worker clusters, two tensor-memory accumulators, the
     epilogue of tile i overlapping the main loop of tile i+1.  The large
     shapes give each worker up to 7 tiles (both accumulators reused several
-    times) and are checked on sampled rows."""
+    times) and are checked on sampled rows; 2048 x 8192 (256 tiles: 3 full
+    rounds, 34 leftover tiles as 68 halves of 256 x 128) and 1024 x 5120
+    (80 tiles: 6 leftover as 12 halves) run the split tail."""
     from emmy_b200 import compiler
     p = synth.matmul(stages=4, **kw)
     g, m = p.build()
@@ -129,7 +132,8 @@ def test_gemm_persistent_pairs(kw):
 
 
 F32_PERSISTENT_CASES = [dict(M=256, N=256, K=128), dict(M=1024, N=768, K=256),
-                        dict(M=4096, N=2048, K=256), dict(M=8192, N=4096, K=128)]
+                        dict(M=4096, N=2048, K=256), dict(M=8192, N=4096, K=128),
+                        dict(M=2048, N=8192, K=128), dict(M=1024, N=5120, K=128)]
 
 
 @pytest.mark.parametrize("kw", F32_PERSISTENT_CASES,
@@ -140,7 +144,7 @@ def test_gemm_f32_persistent_pairs(kw):
     conversion barrier; the leader issues lo*hi, hi*lo, hi*hi as
     ``kind::tf32`` pair MMAs; the same warps drain the previous tile's
     accumulator.  Rel 2e-5 of max|C| (BASELINE asks 1e-4); large shapes on
-    sampled rows."""
+    sampled rows; the last two shapes run the split 256 x 128 tail."""
     from emmy_b200 import compiler
     p = synth.config("matmul_f32", **kw)
     g, m = p.build()
