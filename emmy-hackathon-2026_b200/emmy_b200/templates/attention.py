@@ -43,7 +43,7 @@ import struct
 from ..analysis import NotAffine, affine, kind, walk
 from ..ptx import Kernel
 from .common import TemplateMismatch
-from .gemm import GemmTemplate, _desc_hi, idesc_mma
+from .gemm import WAIT_NS, GemmTemplate, _desc_hi, idesc_mma
 
 LOG2E = 1.4426950408889634
 SMEM_MAX = 227 * 1024
@@ -52,10 +52,72 @@ SMEM_MAX = 227 * 1024
 EXP2_POLY = (0.9999280571937561, 0.6932608485221863, 0.24261115491390228, 0.05517221987247467)
 
 # warp roles (512 threads): softmax warps 0..4*NT-1, then these
-MMA_WARP, PROD_K_WARP, PROD_V_WARP = 8, 9, 10
+MMA_WARP, PROD_K_WARP, PROD_V_WARP, PROD_Q_WARP = 8, 9, 10, 11
+WORKERS = 148                # persistent CTAs: one per SM of a B200
 # registers per thread: at launch, and after setmaxnreg for the softmax
 # warpgroups and for the rest (2 x 128 x 200 + 2 x 128 x 56 = 512 x 128)
 LAUNCH_REGS, SOFT_REGS, ROLE_REGS = 128, 200, 56
+
+
+def unit_schedule(units: int, workers: int, split_tail: bool):
+    """(W, NF, R, half) of a persistent launch over ``units`` (batch, head,
+    256-row query block) units: ``W`` worker CTAs, each runs ``NF`` full
+    rounds (CTA c: units c, c + W, ...); ``R`` units are left over.  With
+    ``half`` (2R <= W) each leftover unit is split by keys: CTAs 2i and
+    2i+1 both compute all 256 rows of leftover unit i, over the first and
+    the second half of the key blocks, and the later of the two to finish
+    merges the partial results, so the last round costs about half a round;
+    otherwise CTAs 0 .. R-1 take one more whole unit."""
+    W = min(workers, units)
+    NF, R = divmod(units, W)
+    return W, NF, R, bool(split_tail and R and 2 * R <= W)
+
+
+def cta_units(c: int, units: int, workers: int, split_tail: bool):
+    """The work list of CTA ``c``: (unit, key half: None for all keys, else 0
+    or 1) per iteration -- the order every role walks."""
+    W, NF, R, half = unit_schedule(units, workers, split_tail)
+    out = [(c + W * i, None) for i in range(NF)] if c < W else []
+    if c < W and half and c < 2 * R:
+        out.append((NF * W + c // 2, c % 2))
+    elif c < W and not half and c < R:
+        out.append((NF * W + c, None))
+    return out
+
+
+def unit_rows(k, u, cta, sched, QB, S, NT, want_q=True):
+    """Emitted form of ``cta_units``: unit iteration ``u`` of CTA ``cta`` ->
+    registers (first query row, first key row) of its unit in the flattened
+    [B*H*S] row space, and the split-unit predicate (None without a split
+    tail; the key row then already starts at the CTA's half of the keys)."""
+    W, NF, _, half = sched
+    uu = k.reg("r")
+    k(f"mad.lo.u32 {uu}, {u}, {W}, {cta};")
+    ph_ = None
+    if half:                       # unit NF*W + cta/2, rows 128*(cta%2) of it
+        ph_ = k.reg("p")
+        k(f"setp.ge.u32 {ph_}, {u}, {NF};")
+        tl = k.reg("r")
+        k(f"shr.u32 {tl}, {cta}, 1;")
+        k(f"add.u32 {tl}, {tl}, {NF * W};")
+        k(f"selp.u32 {uu}, {tl}, {uu}, {ph_};")
+    bh = k.reg("r")
+    k(f"div.u32 {bh}, {uu}, {QB};")
+    krow0 = k.reg("r")
+    k(f"mul.lo.u32 {krow0}, {bh}, {S};")
+    qrow0 = None
+    if want_q:
+        qb = k.reg("r")
+        k(f"rem.u32 {qb}, {uu}, {QB};")
+        qrow0 = k.reg("r")
+        k(f"mad.lo.u32 {qrow0}, {qb}, {128 * NT}, {krow0};")
+    if half:                       # this CTA's half of the keys
+        hs = k.reg("r")
+        k(f"and.b32 {hs}, {cta}, 1;")
+        k(f"mul.lo.u32 {hs}, {hs}, {S // 2};")
+        k(f"selp.u32 {hs}, {hs}, 0, {ph_};")
+        k(f"add.u32 {krow0}, {krow0}, {hs};")
+    return qrow0, krow0, ph_
 
 
 class AttentionTemplate:
@@ -93,6 +155,12 @@ class AttentionTemplate:
     # but the two tiles' softmax passes in phase, contending for the MUFU
     # (3,200 cycles a pass instead of 1,750), a 4,570-cycle block period
     PAIR = {64: False, 128: False}
+    # two-tile CTAs run persistent: the first WORKERS CTAs loop over the
+    # (batch, head, 256-row) units and every other CTA returns at once; with
+    # TAIL_SPLIT the units of a partial last round are split by keys over
+    # two CTAs each
+    PERSIST = True
+    TAIL_SPLIT = True
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -173,8 +241,9 @@ class AttentionTemplate:
         if BM not in (128, 256) or ext["a0_b"] * BM != S or ext["a5_b"] != 1 or \
                 D not in (64, 128) or S % 128 or ext["ab"] != B or ext["ah"] != H:
             raise TemplateMismatch("tile geometry")
-        if ctx.block != (512, 1, 1) or ctx.grid[0] * ctx.grid[1] * ctx.grid[2] != B * H * S // BM:
-            raise TemplateMismatch("launch geometry")
+        if ctx.block != (512, 1, 1) or tuple(ctx.grid[1:]) != (1, 1) or \
+                ctx.grid[0] != B * H * S // BM:
+            raise TemplateMismatch("launch geometry (512 threads, a 1-D grid of one CTA per unit)")
         self = cls()
         self.ctx, self.q, self.k, self.v, self.out, self.scale_buf = ctx, q, k_, v, out, scale_buf
         self.B, self.H, self.S, self.D = B, H, S, D
@@ -187,12 +256,21 @@ class AttentionTemplate:
             raise TemplateMismatch("meta smem_bytes too small for 2+2 K/V stages")
         self.SK, self.SV = (n + 1) // 2, n // 2
         self.split_p = bool(cls.SPLIT_P.get(D, False)) and self.NT * (128 + 64 + D) <= 512
+        # (a CTA's half of a V block is D/2 columns: whole 64-column boxes)
         self.pair = (bool(cls.PAIR.get(D, False)) and not self.split_p and self.NT == 2
-                     and (S // 256) % 2 == 0 and tuple(ctx.grid[1:]) == (1, 1))
+                     and D % 128 == 0 and (S // 256) % 2 == 0 and tuple(ctx.grid[1:]) == (1, 1))
         if self.pair:
             # K and V stages hold half a block each: twice as many fit
             n = min(12, avail // (TB // 2))
             self.SK, self.SV = (n + 1) // 2, n // 2
+        self.units = B * H * S // BM
+        # persistent only when the launch's shared memory keeps one CTA per
+        # SM (228 KiB an SM): two co-resident workers would queue on the
+        # 512-column tensor-memory allocation while other SMs sit idle
+        self.persist = (bool(cls.PERSIST) and self.NT == 2 and not self.pair
+                        and ctx.smem_bytes > 114 * 1024)
+        self.sched = unit_schedule(self.units, WORKERS if self.persist else self.units,
+                                   self.persist and bool(cls.TAIL_SPLIT))
         return self
 
     # ------------------------------------------------------------------- emit
@@ -217,6 +295,13 @@ class AttentionTemplate:
             k.directive("cluster 2 1 1")
         k.decl(".extern .shared .align 1024 .b8 __emmy_smem[];")
         k.decl(".global .align 4 .u32 __emmy_status;")
+        W_, _, RU_, half_ = self.sched
+        if half_:
+            # split units: each CTA's partial O [256][D], then its m[256]
+            # and l[256], per (leftover unit, key half); one arrival counter
+            # per leftover unit, 2 added per launch (even: nobody finished)
+            k.decl(f".global .align 32 .b8 __emmy_part[{2 * RU_ * 256 * (D + 2) * 4}];")
+            k.decl(f".global .align 4 .u32 __emmy_pairs[{RU_}];")
         rows = self.B * self.H * S
         for nm, buf in (("tmapQ", self.q), ("tmapK", self.k), ("tmapV", self.v)):
             bk = 64 if pair and nm == "tmapK" else 128
@@ -236,14 +321,38 @@ class AttentionTemplate:
         lane = k.reg("r")
         k(f"and.b32 {lane}, {tid}, 31;")
         cta = k.special("%ctaid.x")
-        bh = k.reg("r")
-        k(f"div.u32 {bh}, {cta}, {QB};")
-        qb = k.reg("r")
-        k(f"rem.u32 {qb}, {cta}, {QB};")
-        krow0 = k.reg("r")
-        k(f"mul.lo.u32 {krow0}, {bh}, {S};")
-        qrow0 = k.reg("r")
-        k(f"mad.lo.u32 {qrow0}, {qb}, {128 * NT}, {krow0};")
+        W, NF, RU, half = self.sched
+        if W < self.units or half:
+            k.comment(f"persistent: {W} worker CTAs, {NF} full rounds of {self.units} units"
+                      + (f", {RU} leftover units split by keys over {2 * RU} CTAs" if half
+                         else f", {RU} leftover units"))
+        pidle = k.reg("p")
+        k(f"setp.ge.u32 {pidle}, {cta}, {W};")
+        idle = k.label("IDLE")
+        k(f"@{pidle} bra {idle};")
+        nunit = k.reg("r")                 # units of this CTA
+        pnu = k.reg("p")
+        k(f"setp.lt.u32 {pnu}, {cta}, {2 * RU if half else RU};")
+        k(f"selp.u32 {nunit}, {NF + 1}, {NF}, {pnu};")
+        u = k.reg("r")                     # unit iteration of the role
+        g0 = k.reg("r")                    # its first key block, counted over all units
+        gend = k.reg("r")                  # one past its last
+
+        def unit_coords(want_q=True):
+            """(first query row, first key row, half-unit predicate or None) of
+            unit iteration ``u``; sets ``g0`` and ``gend``."""
+            k(f"mul.lo.u32 {g0}, {u}, {NB};")
+            k(f"add.u32 {gend}, {g0}, {NB};")
+            r = unit_rows(k, u, cta, self.sched, QB, S, NT, want_q)
+            if half:                       # a split unit: half of the key blocks
+                k(f"@{r[2]} sub.u32 {gend}, {gend}, {NB // 2};")
+            return r
+
+        def unit_loop_tail(top):
+            k(f"add.u32 {u}, {u}, 1;")
+            pu = k.reg("p")
+            k(f"setp.lt.u32 {pu}, {u}, {nunit};")
+            k(f"@{pu} bra {top};")
         SK, SV = self.SK, self.SV
         if pair:
             rank = k.special("%cluster_ctarank")
@@ -281,7 +390,11 @@ class AttentionTemplate:
         R = max(SK, SV)
         DONE = S_FREE + NT
         DRAIN = DONE + (R if split else 0)   # the MMA thread's own ops in flight at exit
-        NSLOT = DRAIN + 1
+        Q_EMPTY = DRAIN + 1            # every Q K^T of the unit done: Q may be reloaded
+        MERGE_READY = Q_EMPTY + 1      # split unit: every softmax warp wrote its partial
+        MERGE_GO = MERGE_READY + 1     # split unit: this CTA merges
+        MERGE_SKIP = MERGE_GO + 1      # split unit: the other CTA merges
+        NSLOT = MERGE_SKIP + 1
         assert NSLOT * 8 + 4 <= 512
         tslot = k.reg("r")
         k(f"add.u32 {tslot}, {bars}, {NSLOT * 8};")
@@ -297,7 +410,8 @@ class AttentionTemplate:
             else:
                 # pair: the leader's P_READY counts both CTAs' softmax warps
                 cnt = (8 if pair else 4) if P_READY <= slot < P_READY + NT else 1
-
+            if slot == MERGE_READY:
+                cnt = 4 * NT
             k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * slot}], {cnt};")
         k("fence.mbarrier_init.release.cluster;")
         for r in (tq, tk, tv):
@@ -383,7 +497,7 @@ class AttentionTemplate:
 
         j = k.reg("r")
 
-        def producer(which, warp_id, tmap, ring, depth, full, empty, load_q):
+        def producer(which, warp_id, tmap, ring=None, depth=0, full=None, empty=None):
             pp = k.reg("p")
             k(f"setp.eq.u32 {pp}, {warp}, {warp_id};")
             k(f"and.pred {pp}, {pp}, {pl0};")
@@ -403,7 +517,21 @@ class AttentionTemplate:
                 r = k.reg("r")
                 k(f"mapa.shared::cluster.u32 {r}, {addr}, 0;")
                 return r
-            if load_q:
+            k(f"mov.u32 {u}, 0;")
+            utop = k.label(f"UNIT_{which}")
+            k.mark(utop)
+            if which == "Q":
+                # the unit's Q tiles, once the previous unit's last Q K^T is done
+                qrow0, _, _ = unit_coords()
+                first = k.label("Q_FIRST")
+                pu0 = k.reg("p")
+                k(f"setp.eq.u32 {pu0}, {u}, 0;")
+                k(f"@{pu0} bra {first};")
+                qpar = k.reg("r")
+                k(f"sub.u32 {qpar}, {u}, 1;")
+                k(f"and.b32 {qpar}, {qpar}, 1;")
+                wait(k, bar(Q_EMPTY), qpar, status, 1, end_p)
+                k.mark(first)
                 qf = bar(Q_FULL)
                 k(f"{arm}mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qf}], {ncta * NT * TB};")
                 qft = target(qf)
@@ -413,21 +541,32 @@ class AttentionTemplate:
                     for i in range(NBX):
                         k(f"{cpy} [{qs}+{t * TB + i * 16384}], [{tq}, {{{64 * i}, {qr}}}], "
                           f"[{qft}];")
-            k(f"mov.u32 {j}, 0;")
+                unit_loop_tail(utop)
+                k.mark(end_p)
+                return
+            _, krow0, _ = unit_coords(want_q=False)
+            k(f"mov.u32 {j}, {g0};")       # j counts key blocks over all units
             top = k.label(f"PROD_{which}")
             k.mark(top)
             st_, ph_ = ring_slot(j, depth)
             if split:
                 # the stage's previous block b = j - depth is free once the
                 # P V iteration that last read it is done: V(b) -> DONE(b);
-                # K(b) (read by the Q K^T of iteration b-1) -> DONE(max(b-1, 0))
+                # K(b), read by the Q K^T issued in iteration b-1 -> DONE(b-1),
+                # or, the first block of a unit (its Q K^T issued before the
+                # unit's first iteration) -> DONE(b)
                 nowait = k.label(f"NOWAIT_{which}")
                 pf = k.reg("p")
                 k(f"setp.lt.u32 {pf}, {j}, {depth};")
                 k(f"@{pf} bra {nowait};")
                 n_ = k.reg("r")
-                k(f"sub.u32 {n_}, {j}, {depth + (1 if which == 'K' else 0)};")
-                k(f"max.s32 {n_}, {n_}, 0;")
+                k(f"sub.u32 {n_}, {j}, {depth};")
+                if which == "K":
+                    bm = k.reg("r")
+                    k(f"rem.u32 {bm}, {n_}, {NB};")
+                    pb = k.reg("p")
+                    k(f"setp.ne.u32 {pb}, {bm}, 0;")
+                    k(f"@{pb} sub.u32 {n_}, {n_}, 1;")
                 ds, dph = ring_slot(n_, R)
                 wait(k, bar(DONE, ds), dph, status, 1, end_p)
                 k.mark(nowait)
@@ -436,7 +575,8 @@ class AttentionTemplate:
                 k(f"xor.b32 {par}, {ph_}, 1;")
                 wait(k, bar(empty, st_), par, status, 1, end_p)
             kr = k.reg("r")
-            k(f"mad.lo.u32 {kr}, {j}, 128, {krow0};")
+            k(f"sub.u32 {kr}, {j}, {g0};")
+            k(f"mad.lo.u32 {kr}, {kr}, 128, {krow0};")
             stage = TBK if which == "K" else TBV
             dst = k.reg("r")
             k(f"mad.lo.u32 {dst}, {st_}, {stage}, {ring};")
@@ -459,16 +599,18 @@ class AttentionTemplate:
             else:
                 for i in range(NBX):
                     k(f"{cpy} [{dst}+{i * 16384}], [{tmap}, {{{64 * i}, {kr}}}], [{fbt}];")
-            k.comment(f"@trace {10 if load_q else 11} {j}")
+            k.comment(f"@trace {10 if which == 'K' else 11} {j}")
             k(f"add.u32 {j}, {j}, 1;")
             pl = k.reg("p")
-            k(f"setp.lt.u32 {pl}, {j}, {NB};")
+            k(f"setp.lt.u32 {pl}, {j}, {gend};")
             k(f"@{pl} bra {top};")
+            unit_loop_tail(utop)
             k.mark(end_p)
 
-        # ---------------- producers: Q and K on one warp, V on another ----------------
-        producer("K", PROD_K_WARP, tk, kring, SK, K_FULL, K_EMPTY, True)
-        producer("V", PROD_V_WARP, tv, vring, SV, V_FULL, V_EMPTY, False)
+        # ---------------- producers: Q, K and V, one warp each ----------------
+        producer("Q", PROD_Q_WARP, tq)
+        producer("K", PROD_K_WARP, tk, kring, SK, K_FULL, K_EMPTY)
+        producer("V", PROD_V_WARP, tv, vring, SV, V_FULL, V_EMPTY)
 
         # ---------------- MMA issuer ----------------
         pm = k.reg("p")
@@ -492,7 +634,6 @@ class AttentionTemplate:
         k(f"setp.ne.u32 {pfalse}, 0, 0;")
         zero = k.reg("r")
         k(f"mov.u32 {zero}, 0;")
-        wait(k, bar(Q_FULL), zero, status, 2, end_mma)
         dq = []
         for t in range(NT):
             qa = k.reg("r")
@@ -548,9 +689,30 @@ class AttentionTemplate:
                 p_tm.append(r3)
             else:
                 p_tm.append(r1)
+        k(f"mov.u32 {u}, 0;")
+        mtop = k.label("UNIT_M")
+        k.mark(mtop)
+        unit_coords(want_q=False)
+        glast = k.reg("r")
+        k(f"sub.u32 {glast}, {gend}, 1;")
+        qpar = k.reg("r")
+        k(f"and.b32 {qpar}, {u}, 1;")
+        wait(k, bar(Q_FULL), qpar, status, 2, end_mma)
         # block 0 scores of every tile
-        k(f"mov.u32 {j}, 0;")
+        k(f"mov.u32 {j}, {g0};")
         dk0, kst0 = k_ready(j)
+        if split:
+            # the previous unit's last scores have been read
+            sfirst = k.label("S_FIRST")
+            pu0 = k.reg("p")
+            k(f"setp.eq.u32 {pu0}, {u}, 0;")
+            k(f"@{pu0} bra {sfirst};")
+            spar0 = k.reg("r")
+            k(f"sub.u32 {spar0}, {j}, 1;")
+            k(f"and.b32 {spar0}, {spar0}, 1;")
+            wait(k, bar(S_FREE), spar0, status, 2, end_mma)
+            k("tcgen05.fence::after_thread_sync;")
+            k.mark(sfirst)
         for t in range(NT):
             issue_qk(t, dk0, j, not split)
         if split:
@@ -571,7 +733,7 @@ class AttentionTemplate:
             vad = k.reg("r")
             k(f"mad.lo.u32 {vad}, {vst}, {TBV}, {vring};")
             dv = GemmTemplate._desc(k, vad, hiV)
-            k(f"setp.ne.u32 {pacc}, {j}, 0;")
+            k(f"setp.ne.u32 {pacc}, {j}, {g0};")
             k(f"and.b32 {par}, {j}, 1;")
             dk = kst = None
             if not last and self.EARLY_K:
@@ -621,7 +783,7 @@ class AttentionTemplate:
             vad = k.reg("r")
             k(f"mad.lo.u32 {vad}, {vst}, {TBV}, {vring};")
             dv = GemmTemplate._desc(k, vad, hiV)
-            k(f"setp.ne.u32 {pacc}, {j}, 0;")
+            k(f"setp.ne.u32 {pacc}, {j}, {g0};")
             wait(k, bar(P_READY), par, status, 2, end_mma)
             k.comment(f"@trace 1 {j}")
             k("tcgen05.fence::after_thread_sync;")
@@ -640,10 +802,13 @@ class AttentionTemplate:
             block(False)
             k(f"add.u32 {j}, {j}, 1;")
             pl2 = k.reg("p")
-            k(f"setp.lt.u32 {pl2}, {j}, {NB - 1};")
+            k(f"setp.lt.u32 {pl2}, {j}, {glast};")
             k(f"@{pl2} bra {top2};")
-        k(f"mov.u32 {j}, {NB - 1};")
+        # every Q K^T of the unit is issued: Q is free once they complete
+        commit(bar(Q_EMPTY))
+        k(f"mov.u32 {j}, {glast};")
         block(True)
+        unit_loop_tail(mtop)
         k.mark(end_mma)
         # wait (bounded) for this thread's tensor-core operations still in
         # flight, so that no MMA outlives the TMEM allocation on an error path
@@ -702,11 +867,16 @@ class AttentionTemplate:
             k(f"mov.b64 {r}, 0x{val:08X}{val:08X};" if nm != "clamp" else f"mov.b32 {r}, 0x{val:08X};")
             cst[nm] = r
         poly = self.poly_pairs()
+        units_done = k.label("UNITS_DONE")
+        k(f"mov.u32 {u}, 0;")
+        stop = k.label("UNIT_S")
+        k.mark(stop)
+        qrow0, _, shalf = unit_coords()
         m = k.reg("f")                             # max used for the exponents
         k(f"mov.f32 {m}, 0fFF800000;")
         lsum = k.reg("f")
         k(f"mov.f32 {lsum}, 0f00000000;")
-        k(f"mov.u32 {j}, 0;")
+        k(f"mov.u32 {j}, {g0};")
         top3 = k.label("SMX")
         k.mark(top3)
         spar = k.reg("r")
@@ -804,7 +974,8 @@ class AttentionTemplate:
                 ld32=ld32, wait_ld=wait_ld, st16=st16, rescale_o=rescale_o,
                 p_ready_arrive=p_ready_arrive, row_sum=row_sum, max_into=max_into, sc=sc,
                 sc2=sc2, cst=cst, poly=poly, m=m, lsum=lsum, j=j, top3=top3, sfree=sfree,
-                fin=fin, pl0=pl0, NB=NB, R=R, status=status, fail=soft_teardown, wait=wait))
+                fin=fin, pl0=pl0, g0=g0, gend=gend, R=R, status=status, fail=soft_teardown,
+                wait=wait))
         else:
             # the row's 128 scores stay in registers for the whole block
             sv = ld32(0) + ld32(32) + ld32(64) + ld32(96)
@@ -914,7 +1085,7 @@ class AttentionTemplate:
             p_pass(meff, False)
             skip_rs = k.label("NO_RESCALE")
             pj0 = k.reg("p")
-            k(f"setp.eq.u32 {pj0}, {j}, 0;")
+            k(f"setp.eq.u32 {pj0}, {j}, {g0};")
             k(f"@{pj0} bra {skip_rs};")
             rescale_o(alpha)
             k.mark(skip_rs)
@@ -927,17 +1098,34 @@ class AttentionTemplate:
             k(f"add.rn.f32 {lsum}, {lsum}, {rsum};")
             k(f"add.u32 {j}, {j}, 1;")
             pl3 = k.reg("p")
-            k(f"setp.lt.u32 {pl3}, {j}, {NB};")
+            k(f"setp.lt.u32 {pl3}, {j}, {gend};")
             k(f"@{pl3} bra {top3};")
         # epilogue: O row * (1 / l) -> global
+        def done_wait(blk):
+            """Wait for DONE of key block ``blk`` (a register): ring slot
+            blk % R, its (blk / R)-th completion."""
+            ds = k.reg("r")
+            k(f"rem.u32 {ds}, {blk}, {R};")
+            fpar = k.reg("r")
+            k(f"div.u32 {fpar}, {blk}, {R};")
+            k(f"and.b32 {fpar}, {fpar}, 1;")
+            fa = k.reg("r")
+            k(f"mad.lo.u32 {fa}, {ds}, 8, {fin};")
+            wait(k, fa, fpar, status, 3, soft_teardown)
+
         if split:
-            # the last block's P V: DONE[(NB-1) % R], its ((NB-1) // R)-th completion
-            fl = k.reg("r")
-            k(f"add.u32 {fl}, {fin}, {8 * ((NB - 1) % R)};")
-            wait(k, fl, ((NB - 1) // R) & 1, status, 3, soft_teardown)
+            # the unit's last block's P V
+            gl = k.reg("r")
+            k(f"sub.u32 {gl}, {gend}, 1;")
+            done_wait(gl)
         else:
-            wait(k, fin, self._zero(k), status, 3, soft_teardown)
+            fpar = k.reg("r")                      # FINAL completes once per unit
+            k(f"and.b32 {fpar}, {u}, 1;")
+            wait(k, fin, fpar, status, 3, soft_teardown)
         k("tcgen05.fence::after_thread_sync;")
+        if half:
+            merge = k.label("MERGE")
+            k(f"@{shalf} bra {merge};")
         inv = k.reg("f")
         k(f"rcp.rn.f32 {inv}, {lsum};")
         inv2 = k.reg("rd")
@@ -957,6 +1145,16 @@ class AttentionTemplate:
             for v8 in range(4):
                 k(f"st.global.v8.b32 [{oa}+{128 * c + 32 * v8}], "
                   f"{{{', '.join(regs[8 * v8:8 * v8 + 8])}}};")
+        unit_loop_tail(stop)
+        if half:
+            k(f"bra {units_done};")
+            k.mark(merge)
+            self._merge_split(k, dict(
+                cta=cta, tid=tid, tt=tt, row=row, orow_tm=orow_tm, m=m, lsum=lsum, qrow0=qrow0,
+                obase=obase, wait_ld=wait_ld, done=units_done, pl0=pl0,
+                ready=bar(MERGE_READY), go=bar(MERGE_GO), skip=bar(MERGE_SKIP), status=status,
+                fail=soft_teardown, wait=wait))
+        k.mark(units_done)
         k.mark(end_sm)
         k.mark(soft_teardown)
         k("tcgen05.fence::before_thread_sync;")
@@ -979,6 +1177,7 @@ class AttentionTemplate:
         k("tcgen05.fence::after_thread_sync;")
         k(f"tcgen05.dealloc.{cg}.sync.aligned.b32 {tmem}, 512;")
         k.mark(end)
+        k.mark(idle)
         k("ret;")
         return k.render()
 
@@ -1082,7 +1281,7 @@ class AttentionTemplate:
         # the tile's previous P V is done: its P columns and O rows are free
         skip_w = k.label("FIRST_BLOCK")
         pj0 = k.reg("p")
-        k(f"setp.eq.u32 {pj0}, {j}, 0;")
+        k(f"setp.eq.u32 {pj0}, {j}, {e['g0']};")
         k(f"@{pj0} bra {skip_w};")
         jp = k.reg("r")
         k(f"sub.u32 {jp}, {j}, 1;")                  # DONE of block j-1
@@ -1109,8 +1308,151 @@ class AttentionTemplate:
         k(f"fma.rn.f32 {lsum}, {lsum}, {alpha}, {rsum};")
         k(f"add.u32 {j}, {j}, 1;")
         pl3 = k.reg("p")
-        k(f"setp.lt.u32 {pl3}, {j}, {e['NB']};")
+        k(f"setp.lt.u32 {pl3}, {j}, {e['gend']};")
         k(f"@{pl3} bra {e['top3']};")
+
+    def _merge_split(self, k, e):
+        """Epilogue of a key-split unit.  CTAs 2i and 2i+1 each hold all 256
+        rows of leftover unit i over one half of the keys.  Every softmax
+        thread writes its row's partial -- O unnormalised (to the row's base
+        m), m and l -- to ``__emmy_part`` and fences it (gpu scope); once all
+        softmax warps have arrived on MERGE_READY, thread 0 adds 1 to the
+        unit's counter (acq_rel, gpu scope) and publishes the old value
+        through shared memory (MERGE_GO).  Old value even: the other CTA has
+        not finished and will merge; this CTA is done.  Odd: the other's
+        partial is complete and each thread merges its row.  Thread 0 tells
+        the others by which barrier it arrives on (MERGE_GO or MERGE_SKIP;
+        they poll both, bounded like every wait):
+        m = max(m_a, m_b), f = 2^(m_x - m), l = l_a f_a + l_b f_b,
+        O = (O_a f_a + O_b f_b) / l -- a product per side and one add, so
+        the result does not depend on which CTA merges.  No thread waits for
+        the other CTA: the later one merges, whichever it is."""
+        D = self.D
+        W, _, RU, _ = self.sched
+        PER = 256 * (D + 2) * 4                 # bytes per (unit, key half)
+        cta, tt, row = e["cta"], e["tt"], e["row"]
+        slot = k.reg("r")
+        k(f"shr.u32 {slot}, {cta}, 1;")
+        hk = k.reg("r")
+        k(f"and.b32 {hk}, {cta}, 1;")
+        rr = k.reg("r")                         # row within the unit
+        k(f"mad.lo.u32 {rr}, {tt}, 128, {row};")
+        part = k.reg("rd")
+        k(f"mov.u64 {part}, __emmy_part;")
+
+        def rows_of(half_reg):
+            """(O row, m, l) addresses of row rr in the partial of key half
+            ``half_reg``."""
+            pi = k.reg("r")
+            k(f"mad.lo.u32 {pi}, {slot}, 2, {half_reg};")
+            base = k.reg("rd")
+            k(f"mul.wide.u32 {base}, {pi}, {PER};")
+            k(f"add.s64 {base}, {base}, {part};")
+            o = k.reg("rd")
+            k(f"mul.wide.u32 {o}, {rr}, {D * 4};")
+            k(f"add.s64 {o}, {o}, {base};")
+            ml = k.reg("rd")
+            k(f"mul.wide.u32 {ml}, {rr}, 4;")
+            k(f"add.s64 {ml}, {ml}, {base};")
+            return o, ml                        # m at ml + 256 D 4, l 1 KiB after
+
+        own_o, own_ml = rows_of(hk)
+        for c in range(D // 32):
+            regs = k.regs("r", 32)
+            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, "
+              f"[{e['orow_tm']}+{32 * c}];")
+            e["wait_ld"]()
+            for v8 in range(4):
+                k(f"st.global.v8.b32 [{own_o}+{128 * c + 32 * v8}], "
+                  f"{{{', '.join(regs[8 * v8:8 * v8 + 8])}}};")
+        k(f"st.global.f32 [{own_ml}+{256 * D * 4}], {e['m']};")
+        k(f"st.global.f32 [{own_ml}+{256 * (D + 1) * 4}], {e['lsum']};")
+        k("fence.acq_rel.gpu;")
+        k("bar.warp.sync 0xffffffff;")
+        k(f"@{e['pl0']} mbarrier.arrive.shared::cta.b64 _, [{e['ready']}];")
+        pt0 = k.reg("p")
+        k(f"setp.eq.u32 {pt0}, {e['tid']}, 0;")
+        not0 = k.label("MERGE_WAIT")
+        k(f"@!{pt0} bra {not0};")
+        e["wait"](k, e["ready"], 0, e["status"], 3, e["fail"])
+        cnt = k.reg("rd")
+        k(f"mov.u64 {cnt}, __emmy_pairs;")
+        ca = k.reg("rd")
+        k(f"mul.wide.u32 {ca}, {slot}, 4;")
+        k(f"add.s64 {ca}, {ca}, {cnt};")
+        old = k.reg("r")
+        k(f"atom.acq_rel.gpu.global.add.u32 {old}, [{ca}], 1;")
+        k(f"and.b32 {old}, {old}, 1;")
+        psecond = k.reg("p")
+        k(f"setp.ne.u32 {psecond}, {old}, 0;")
+        k(f"@{psecond} mbarrier.arrive.shared::cta.b64 _, [{e['go']}];")
+        k(f"@!{psecond} mbarrier.arrive.shared::cta.b64 _, [{e['skip']}];")
+        k.mark(not0)
+        # poll both decisions, bounded by %globaltimer
+        domerge = k.label("MERGE_ROWS")
+        pg, ps = k.reg("p"), k.reg("p")
+        t0, t1 = k.reg("rd"), k.reg("rd")
+        k(f"mov.u64 {t0}, %globaltimer;")
+        poll = k.label("MERGE_POLL")
+        k.mark(poll)
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {pg}, [{e['go']}], 0;")
+        k(f"@{pg} bra {domerge};")
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {ps}, [{e['skip']}], 0;")
+        k(f"@{ps} bra {e['done']};")
+        k(f"mov.u64 {t1}, %globaltimer;")
+        k(f"sub.s64 {t1}, {t1}, {t0};")
+        pt = k.reg("p")
+        k(f"setp.lt.s64 {pt}, {t1}, {WAIT_NS};")
+        k(f"@{pt} bra {poll};")
+        k(f"st.global.u32 [{e['status']}], 3;")
+        k(f"bra {e['fail']};")
+        k.mark(domerge)
+        # the other CTA's partial is complete: merge
+        k("fence.acq_rel.gpu;")
+        ho = k.reg("r")
+        k(f"xor.b32 {ho}, {hk}, 1;")
+        oth_o, oth_ml = rows_of(ho)
+        mb, lb = k.reg("f"), k.reg("f")
+        k(f"ld.global.f32 {mb}, [{oth_ml}+{256 * D * 4}];")
+        k(f"ld.global.f32 {lb}, [{oth_ml}+{256 * (D + 1) * 4}];")
+        mm = k.reg("f")
+        k(f"max.f32 {mm}, {e['m']}, {mb};")
+        fa, fb, t_ = k.reg("f"), k.reg("f"), k.reg("f")
+        k(f"sub.rn.f32 {t_}, {e['m']}, {mm};")
+        k(f"ex2.approx.ftz.f32 {fa}, {t_};")
+        k(f"sub.rn.f32 {t_}, {mb}, {mm};")
+        k(f"ex2.approx.ftz.f32 {fb}, {t_};")
+        la, l_ = k.reg("f"), k.reg("f")
+        k(f"mul.rn.f32 {la}, {e['lsum']}, {fa};")
+        k(f"mul.rn.f32 {l_}, {lb}, {fb};")
+        k(f"add.rn.f32 {l_}, {la}, {l_};")
+        inv = k.reg("f")
+        k(f"rcp.rn.f32 {inv}, {l_};")
+        grow = k.reg("r")
+        k(f"add.u32 {grow}, {rr}, {e['qrow0']};")
+        oa = k.reg("rd")
+        k(f"mul.wide.u32 {oa}, {grow}, {D * 4};")
+        k(f"add.s64 {oa}, {oa}, {e['obase']};")
+        for c in range(D // 32):
+            regs = k.regs("r", 32)
+            k(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, "
+              f"[{e['orow_tm']}+{32 * c}];")
+            e["wait_ld"]()
+            for v4 in range(8):
+                ob = k.regs("f", 4)
+                k(f"ld.global.v4.f32 {{{', '.join(ob)}}}, [{oth_o}+{128 * c + 16 * v4}];")
+                for i in range(4):
+                    a = regs[4 * v4 + i]
+                    x = k.reg("f")
+                    k(f"mul.rn.f32 {x}, {a}, {fa};")
+                    y = k.reg("f")
+                    k(f"mul.rn.f32 {y}, {ob[i]}, {fb};")
+                    k(f"add.rn.f32 {x}, {x}, {y};")
+                    k(f"mul.rn.f32 {x}, {x}, {inv};")
+                    k(f"mov.b32 {a}, {x};")
+            for v8 in range(4):
+                k(f"st.global.v8.b32 [{oa}+{128 * c + 32 * v8}], "
+                  f"{{{', '.join(regs[8 * v8:8 * v8 + 8])}}};")
 
     def poly_pairs(self) -> set:
         """Which of the 16 column pairs of a 32-column chunk take the FMA-pipe

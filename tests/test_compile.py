@@ -300,7 +300,7 @@ def test_gemm_raster_is_a_bijection(MB, NB, group):
     all clusters every column of every (row band, column block) is computed
     exactly once -- including a last raster group with fewer bands and the
     split tails (8 x 32 = 256 tiles, the matmul shard of one GPU in eight:
-    34 leftover tiles become 68 halves)."""
+    34 leftover tiles become 68 halves of 256 x 128)."""
     from emmy_b200.ptx import Kernel
     from emmy_b200.templates.gemm_persistent import (WORKERS, cluster_tiles, raster, schedule,
                                                      tile_index)
@@ -327,6 +327,47 @@ def test_gemm_raster_is_a_bijection(MB, NB, group):
             for col in range(off, off + width, 64):
                 cover[(band, blk, col)] = cover.get((band, blk, col), 0) + 1
     assert len(cover) == tiles * 4 and set(cover.values()) == {1}
+
+
+@pytest.mark.parametrize("units,workers", [(512, 148), (4096, 148), (4, 148), (150, 148),
+                                           (160, 148), (296, 148), (300, 148), (7, 3)])
+@pytest.mark.parametrize("split", [True, False])
+def test_attention_units_cover_every_row_once(units, workers, split):
+    """The persistent attention schedule (``attention.cta_units``, and its
+    emitted form ``unit_rows`` run by interpreting the integer PTX): over all
+    worker CTAs every (unit, key) pair is computed exactly once -- a whole
+    unit by one CTA, or a split unit's 256 rows by two CTAs over the two
+    halves of the keys, only in the last iteration of each.  Key rows are
+    the unit's own (batch, head)'s.  512 units on 148 workers is one GPU's
+    share of the attention config at 8 GPUs: 3 full rounds and 68 leftover
+    units split over 136 CTAs."""
+    from emmy_b200.ptx import Kernel
+    from emmy_b200.templates.attention import cta_units, unit_rows, unit_schedule
+    S, NT = 1024, 2
+    QB = S // (128 * NT)
+    sched = unit_schedule(units, workers, split)
+    W, NF, R, half = sched
+    assert half == (split and R > 0 and 2 * R <= W)
+    k = Kernel("t", [])
+    u, cta = k.reg("r"), k.reg("r")
+    q0, k0, ph_ = unit_rows(k, u, cta, sched, QB, S, NT)
+    prog = [ln.strip().rstrip(";") for ln in k.lines]
+    cover = {}
+    for c in range(workers + 2):
+        work = cta_units(c, units, workers, split)
+        assert (c >= W) == (not work)
+        assert all(h is None for _, h in work[:-1])
+        for i, (unit, kh) in enumerate(work):
+            env = _interpret(prog, {u: i, cta: c})
+            bh, qb = divmod(unit, QB)
+            assert env[q0] == bh * S + qb * 256
+            assert env[k0] == bh * S + (0 if kh is None else kh * S // 2)
+            if half:
+                assert env[ph_] == (kh is not None)
+            for h in ((0, 1) if kh is None else (kh,)):
+                cover[(unit, h)] = cover.get((unit, h), 0) + 1
+    assert sorted(cover) == [(x, h) for x in range(units) for h in (0, 1)]
+    assert set(cover.values()) == {1}
 
 
 def test_pointwise_batch_follows_the_launch():

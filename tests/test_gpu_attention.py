@@ -110,3 +110,47 @@ def test_attention_cta_pairs(kw, ramp, monkeypatch):
     g, m = p.build()
     assert compile_graph(g, m).template.pair
     _run(p, transform=_key_ramp if ramp else None)
+
+
+# persistent launches: 148 worker CTAs loop over (batch, head, 256-row) units
+UNIT_CASES = [dict(B=1, H=40, S=1024, D=128), dict(B=1, H=40, S=1024, D=64),
+              dict(B=1, H=80, S=1024, D=128), dict(B=1, H=80, S=1024, D=64),
+              dict(B=1, H=62, S=1024, D=128), dict(B=1, H=62, S=1024, D=64)]
+
+
+@pytest.mark.parametrize("kw", UNIT_CASES,
+                         ids=[f"h{c['H']}_d{c['D']}" for c in UNIT_CASES])
+@pytest.mark.parametrize("ramp", [False, True], ids=["plain", "growing"])
+def test_attention_persistent_units(kw, ramp):
+    """Two-tile CTAs run persistent: 160 units (one round, 12 leftover units
+    each split by keys over two CTAs: CTAs 0..23 compute all 256 rows of a
+    unit over half of its key blocks, and the later of each pair merges the
+    two partials), 320 units (two rounds, 24 leftover units on 48 CTAs), 248
+    units (100 leftover: too many to split, CTAs 0..99 take a second whole
+    unit).  Every role walks the same unit list; Q is reloaded once the
+    unit's last Q K^T is done.  Checked in full, also with the exponent base
+    moving inside blocks (the two halves then merge rows whose bases differ
+    by many binades)."""
+    from emmy_b200.compiler import compile_graph
+    from emmy_b200.templates.attention import cta_units
+    p = synth.attention(**kw)
+    g, m = p.build()
+    t = compile_graph(g, m).template
+    assert t.persist and t.sched[0] == 148
+    work = [cta_units(c, t.units, 148, True) for c in range(148)]
+    assert sum(len(w) for w in work) > 148
+    _run(p, transform=_key_ramp if ramp else None)
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_attention_gpu_shard_of_eight(D):
+    """One GPU's share of the attention config at 8 GPUs (B=1, H=32, S=4096:
+    512 units, 3 full rounds on 148 CTAs and 68 leftover units split by keys
+    over 136 CTAs), checked on heads of the first rounds and of the split
+    tail (units 444..511 are heads 27..31)."""
+    from emmy_b200.compiler import compile_graph
+    p = synth.attention(B=1, H=32, S=4096, D=D)
+    g, m = p.build()
+    t = compile_graph(g, m).template
+    assert t.sched == (148, 3, 68, True)
+    _run(p, heads=[(0, 0), (0, 13), (0, 27), (0, 29), (0, 31)])
