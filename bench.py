@@ -754,7 +754,8 @@ def run_shards(rank: int, world: int, dev) -> dict:
         if err:
             d["error"] = err
         if nm == "full_sum":
-            d["collective"] = "NCCL all-reduce of the per-rank partial, inside each timed launch"
+            d["collective"] = ("NCCL all-reduce of the per-rank partial, inside each timed step "
+                               "(output reset, sum kernel and all-reduce replayed as one CUDA graph)")
         shards[nm] = d
     return shards
 
@@ -762,8 +763,11 @@ def run_shards(rank: int, world: int, dev) -> dict:
 def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -> dict:
     """The strong-scaled full sum: each rank sums its CTA slices of the global
     input, then one NCCL all-reduce finishes the sum; both are inside each
-    timed step (CUDA events on the launching stream, which the all-reduce
-    joins).  Checked against the float64 sum of all ranks' slices."""
+    timed step.  The step (output reset, sum kernel, all-reduce) is captured
+    once as a CUDA graph and each replay is bracketed by CUDA events on the
+    launching stream, so the time is the device's: no host launch gap
+    between the kernel and the collective.  Checked against the float64 sum
+    of all ranks' slices."""
     import numpy as np
     import torch
     from emmy_b200 import dist as D
@@ -772,13 +776,13 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -
     kern = harness.CompiledKernel(*p.build())
     bufs = harness.Buffers.random(kern, seed=rank)
     stream = torch.cuda.current_stream()
-    sh = stream.cuda_stream
     out = bufs.t["sum_1"]
     L = native.lib()
     k = kern.kernel()
     arr, keep = kern.params(bufs.ptrs())
 
     def step():
+        sh = torch.cuda.current_stream().cuda_stream
         native.check(L.emmy_memset_async(out.data_ptr(), 0, 4, sh))
         native.check(L.emmy_launch(k.h, native.u32x3(kern.grid), native.u32x3(kern.block),
                                    kern.smem, kern._cluster_arg(), arr, sh))
@@ -788,14 +792,24 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -
         step()
     D.barrier()
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(warmup):
+        graph.replay()
+    D.barrier()
+    torch.cuda.synchronize()
     ms = []
     for _ in range(steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        step()
+        graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
         ms.append(e0.elapsed_time(e1))
+    # a graph holding NCCL calls is released before the process group is
+    del graph
+    torch.cuda.synchronize()
     got = float(out.item())
     part = torch.tensor([float(np.sum(bufs.t["x"].cpu().numpy(), dtype=np.float64))],
                         dtype=torch.float64, device=dev)
@@ -847,7 +861,9 @@ def measure_case(name: str, kw: dict, steps: int, warmup: int, seed: int = 0,
                  extras: bool = False) -> dict:
     """Time one synthesised configuration: ``steps`` launches through the C ABI,
     each bracketed by CUDA events on the launching stream; L2 flushed between
-    launches when the inputs would fit in it.  Then, outside the timing, the
+    launches when the inputs would fit in it (512 MiB written, then that
+    buffer's lines discarded from L2, so the timed launch neither finds its
+    inputs in L2 nor pays the flush's write-back).  Then, outside the timing, the
     outputs are checked (``check_outputs``); a failed check drops the numbers.
     Includes the reference compiler's PTX for the same IR (``oracle/_ref``)
     when it exists, checked the same way.  ``extras`` (the vector add): the
@@ -878,7 +894,9 @@ def measure_case(name: str, kw: dict, steps: int, warmup: int, seed: int = 0,
     flops = synth.algorithmic_flops(p)
     line = {"case": name, "size": kw, "template": kern.kind, "entry": kern.entry,
             "ms_median": round(med, 5), "ms_min": round(float(np.min(ms)), 5),
-            "launches": steps, "l2_flush": flush is not None,
+            "launches": steps,
+            "l2_flush": ("512 MiB written, then discarded from L2" if flush is not None
+                         else "inputs larger than twice the L2"),
             "regs": kern.image.registers().get(kern.entry), "check": chk}
     if flops:
         tf = flops / (med / 1e3) / 1e12

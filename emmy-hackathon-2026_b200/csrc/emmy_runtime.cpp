@@ -442,6 +442,46 @@ int emmy_mem_free(uint64_t dptr) {
 // ---------------------------------------------------------------------------
 // timing
 // ---------------------------------------------------------------------------
+namespace {
+
+// After the L2 flush (a memset of a buffer larger than L2) the cache holds
+// dirty lines of that buffer; a timed kernel that misses in L2 would pay
+// their write-back to HBM.  This kernel drops every 128-byte line of the
+// flush buffer from L2 with discard.global.L2 (no write-back), so a timed
+// launch starts with neither its inputs nor dirty data in L2.
+const char kDiscardPtx[] =
+    ".version 8.8\n.target sm_100a\n.address_size 64\n"
+    ".visible .entry emmy_l2_discard(.param .u64 p_base, .param .u64 p_lines)\n{\n"
+    "  .reg .pred %q;\n  .reg .b32 %r<5>;\n  .reg .b64 %d<8>;\n"
+    "  ld.param.u64 %d0, [p_base];\n  ld.param.u64 %d1, [p_lines];\n"
+    "  mov.u32 %r0, %tid.x;\n  mov.u32 %r1, %ctaid.x;\n  mov.u32 %r2, %ntid.x;\n"
+    "  mov.u32 %r3, %nctaid.x;\n  mad.wide.u32 %d2, %r1, %r2, 0;\n"
+    "  cvt.u64.u32 %d3, %r0;\n  add.u64 %d2, %d2, %d3;\n  mul.wide.u32 %d4, %r2, %r3;\n"
+    "LOOP:\n  setp.ge.u64 %q, %d2, %d1;\n  @%q bra DONE;\n"
+    "  mad.lo.u64 %d5, %d2, 128, %d0;\n  discard.global.L2 [%d5], 128;\n"
+    "  add.u64 %d2, %d2, %d4;\n  bra LOOP;\nDONE:\n  ret;\n}\n";
+
+// the discard kernel, loaded once per context
+int discard_fn(CUfunction *out) {
+  static std::vector<std::pair<CUcontext, CUfunction>> loaded;
+  CUcontext cur = nullptr;
+  CU(g_drv.CtxGetCurrent(&cur), "cuCtxGetCurrent");
+  for (auto &e : loaded)
+    if (e.first == cur) {
+      *out = e.second;
+      return 0;
+    }
+  CUmodule m;
+  CU(g_drv.ModuleLoadData(&m, kDiscardPtx), "cuModuleLoadData(l2 discard)");
+  CUfunction f;
+  CU(g_drv.ModuleGetFunction(&f, m, "emmy_l2_discard"), "cuModuleGetFunction(l2 discard)");
+  loaded.emplace_back(cur, f);
+  *out = f;
+  return 0;
+}
+
+}  // namespace
+
 int emmy_time_launches(emmy_kernel_t k, const uint32_t grid[3], const uint32_t block[3],
                        uint32_t smem, const uint32_t *cluster, void **params, void *stream,
                        int warmup, int iters, uint64_t flush_dptr, size_t flush_bytes,
@@ -451,10 +491,22 @@ int emmy_time_launches(emmy_kernel_t k, const uint32_t grid[3], const uint32_t b
       (n_zero > 0 && (!zero_dptrs || !zero_bytes)))
     return fail(EMMY_EINVAL, "emmy_time_launches: bad argument");
   CUstream s = static_cast<CUstream>(stream);
+  CUfunction discard = nullptr;
+  if (flush_dptr && flush_bytes)
+    if (int e = discard_fn(&discard)) return e;
   auto prep = [&](int it) -> int {
-    if (flush_dptr && flush_bytes)
+    if (flush_dptr && flush_bytes) {
       CU(g_drv.MemsetD8Async(flush_dptr, static_cast<unsigned char>(it & 0xff), flush_bytes, s),
          "L2 flush");
+      // whole 128-byte lines inside the buffer only: a line that reaches
+      // past either end may hold someone else's data
+      uint64_t base = (flush_dptr + 127) & ~static_cast<uint64_t>(127);
+      uint64_t end = (flush_dptr + flush_bytes) & ~static_cast<uint64_t>(127);
+      uint64_t lines = end > base ? (end - base) / 128 : 0;
+      void *args[] = {&base, &lines};
+      CU(g_drv.LaunchKernel(discard, 148 * 4, 1, 1, 256, 1, 1, 0, s, args, nullptr),
+         "L2 discard");
+    }
     for (int z = 0; z < n_zero; ++z)
       CU(g_drv.MemsetD8Async(zero_dptrs[z], 0, zero_bytes[z], s), "zero output");
     return 0;

@@ -8,13 +8,20 @@ row, the online-softmax ``Assign``/``Accum`` chain with the running max
 then ``reciprocal`` + ``multiply``), here with leading batch/head axes, bf16
 Q/K/V [B,H,S,D] and an f32 output.  The reference lowers each thread's
 micro-tile to scalar FFMAs that recompute the scores per output column
-(``compile.py:1882-1928``).  This template keeps the IR's CTA -> (batch,
-head, BM query rows) assignment, BM = 128 * NT with NT = 1 or 2 query tiles
-of 128 rows, and computes the CTA's rows as:
+(``compile.py:1882-1928``).  This template keeps the IR's units of work --
+(batch, head, BM query rows), BM = 128 * NT with NT = 1 or 2 query tiles of
+128 rows -- and its launch (one CTA per unit).  With two tiles the first 148
+CTAs (one per SM) run persistent, looping over the units (CTA c: c, c + 148,
+...), and every other CTA returns at once; the units of a partial last
+round are split by keys over two CTAs each, the later of the two merging
+the partials (``unit_schedule``, ``_merge_split``).  A unit's rows:
 
-* TMA loads the NT Q tiles once and K and V tiles of 128 keys into two
-  separate rings (3 + 2 stages at D=128, 4 + 4 at D=64; 128-byte swizzle;
-  one copy per CTA), each fed by its own producer thread;
+* TMA loads the NT Q tiles once per unit (their own producer thread, once
+  the previous unit's last Q K^T is done) and K and V tiles of 128 keys into
+  two separate rings (3 + 2 stages at D=128, 4 + 4 at D=64; 128-byte
+  swizzle; one copy per CTA), each fed by its own producer thread; the
+  rings and every per-block barrier run on across units (key blocks are
+  counted over all of the CTA's units);
 * one thread issues, per key block j and query tile t, ``O_t += P_t V_j``
   (P read from TMEM, the ``[a-tmem]`` form; V an MN-major shared operand)
   followed by ``S_t = Q_t K_{j+1}^T`` (M=N=128) into the tile's TMEM score

@@ -132,7 +132,9 @@ EMMY_API int emmy_mem_free(uint64_t dptr);
 /* `warmup` (reference docs/API.md:15-36).  This launches `iters` times       */
 /* back to back on `stream`, records a CUDA event pair around each launch,    */
 /* and between launches (outside the events) optionally writes `flush_bytes`  */
-/* of `flush_dptr` to evict L2 and re-zeroes `n_zero` output buffers.         */
+/* of `flush_dptr` to evict L2, then drops that buffer's lines from L2 with   */
+/* discard.global.L2 (so no dirty line of the flush is written back inside a  */
+/* timed launch), and re-zeroes `n_zero` output buffers.                      */
 /* ms_out receives `iters` per-launch times in milliseconds.                  */
 /* ------------------------------------------------------------------------ */
 EMMY_API int emmy_time_launches(emmy_kernel_t k, const uint32_t grid[3], const uint32_t block[3],

@@ -103,7 +103,13 @@ def test_shard_kwargs_cover_the_problem(world):
         if name.startswith("matmul"):
             assert all(p["M"] % 256 == 0 for p in parts)
         if name == "full_sum":
-            assert all(p["n"] == p["ctas"] * D.SUM_SLICE for p in parts)
+            # whole slices per rank, each on a power-of-two number of CTAs,
+            # at least 1024 CTAs a launch (2048 slices: one CTA each at N=1)
+            for p in parts:
+                split = p["ctas"] * D.SUM_SLICE // p["n"]
+                assert p["n"] % D.SUM_SLICE == 0 and split & (split - 1) == 0
+                assert p["ctas"] >= min(D.SUM_MIN_CTAS, p["n"] // D.SUM_SLICE)
+                assert D.SUM_SLICE % split == 0 and p["ctas"] < 2 * D.SUM_MIN_CTAS or split == 1
     want = {"vector_add": "pointwise", "full_sum": "rows", "row_mean": "rows", "softmax": "rows",
             "matmul_bf16": "gemm", "attention_d64": "attention"}
     for name, kind in want.items():
