@@ -725,7 +725,7 @@ def run_shards(rank: int, world: int, dev) -> dict:
         kw = D.shard_kwargs(nm, rank, world)
         try:
             if nm == "full_sum":
-                r = measure_full_sum_strong(kw, 10, 3, dev, rank)
+                r = measure_full_sum_strong(kw, 20, 3, dev, rank)
             else:
                 r = measure_case(nm, kw, 10, 3, seed=rank)
             ms_r, err = r["ms_median"], None
@@ -764,10 +764,10 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -
     """The strong-scaled full sum: each rank sums its CTA slices of the global
     input, then one NCCL all-reduce finishes the sum; both are inside each
     timed step.  The step (output reset, sum kernel, all-reduce) is captured
-    once as a CUDA graph and each replay is bracketed by CUDA events on the
-    launching stream, so the time is the device's: no host launch gap
-    between the kernel and the collective.  Checked against the float64 sum
-    of all ranks' slices."""
+    once as a CUDA graph and ``steps`` replays run back to back between one
+    pair of CUDA events on the launching stream (after a barrier), so the
+    time per step is the device's: no host launch gap between the kernel and
+    the collective.  Checked against the float64 sum of all ranks' slices."""
     import numpy as np
     import torch
     from emmy_b200 import dist as D
@@ -799,14 +799,15 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -
         graph.replay()
     D.barrier()
     torch.cuda.synchronize()
-    ms = []
+    # the steps back to back between one event pair (a host synchronisation
+    # after every step would put the ranks' host skew into each all-reduce)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
     for _ in range(steps):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
         graph.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ms.append(e0.elapsed_time(e1))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = [e0.elapsed_time(e1) / steps]
     # a graph holding NCCL calls is released before the process group is
     del graph
     torch.cuda.synchronize()
