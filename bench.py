@@ -907,6 +907,10 @@ def measure_case(name: str, kw: dict, steps: int, warmup: int, seed: int = 0,
             # fp32 through 3xTF32: tf32 runs at half the bf16 rate and every
             # product costs three tf32 MMAs
             peak, basis = peak / 2 / 3, f"3xTF32 effective = {psrc} bf16 peak / 2 / 3"
+            # the tensor work itself: three tf32 products per multiply-add
+            line["raw_tf32"] = {"TFLOP/s": round(3 * tf, 1), "peak": round(3 * peak, 1),
+                                "frac": round(tf / peak, 3),
+                                "basis": f"{psrc} bf16 peak / 2 (the tf32 rate)"}
         line.update({"TFLOP/s": round(tf, 1), "peak": round(peak, 1), "peak_basis": basis,
                      "frac": round(tf / peak, 3), "flops": flops})
     else:
