@@ -756,14 +756,46 @@ def run_shards(rank: int, world: int, dev) -> dict:
         if nm == "full_sum":
             d["collective"] = ("NCCL all-reduce of the per-rank partial, inside each timed step "
                                "(output reset, sum kernel and all-reduce replayed as one CUDA graph)")
+            if world > 1:
+                d["nvlink_finish"] = peer_finish_shard(kw, world, rank, dev, hbm)
         shards[nm] = d
     return shards
 
 
-def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -> dict:
+def peer_finish_shard(kw: dict, world: int, rank: int, dev, hbm: float) -> dict:
+    """The strong-scaled full sum with its cross-GPU step done by
+    ``peer.PeerSum`` (partials written into every peer's memory over NVLink,
+    no collective library), timed and checked like the NCCL form."""
+    from emmy_b200 import dist as D
+    from emmy_b200 import synth
+    try:
+        r = measure_full_sum_strong(kw, 20, 3, dev, rank, exchange="nvlink")
+        ms_r, ok_r, err = r["ms_median"], bool(r["check"]["ok"]), None
+    except Exception as e:  # every rank still joins the reductions below
+        r, ms_r, ok_r, err = None, float("inf"), False, f"{type(e).__name__}: {e}"[:300]
+    ms_all = D.max_over_ranks(ms_r, device=dev)
+    ok_all = D.max_over_ranks(0.0 if ok_r else 1.0, device=dev) == 0.0
+    d = {"exchange": "peer.PeerSum: each rank's partial stored into every rank's slot over "
+                     "NVLink (CUDA IPC mappings), one polling kernel per rank, summed in rank "
+                     "order; replayed with the sum kernel as one CUDA graph",
+         "ms_max_over_ranks": round(ms_all, 5) if ok_all else None,
+         "check": {"checked": True, "ok_all_ranks": ok_all,
+                   "status": r["check"]["status"] if r else None}}
+    if ok_all and ms_all < 1e30:
+        gbs = synth.algorithmic_bytes(synth.config("full_sum")) / (ms_all / 1e3) / 1e9
+        d.update({"GB/s": round(gbs, 1), "frac_of_n_peaks": round(gbs / (world * hbm), 3)})
+    if err:
+        d["error"] = err
+    return d
+
+
+def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int,
+                            exchange: str = "nccl") -> dict:
     """The strong-scaled full sum: each rank sums its CTA slices of the global
-    input, then one NCCL all-reduce finishes the sum; both are inside each
-    timed step.  The step (output reset, sum kernel, all-reduce) is captured
+    input, then the ranks' partials are summed across GPUs -- by one NCCL
+    all-reduce (``exchange="nccl"``) or by ``peer.PeerSum``, one kernel per
+    rank that writes its partial into every peer's memory over NVLink and
+    sums what arrives (``"nvlink"``); both are inside each timed step.  The step (output reset, sum kernel, all-reduce) is captured
     once as a CUDA graph and ``steps`` replays run back to back between one
     pair of CUDA events on the launching stream (after a barrier), so the
     time per step is the device's: no host launch gap between the kernel and
@@ -780,13 +812,31 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -
     L = native.lib()
     k = kern.kernel()
     arr, keep = kern.params(bufs.ptrs())
+    ps = None
+    if exchange == "nvlink":
+        from emmy_b200 import peer
+        world = D.from_env().world
+        try:
+            ps = peer.PeerSum(rank, world)
+            built = True
+        except Exception:
+            built = False
+        # every rank maps its peers before any rank launches a kernel that
+        # waits for the others
+        if D.max_over_ranks(0.0 if built else 1.0, device=dev) != 0.0:
+            if ps is not None:
+                ps.close()
+            raise RuntimeError("peer memory could not be mapped on every rank")
 
     def step():
         sh = torch.cuda.current_stream().cuda_stream
         native.check(L.emmy_memset_async(out.data_ptr(), 0, 4, sh))
         native.check(L.emmy_launch(k.h, native.u32x3(kern.grid), native.u32x3(kern.block),
                                    kern.smem, kern._cluster_arg(), arr, sh))
-        D.global_sum(out)
+        if ps is not None:
+            ps.launch(out.data_ptr(), sh)
+        else:
+            D.global_sum(out)
 
     for _ in range(warmup):
         step()
@@ -811,6 +861,11 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -
     # a graph holding NCCL calls is released before the process group is
     del graph
     torch.cuda.synchronize()
+    status = None
+    if ps is not None:
+        status = ps.status()
+        D.barrier()                  # every rank's kernels are done before unmapping
+        ps.close()
     got = float(out.item())
     part = torch.tensor([float(np.sum(bufs.t["x"].cpu().numpy(), dtype=np.float64))],
                         dtype=torch.float64, device=dev)
@@ -819,10 +874,10 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int) -
     rel = abs(got - want) / abs(want)
     del keep
     return {"ms_median": float(np.median(ms)),
-            "check": {"checked": True, "ok": rel <= 1e-4, "status": None, "rel_err": rel,
-                      "err_over_max_ref": rel,
-                      "sample": "the all-reduced sum against the float64 sum of every rank's "
-                                "slices"}}
+            "check": {"checked": True, "ok": rel <= 1e-4 and not status, "status": status,
+                      "rel_err": rel, "err_over_max_ref": rel,
+                      "sample": f"the sum finished by {exchange} against the float64 sum of "
+                                "every rank's slices"}}
 
 
 def back_to_back(kern, ptrs: dict, n: int = 100, reps: int = 5) -> float:

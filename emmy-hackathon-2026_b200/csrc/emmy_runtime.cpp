@@ -81,6 +81,9 @@ struct Driver {
   CUresult (*EventRecord)(CUevent, CUstream);
   CUresult (*EventSynchronize)(CUevent);
   CUresult (*EventElapsedTime)(float *, CUevent, CUevent);
+  CUresult (*IpcGetMemHandle)(CUipcMemHandle *, CUdeviceptr);
+  CUresult (*IpcOpenMemHandle)(CUdeviceptr *, CUipcMemHandle, unsigned);
+  CUresult (*IpcCloseMemHandle)(CUdeviceptr);
 };
 
 Driver g_drv;
@@ -137,7 +140,10 @@ int driver() {
             sym(l, g_drv.EventDestroy, "cuEventDestroy_v2") &&
             sym(l, g_drv.EventRecord, "cuEventRecord") &&
             sym(l, g_drv.EventSynchronize, "cuEventSynchronize") &&
-            sym(l, g_drv.EventElapsedTime, "cuEventElapsedTime");
+            sym(l, g_drv.EventElapsedTime, "cuEventElapsedTime") &&
+            sym(l, g_drv.IpcGetMemHandle, "cuIpcGetMemHandle") &&
+            sym(l, g_drv.IpcOpenMemHandle, "cuIpcOpenMemHandle_v2") &&
+            sym(l, g_drv.IpcCloseMemHandle, "cuIpcCloseMemHandle");
   if (!ok) return fail(EMMY_ENODRIVER, "libcuda.so.1 lacks a required symbol: %s", dlerror());
   CUresult r = g_drv.Init(0);
   if (r != CUDA_SUCCESS) return cuerr(r, "cuInit");
@@ -436,6 +442,37 @@ int emmy_mem_free(uint64_t dptr) {
   if (!dptr) return 0;
   if (int e = ensure_ctx()) return e;
   CU(g_drv.MemFree(dptr), "cuMemFree");
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// peer memory (CUDA IPC): another process's allocation mapped into this one
+// ---------------------------------------------------------------------------
+int emmy_ipc_handle(uint64_t dptr, unsigned char handle_out[64]) {
+  if (!dptr || !handle_out) return fail(EMMY_EINVAL, "emmy_ipc_handle: bad argument");
+  if (int e = ensure_ctx()) return e;
+  CUipcMemHandle h;
+  CU(g_drv.IpcGetMemHandle(&h, static_cast<CUdeviceptr>(dptr)), "cuIpcGetMemHandle");
+  static_assert(sizeof h.reserved == 64, "CUDA IPC handles are 64 bytes");
+  memcpy(handle_out, h.reserved, 64);
+  return 0;
+}
+
+int emmy_ipc_open(const unsigned char handle[64], uint64_t *dptr_out) {
+  if (!handle || !dptr_out) return fail(EMMY_EINVAL, "emmy_ipc_open: bad argument");
+  if (int e = ensure_ctx()) return e;
+  CUipcMemHandle h;
+  memcpy(h.reserved, handle, 64);
+  CUdeviceptr p = 0;
+  CU(g_drv.IpcOpenMemHandle(&p, h, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS), "cuIpcOpenMemHandle");
+  *dptr_out = static_cast<uint64_t>(p);
+  return 0;
+}
+
+int emmy_ipc_close(uint64_t dptr) {
+  if (!dptr) return 0;
+  if (int e = driver()) return e;
+  CU(g_drv.IpcCloseMemHandle(static_cast<CUdeviceptr>(dptr)), "cuIpcCloseMemHandle");
   return 0;
 }
 

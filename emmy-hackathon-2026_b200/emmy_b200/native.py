@@ -29,7 +29,8 @@ EXPORTS = [
     "emmy_module_load", "emmy_module_unload", "emmy_kernel_get", "emmy_kernel_attrs",
     "emmy_module_global", "emmy_tensormap_encode", "emmy_launch", "emmy_memset_async",
     "emmy_memcpy_htod_async", "emmy_memcpy_dtoh_async", "emmy_stream_sync", "emmy_mem_alloc",
-    "emmy_mem_free", "emmy_time_launches", "emmy_run_host", "emmy_rmsnorm_noalloc",
+    "emmy_mem_free", "emmy_ipc_handle", "emmy_ipc_open", "emmy_ipc_close",
+    "emmy_time_launches", "emmy_run_host", "emmy_rmsnorm_noalloc",
 ]
 
 
@@ -118,6 +119,9 @@ def lib() -> ctypes.CDLL:
         L.emmy_stream_sync.argtypes = [ctypes.c_void_p]
         L.emmy_mem_alloc.argtypes = [ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t]
         L.emmy_mem_free.argtypes = [ctypes.c_uint64]
+        L.emmy_ipc_handle.argtypes = [ctypes.c_uint64, ctypes.c_char_p]
+        L.emmy_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)]
+        L.emmy_ipc_close.argtypes = [ctypes.c_uint64]
         L.emmy_device_count.argtypes = [ctypes.POINTER(ctypes.c_int)]
         L.emmy_device_init.argtypes = [ctypes.c_int]
         L.emmy_time_launches.argtypes = [ctypes.c_void_p, c_u32p, c_u32p, ctypes.c_uint32, c_u32p,

@@ -128,6 +128,20 @@ EMMY_API int emmy_mem_alloc(uint64_t *dptr, size_t bytes);
 EMMY_API int emmy_mem_free(uint64_t dptr);
 
 /* ------------------------------------------------------------------------ */
+/* Peer memory between the processes of one multi-GPU job (one process per   */
+/* GPU).  The reference is single-GPU and has no counterpart: these serve     */
+/* the harness's cross-GPU finish of the global sum (the host side of         */
+/* emmy_b200/peer.py), which writes each rank's partial straight into every   */
+/* peer's memory over NVLink.  `emmy_ipc_handle` exports an allocation made   */
+/* by `emmy_mem_alloc` (64 opaque bytes, exchanged by the caller);            */
+/* `emmy_ipc_open` maps a peer's allocation into this process (peer access    */
+/* enabled as needed) and `emmy_ipc_close` unmaps it.                        */
+/* ------------------------------------------------------------------------ */
+EMMY_API int emmy_ipc_handle(uint64_t dptr, unsigned char handle_out[64]);
+EMMY_API int emmy_ipc_open(const unsigned char handle[64], uint64_t *dptr_out);
+EMMY_API int emmy_ipc_close(uint64_t dptr);
+
+/* ------------------------------------------------------------------------ */
 /* Timing: the runner reports `median_us` over `iters` launches after         */
 /* `warmup` (reference docs/API.md:15-36).  This launches `iters` times       */
 /* back to back on `stream`, records a CUDA event pair around each launch,    */

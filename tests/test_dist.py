@@ -116,3 +116,44 @@ def test_shard_kwargs_cover_the_problem(world):
         kw = D.shard_kwargs(name, world - 1, world)
         g, m = synth.config(name, **kw).build()
         assert compile_graph(g, m).kind == kind, name
+
+
+def _handles(rank, world, port, q):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port),
+                       "RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank)})
+    from emmy_b200 import peer
+    D.init("gloo", D.from_env(), timeout_s=30)
+    got = peer.exchange_handles(bytes([rank + 1]) * 64, world)
+    q.put((rank, got))
+    D.barrier()
+    D.finish()
+
+
+def test_peer_handles_are_exchanged_in_rank_order():
+    """The NVLink finish of the global sum (``peer.PeerSum``) maps every
+    rank's slot array from the 64-byte handles the ranks exchange through the
+    process group: each rank receives all of them, in rank order (gloo, two
+    ranks on CPU; the mapping itself needs GPUs)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_handles, args=(r, 3, port, q)) for r in range(3)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, got in res:
+        assert got == [bytes([r + 1]) * 64 for r in range(3)]
+
+
+def test_peer_sum_kernel_assembles_and_checks(native_lib):
+    """The peer-sum kernel assembles for sm_100a and passes the static PTX
+    checks; every poll is bounded by %globaltimer and reports code 9."""
+    from emmy_b200 import native, peer, ptxcheck
+    img = native.Image(peer.PEER_SUM_PTX)
+    assert img.registers().get("emmy_peer_sum")
+    assert ptxcheck.check(peer.PEER_SUM_PTX) == []
+    assert "%globaltimer" in peer.PEER_SUM_PTX and f"], {peer.STATUS_TIMEOUT};" in peer.PEER_SUM_PTX
+    assert "multimem" not in peer.PEER_SUM_PTX and "multicast" not in peer.PEER_SUM_PTX
