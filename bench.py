@@ -24,8 +24,11 @@ configuration's tolerance; a case that fails reports no number.  After the
 headline, N=1 times every other category at its BASELINE size (``categories``,
 each with a bounded CPU baseline); N>1 times every configuration as strong
 scaling of the BASELINE problem (``shards``: rows, element chunks, CTA slices
-of the full sum finished by the all-reduce, 256-row bands of matmul,
-(batch, head) pairs of attention).
+of the full sum finished by the all-reduce -- and again by ``peer.PeerSum``,
+the same finish over NVLink peer memory without NCCL -- 256-row bands of
+matmul, (batch, head) pairs of attention).  Inputs smaller than twice the L2
+are flushed between launches (a 512 MiB write whose lines are then discarded
+from L2).
 
 ``--impl reference`` times the reference's own CPU evaluation of the same
 expressions (numpy, as in the reference's tools/harness/refs.py:41-124) on
