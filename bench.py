@@ -828,7 +828,9 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int,
         # waits for the others
         if D.max_over_ranks(0.0 if built else 1.0, device=dev) != 0.0:
             if ps is not None:
-                ps.close()
+                ps.close(barrier=D.barrier)
+            else:
+                D.barrier()
             raise RuntimeError("peer memory could not be mapped on every rank")
 
     def step():
@@ -868,7 +870,7 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int,
     if ps is not None:
         status = ps.status()
         D.barrier()                  # every rank's kernels are done before unmapping
-        ps.close()
+        ps.close(barrier=D.barrier)
     got = float(out.item())
     part = torch.tensor([float(np.sum(bufs.t["x"].cpu().numpy(), dtype=np.float64))],
                         dtype=torch.float64, device=dev)

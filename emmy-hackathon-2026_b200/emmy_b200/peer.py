@@ -183,14 +183,18 @@ class PeerSum:
         native.check(L.emmy_launch(self.kernel.h, native.u32x3((1, 1, 1)),
                                    native.u32x3((32, 1, 1)), 0, None, params, stream))
 
-    def close(self) -> None:
-        """Unmap the peers' arrays and free this rank's (every rank's kernels
-        must have completed)."""
+    def close(self, barrier=None) -> None:
+        """Unmap the peers' arrays, then free this rank's own (every rank's
+        kernels must have completed).  ``barrier`` (the process group's)
+        runs between the two, so no rank frees an array another rank still
+        has mapped."""
         L = native.lib()
         for r, q in enumerate(self.peers):
             if r != self.rank and q:
                 native.check(L.emmy_ipc_close(q))
         self.peers = []
+        if barrier is not None:
+            barrier()
         for a in ("peer_table", "local"):
             if getattr(self, a, 0):
                 native.check(L.emmy_mem_free(getattr(self, a)))

@@ -55,7 +55,7 @@ def _rank(rank, world, port, q):
     del g
     status = ps.status()
     D.barrier()
-    ps.close()
+    ps.close(barrier=D.barrier)
     q.put((rank, got, status))
     D.barrier()
     D.finish()
