@@ -140,14 +140,26 @@ class PeerSum:
         self.rank, self.world = rank, world
         self.nbytes = (2 * world + 1) * SLOT
         p = ctypes.c_uint64()
-        native.check(L.emmy_mem_alloc(ctypes.byref(p), self.nbytes))
-        self.local = p.value
-        native.check(L.emmy_memset_async(self.local, 0, self.nbytes, None))
-        native.check(L.emmy_stream_sync(None))
-        buf = ctypes.create_string_buffer(64)
-        native.check(L.emmy_ipc_handle(self.local, buf))
-        handles = exchange_handles(buf.raw, world)
+        self.local = self.peer_table = 0
         self.peers = []
+        # every rank joins the exchange, with None if its own export failed,
+        # so that all ranks fail together instead of waiting for each other
+        mine = None
+        try:
+            native.check(L.emmy_mem_alloc(ctypes.byref(p), self.nbytes))
+            self.local = p.value
+            native.check(L.emmy_memset_async(self.local, 0, self.nbytes, None))
+            native.check(L.emmy_stream_sync(None))
+            buf = ctypes.create_string_buffer(64)
+            native.check(L.emmy_ipc_handle(self.local, buf))
+            mine = buf.raw
+        except native.EmmyError:
+            pass
+        handles = exchange_handles(mine, world)
+        if any(h is None for h in handles):
+            if self.local:
+                native.check(L.emmy_mem_free(self.local))
+            raise RuntimeError("a rank could not export its peer-sum slots")
         for r, h in enumerate(handles):
             if r == rank:
                 self.peers.append(self.local)
