@@ -1047,10 +1047,21 @@ def run_problems(args) -> None:
     for folder in sorted(p for p in root.iterdir() if (p / "meta.json").exists()):
         pid = folder.name
         row = {}
-        for arm in ("ours", "reference_ptx"):
+        for arm in ("ours", "ours_generic", "reference_ptx"):
             if arm == "ours":
                 rep = problem.run_problem(folder, out=lambda s_: None, time_launches=True,
                                           iters=args.steps)
+            elif arm == "ours_generic":
+                # the same IRs forced through the statement-by-statement
+                # lowering (only where a template was selected)
+                if all(k_["kind"] == "generic" for k_ in row["ours"]["kernels"]):
+                    continue
+                os.environ["EMMY_TEMPLATE"] = "generic"
+                try:
+                    rep = problem.run_problem(folder, out=lambda s_: None, time_launches=True,
+                                              iters=args.steps)
+                finally:
+                    del os.environ["EMMY_TEMPLATE"]
             else:
                 rdir = REPO / "oracle" / "_ref" / "problems" / pid
                 if not rdir.exists():

@@ -188,14 +188,35 @@ class GenericLowering:
             k(f"setp.ge.u64 {p}, {gid64}, {ncells};")
             k(f"@{p} bra {done};")
         self.gid64 = gid64
-        self.decode(tile, gid64, extents)
+        cell = gid64
+        if ctx.total_threads < 2 ** 31:
+            # every cell id fits in 32 bits: decode with 32-bit integer ops
+            # (a 64-bit divide or remainder is a long emulated sequence)
+            cell = k.reg("r")
+            k(f"cvt.u32.u64 {cell}, {gid64};")
+        self.decode(tile, cell, extents)
         self.body(tile.body)
         k.mark(done)
 
     def decode(self, tile, gid64, extents):
         """Row-major decode of the flat cell id over the Tile axes, with
-        Emmy's grouped rasterisation of two adjacent block axes."""
+        Emmy's grouped rasterisation of two adjacent block axes.  ``gid64``
+        is a 64-bit register, or a 32-bit one when every cell id fits
+        (then power-of-two strides and extents decode by shift and mask)."""
         k = self.k
+        wide = gid64.startswith("%rd")
+
+        def divide(dst, src, d):
+            if not wide and d & (d - 1) == 0:
+                k(f"shr.u32 {dst}, {src}, {d.bit_length() - 1};")
+            else:
+                k(f"div.u{64 if wide else 32} {dst}, {src}, {d};")
+
+        def modulo(dst, src, d):
+            if not wide and d & (d - 1) == 0:
+                k(f"and.b32 {dst}, {src}, {d - 1};")
+            else:
+                k(f"rem.u{64 if wide else 32} {dst}, {src}, {d};")
         strides = [1] * len(extents)
         acc = 1
         for i in range(len(extents) - 1, -1, -1):
@@ -215,26 +236,32 @@ class GenericLowering:
             if extents[i] == 1:
                 self.ints[name] = "0"
                 continue
-            q = k.reg("rd")
+            q = k.reg("rd" if wide else "r")
             if strides[i] != 1:
-                k(f"div.u64 {q}, {gid64}, {strides[i]};")
+                divide(q, gid64, strides[i])
             else:
-                k(f"mov.u64 {q}, {gid64};")
+                k(f"mov.{'u64' if wide else 'u32'} {q}, {gid64};")
             if i != 0:
-                k(f"rem.u64 {q}, {q}, {extents[i]};")
-            r = k.reg("r")
-            k(f"cvt.u32.u64 {r}, {q};")
+                modulo(q, q, extents[i])
+            if wide:
+                r = k.reg("r")
+                k(f"cvt.u32.u64 {r}, {q};")
+            else:
+                r = q
             self.ints[name] = r
         if raster is not None:
             gi, oi, g = raster
             mi, ni = min(gi, oi), max(gi, oi)
             ea, eb = extents[gi], extents[oi]
-            sub = k.reg("rd")
-            k(f"div.u64 {sub}, {gid64}, {strides[ni]};")
+            sub = k.reg("rd" if wide else "r")
+            divide(sub, gid64, strides[ni])
             if mi != 0:
-                k(f"rem.u64 {sub}, {sub}, {ea * eb};")
-            s32 = k.reg("r")
-            k(f"cvt.u32.u64 {s32}, {sub};")
+                modulo(sub, sub, ea * eb)
+            if wide:
+                s32 = k.reg("r")
+                k(f"cvt.u32.u64 {s32}, {sub};")
+            else:
+                s32 = sub
             grp = k.reg("r")
             k(f"div.u32 {grp}, {s32}, {g * eb};")
             rem = k.reg("r")

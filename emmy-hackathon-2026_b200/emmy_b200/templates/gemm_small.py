@@ -285,6 +285,14 @@ class Stager:
 
 class GemmSmallTemplate:
     name = "gemm"
+    # a CTA whose threads own fewer multiply-adds than this each runs
+    # faster through the generic lowering (FFMA): the tensor-memory
+    # allocation, barriers and staging outweigh the products.  Measured on
+    # Emmy's own matmul IRs (per-thread multiply-adds: this template /
+    # generic, us): m02 16: 12.3 / 6.2, mm256 48: 31.2 / 10.8, mm64a 64:
+    # 8.7 / 6.7, mm_rect2 64: 8.6 / 6.7, mm128 1536: 10.8 / 8.7, m01 and
+    # mm512 2048: 21.0 / 98.8
+    MIN_MACS_PER_THREAD = 2048
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -461,6 +469,10 @@ class GemmSmallTemplate:
         warps = T // 32
         if BM > 128 or BM > 32 * min(4, warps) or BN > 256:
             raise TemplateMismatch(f"tile {BM}x{BN} too large for {T} threads")
+        if BM * BN * KC < cls.MIN_MACS_PER_THREAD * T:
+            raise TemplateMismatch(f"{BM}x{BN}x{KC} per CTA is {BM * BN * KC // T} multiply-adds "
+                                   f"a thread: below {cls.MIN_MACS_PER_THREAD}, the generic "
+                                   f"lowering is faster")
         self = cls()
         self.ctx, self.A, self.B, self.C = ctx, A, B, C
         self.M, self.N, self.K, self.KC = M, N, K, KC

@@ -416,6 +416,23 @@ def test_tf32_split_with_raw_high_part():
     assert "and.b32" in ptx and "-8192" in ptx
 
 
+def test_small_matmuls_with_little_work_a_thread_stay_generic():
+    """Emmy's own matmul IRs whose CTAs give each thread fewer than
+    ``GemmSmallTemplate.MIN_MACS_PER_THREAD`` multiply-adds (m02: 16, corpus
+    mm256: 48, mm64a and mm_rect2: 64, mm128: 1536) lower through the generic
+    path, which times faster there; m01 and mm512 (2048) take tcgen05."""
+    from conftest import GOLDEN
+    want = {("problems", "m01_matmul_512"): "gemm", ("problems", "m02_matmul_rect"): "generic",
+            ("corpus", "mm128"): "generic", ("corpus", "mm256"): "generic",
+            ("corpus", "mm512"): "gemm", ("corpus", "mm64a"): "generic",
+            ("corpus", "mm_rect2"): "generic"}
+    for (sub, name), kind_ in want.items():
+        f = GOLDEN / sub / name
+        c = compile_graph(json.loads((f / "kernel.ir.json").read_text()),
+                          json.loads((f / "meta.json").read_text()))
+        assert c.kind == kind_, (name, c.kind, c.rejections)
+
+
 def test_meta_only_gemm_takes_only_meta_parameters(monkeypatch):
     """Emmy's own matmul IRs (m01, m02, corpus mm*) compile to the tcgen05
     kernel whose parameters are exactly meta ``arg_order`` (no tensor-map
@@ -428,6 +445,8 @@ def test_meta_only_gemm_takes_only_meta_parameters(monkeypatch):
         [GOLDEN / "corpus" / n for n in ("mm128", "mm256", "mm512", "mm64a", "mm_rect2")]
     cases = [(json.loads((f / "kernel.ir.json").read_text()),
               json.loads((f / "meta.json").read_text())) for f in folders]
+    from emmy_b200.templates.gemm_small import GemmSmallTemplate
+    monkeypatch.setattr(GemmSmallTemplate, "MIN_MACS_PER_THREAD", 0)   # every IR on tcgen05
     monkeypatch.setenv("EMMY_META_ONLY", "1")
     cases += [synth.config(n).build() for n in ("matmul_bf16", "matmul_f32")]
     for g, m in cases:

@@ -39,8 +39,12 @@ def _status(kern):
 
 
 @pytest.mark.parametrize("folder", EMMY_MATMULS, ids=lambda p: p.name)
-def test_emmy_matmul_irs_on_tensor_cores(folder):
+def test_emmy_matmul_irs_on_tensor_cores(folder, monkeypatch):
     from emmy_b200 import harness
+    from emmy_b200.templates.gemm_small import GemmSmallTemplate
+    # the tcgen05 form also for the IRs whose little work a thread the
+    # selection sends to the generic lowering
+    monkeypatch.setattr(GemmSmallTemplate, "MIN_MACS_PER_THREAD", 0)
     g = json.loads((folder / "kernel.ir.json").read_text())
     meta = json.loads((folder / "meta.json").read_text())
     outs, kern = harness.run(g, meta, folder=folder)
