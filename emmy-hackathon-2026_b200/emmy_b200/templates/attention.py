@@ -1333,7 +1333,9 @@ class AttentionTemplate:
         m = max(m_a, m_b), f = 2^(m_x - m), l = l_a f_a + l_b f_b,
         O = (O_a f_a + O_b f_b) / l -- a product per side and one add, so
         the result does not depend on which CTA merges.  No thread waits for
-        the other CTA: the later one merges, whichever it is."""
+        the other CTA: the later one merges, whichever it is.  The scratch
+        and the counters belong to the module, so two launches of one module
+        must not overlap in time (launches on one stream never do)."""
         D = self.D
         W, _, RU, _ = self.sched
         PER = 256 * (D + 2) * 4                 # bytes per (unit, key half)
