@@ -41,6 +41,9 @@ PERSISTENT_MIN_STAGES = 4    # 4 x 32 KiB ring: one CTA per SM
 EPI_CHUNK = 16               # accumulator columns per tcgen05.ld in the epilogue
 GROUP_M = 16                 # 256-row bands per raster group (tiles run down a group's bands)
 TAIL_SPLIT = True            # leftover pair tiles of a partial last round run as 256 x 128 halves
+# 3xTF32: the A operand's raw (high) and low parts in tensor memory instead of
+# shared memory (tcgen05.mma's [a-tmem] form), one accumulator instead of two
+TF32_A_TMEM = False
 
 
 def schedule(tiles: int, workers: int = WORKERS):
@@ -140,6 +143,11 @@ def emit_pair_persistent(t) -> str:
     BOXN = 128 // es                 # B boxes are 128 bytes wide
     KMMA = 32 // es                  # K per tcgen05.mma
     CONVW = 6 if tf32 else 0         # 3xTF32 converter warps: 2..7
+    # A in tensor memory (3xTF32): one 256-column accumulator, then per ring
+    # stage the A rows' raw values (BK columns) and their low parts (BK more)
+    ATM = tf32 and TF32_A_TMEM and BN + S * 2 * BK <= 512
+    NACC = 1 if ATM else 2
+    ABASE = NACC * BN
     NB = t.NB                        # 256-column tiles per row band
     MB = t.M // 256                  # 256-row bands
     TILES = MB * NB                  # pair tiles
@@ -216,7 +224,7 @@ def emit_pair_persistent(t) -> str:
         k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 1;")
     for s in range(2 * S, NBAR):               # conv[s]: the converter warps of 2 CTAs
         k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], {2 * CONVW};")
-    for b in range(2):
+    for b in range(NACC):
         k(f"mbarrier.init.shared::cta.b64 [{accb}+{8 * b}], 1;")
         k(f"mbarrier.init.shared::cta.b64 [{acce}+{8 * b}], 8;")
     k("fence.mbarrier_init.release.cluster;")
@@ -380,10 +388,14 @@ def emit_pair_persistent(t) -> str:
     else:
         k(f"mov.u32 {idesc}, {idesc_full};")
     buf = k.reg("r")
-    k(f"and.b32 {buf}, {it}, 1;")
     aph = k.reg("r")                              # use count of this buffer, parity
-    k(f"shr.u32 {aph}, {it}, 1;")
-    k(f"and.b32 {aph}, {aph}, 1;")
+    if ATM:                                       # one accumulator: tile i is use i
+        k(f"mov.u32 {buf}, 0;")
+        k(f"and.b32 {aph}, {it}, 1;")
+    else:
+        k(f"and.b32 {buf}, {it}, 1;")
+        k(f"shr.u32 {aph}, {it}, 1;")
+        k(f"and.b32 {aph}, {aph}, 1;")
     k(f"xor.b32 {aph}, {aph}, 1;")
     ae = k.reg("r")
     k(f"mad.lo.u32 {ae}, {buf}, 8, {acce};")
@@ -411,6 +423,10 @@ def emit_pair_persistent(t) -> str:
         k(f"add.u32 {lbd}, {sb}, {RAW + SA};")
         ldesc_a = GemmTemplate._desc(k, lad, hiA)
         ldesc_b = GemmTemplate._desc(k, lbd, hiB)
+    if ATM:
+        ahi = k.reg("r")                          # this stage's A columns in TMEM
+        k(f"mad.lo.u32 {ahi}, {st}, {2 * BK}, {tmem};")
+        k(f"add.u32 {ahi}, {ahi}, {ABASE};")
     pacc = k.reg("p")
     k(f"setp.ne.u32 {pacc}, {kt}, 0;")
     ptrue = k.reg("p")
@@ -422,12 +438,20 @@ def emit_pair_persistent(t) -> str:
         pairs = [(adesc, bdesc)]
         if tf32:                          # small terms first: lo*hi + hi*lo, then hi*hi
             pairs = [(ldesc_a, bdesc), (adesc, ldesc_b), (adesc, bdesc)]
+        if ATM:                           # A from TMEM: KMMA columns a step, low parts BK on
+            pairs = [(("t", BK), bdesc), (("t", 0), ldesc_b), (("t", 0), bdesc)]
         for da_, db_ in pairs:
-            ad = k.reg("rd")
-            k(f"add.s64 {ad}, {da_}, {ao};")
             bd = k.reg("rd")
             k(f"add.s64 {bd}, {db_}, {bo};")
-            k(f"tcgen05.mma.cta_group::2.kind::{kind_} [{dacc}], {ad}, {bd}, {idesc}, "
+            if isinstance(da_, tuple):
+                at = k.reg("r")
+                k(f"add.u32 {at}, {ahi}, {da_[1] + kk * KMMA};")
+                aop = f"[{at}]"
+            else:
+                ad = k.reg("rd")
+                k(f"add.s64 {ad}, {da_}, {ao};")
+                aop = ad
+            k(f"tcgen05.mma.cta_group::2.kind::{kind_} [{dacc}], {aop}, {bd}, {idesc}, "
               f"{pacc if first else ptrue};")
             first = False
     k(f"tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
@@ -457,10 +481,14 @@ def emit_pair_persistent(t) -> str:
 
     def epilogue(idx):
         ebuf = k.reg("r")
-        k(f"and.b32 {ebuf}, {idx}, 1;")
         eph = k.reg("r")
-        k(f"shr.u32 {eph}, {idx}, 1;")
-        k(f"and.b32 {eph}, {eph}, 1;")
+        if ATM:
+            k(f"mov.u32 {ebuf}, 0;")
+            k(f"and.b32 {eph}, {idx}, 1;")
+        else:
+            k(f"and.b32 {ebuf}, {idx}, 1;")
+            k(f"shr.u32 {eph}, {idx}, 1;")
+            k(f"and.b32 {eph}, {eph}, 1;")
         eaf = k.reg("r")
         k(f"mad.lo.u32 {eaf}, {ebuf}, 8, {accb};")
         GemmTemplate._wait(k, eaf, eph, status, 3, teardown)
@@ -500,10 +528,127 @@ def emit_pair_persistent(t) -> str:
         k(f"mad.lo.u32 {eae}, {ebuf}, 8, {lead_ae};")
         k(f"@{pl0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{eae}];")
 
+    def emit_tf32_atm_converters():
+        """3xTF32 with A in tensor memory.  Warps 4-7: per stage, thread r
+        (row r of this CTA's A rows, its TMEM lane) reads the row's BK raw
+        values from the swizzled stage and stores them and their low parts
+        into the stage's TMEM columns; before converting tile i they drain
+        tile i-1 (one accumulator: tile i's MMAs wait for it).  Warps 2-3:
+        the low parts of this CTA's B half, into shared memory as before.
+        Every converter warp arrives once a stage on the leader's conv
+        barrier."""
+        lead_conv = k.reg("r")                    # conv[0] of the leader
+        k(f"add.u32 {lead_conv}, {bars}, {16 * S};")
+        k(f"mapa.shared::cluster.u32 {lead_conv}, {lead_conv}, 0;")
+        ntp1 = k.reg("r")
+        k(f"add.u32 {ntp1}, {ntile}, 1;")
+        b_part = k.label("B_CONV")
+        k(f"@!{pepi} bra {b_part};")
+        # ---- warps 4-7: A rows into TMEM, drains
+        r_ = k.reg("r")
+        k(f"mad.lo.u32 {r_}, {q}, 32, {lane};")   # this thread's A row (its TMEM lane)
+        rsw = k.reg("r")
+        k(f"and.b32 {rsw}, {r_}, 7;")
+        roff = k.reg("r")
+        k(f"shl.b32 {roff}, {r_}, 7;")            # 128 bytes a row
+        ctl = k.reg("r")                          # this warp's TMEM lanes, A columns
+        k(f"shl.b32 {ctl}, {q}, 21;")
+        k(f"add.u32 {ctl}, {ctl}, {tmem};")
+        k(f"add.u32 {ctl}, {ctl}, {ABASE};")
+        chunk = []                                # byte offset of K chunk c in the row
+        for c in range(BK * 4 // 16):
+            o = k.reg("r")
+            k(f"xor.b32 {o}, {rsw}, {c};")
+            k(f"shl.b32 {o}, {o}, 4;")
+            k(f"add.u32 {o}, {o}, {roff};")
+            chunk.append(o)
+        k(f"mov.u32 {st}, 0;")
+        k(f"mov.u32 {ph}, 0;")
+        atop = tile_loop_head("ATILE")
+        pd = k.reg("p")
+        k(f"setp.ne.u32 {pd}, {it}, 0;")
+        no_drain = k.label("A_NO_DRAIN")
+        k(f"@!{pd} bra {no_drain};")
+        prev = k.reg("r")
+        k(f"sub.u32 {prev}, {it}, 1;")
+        epilogue(prev)
+        k.mark(no_drain)
+        pc = k.reg("p")
+        k(f"setp.lt.u32 {pc}, {it}, {ntile};")
+        a_skip = k.label("A_SKIP")
+        k(f"@!{pc} bra {a_skip};")
+        k(f"mov.u32 {kt}, 0;")
+        ak = k.label("AK")
+        k.mark(ak)
+        GemmTemplate._wait(k, bar_addr(0, st), ph, status, 4, teardown)
+        # the stage's TMEM columns were last read by MMAs that completed
+        # before this stage's copies were issued
+        k("tcgen05.fence::after_thread_sync;")
+        sba = stage_base(st)
+        hi = []
+        for c in range(BK * 4 // 16):
+            x = k.regs("r", 4)
+            ad = k.reg("r")
+            k(f"add.u32 {ad}, {sba}, {chunk[c]};")
+            k(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{ad}];")
+            hi += x
+        lo = []
+        for c in range(0, BK, 4):
+            lo += tf32_lo_trunc(k, hi[c:c + 4])
+        tcol = k.reg("r")
+        k(f"mad.lo.u32 {tcol}, {st}, {2 * BK}, {ctl};")
+        k(f"tcgen05.st.sync.aligned.32x32b.x{BK}.b32 [{tcol}], {{{', '.join(hi)}}};")
+        k(f"tcgen05.st.sync.aligned.32x32b.x{BK}.b32 [{tcol}+{BK}], {{{', '.join(lo)}}};")
+        k("tcgen05.wait::st.sync.aligned;")
+        k("tcgen05.fence::before_thread_sync;")
+        k("bar.warp.sync 0xffffffff;")
+        cv = k.reg("r")
+        k(f"mad.lo.u32 {cv}, {st}, 8, {lead_conv};")
+        k(f"@{pl0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{cv}];")
+        k_loop_tail(ak)
+        k.mark(a_skip)
+        tile_loop_tail(atop, ntp1)
+        k(f"bra {teardown};")
+        # ---- warps 2-3: low parts of this CTA's B half into shared memory
+        k.mark(b_part)
+        CTB = 64
+        btid = k.reg("r")
+        k(f"sub.u32 {btid}, {tid}, 64;")          # warps 2-3: threads 0..63
+        boff = k.reg("r")
+        k(f"shl.b32 {boff}, {btid}, 4;")
+        NVB = SBH // 16
+        assert NVB % CTB == 0
+        k(f"mov.u32 {st}, 0;")
+        k(f"mov.u32 {ph}, 0;")
+        btop = tile_loop_head("BTILE")
+        k(f"mov.u32 {kt}, 0;")
+        bk = k.label("BK")
+        k.mark(bk)
+        GemmTemplate._wait(k, bar_addr(0, st), ph, status, 4, teardown)
+        sbb = stage_base(st)
+        b0 = k.reg("r")
+        k(f"add.u32 {b0}, {sbb}, {SA};")
+        k(f"add.u32 {b0}, {b0}, {boff};")
+        for i in range(NVB // CTB):
+            x = k.regs("r", 4)
+            ad = f"{b0}+{i * 16 * CTB}" if i else b0
+            k(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{ad}];")
+            lo = tf32_lo_trunc(k, x)
+            k(f"st.shared.v4.b32 [{b0}+{RAW + i * 16 * CTB}], {{{', '.join(lo)}}};")
+        k("fence.proxy.async.shared::cta;")
+        k("bar.warp.sync 0xffffffff;")
+        cvb = k.reg("r")
+        k(f"mad.lo.u32 {cvb}, {st}, 8, {lead_conv};")
+        k(f"@{pl0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{cvb}];")
+        k_loop_tail(bk)
+        tile_loop_tail(btop)
+
     if not tf32:
         etop = tile_loop_head("ETILE")
         epilogue(it)
         tile_loop_tail(etop)
+    elif ATM:
+        emit_tf32_atm_converters()
     else:
         # iteration i converts tile i's k-slices (i < ntile), then drains tile
         # i-1 (i >= 1): the drain overlaps the MMAs of tile i's last stages

@@ -178,3 +178,27 @@ def test_gemm_f32_3xtf32_error_against_float64():
     nrm = np.linalg.norm(ref)
     assert np.linalg.norm(got - ref) / nrm < 1e-4
     assert abs(float((got - ref).mean())) * 1024 / nrm < 1e-6
+
+
+@pytest.mark.parametrize("kw", F32_PERSISTENT_CASES,
+                         ids=[f"{c['M']}x{c['N']}x{c['K']}" for c in F32_PERSISTENT_CASES])
+def test_gemm_f32_persistent_pairs_a_in_tmem(kw, monkeypatch):
+    """3xTF32 with the A operand in tensor memory (``TF32_A_TMEM``): warps
+    4-7 store each A row's raw values and low parts into the stage's TMEM
+    columns, the MMAs read A there (``[a-tmem]``) and B from shared memory,
+    one accumulator (each tile drained before the next one's MMAs).  The
+    same bounds as the shared-memory form."""
+    from emmy_b200 import compiler
+    from emmy_b200.templates import gemm_persistent
+    monkeypatch.setattr(gemm_persistent, "TF32_A_TMEM", True)
+    p = synth.config("matmul_f32", **kw)
+    g, m = p.build()
+    ptx = compiler.compile_graph(g, m).render()
+    import re
+    assert "persistent CTA pairs" in ptx
+    assert re.search(r"kind::tf32 \[%r\d+\], \[%r\d+\]", ptx)     # A from tensor memory
+    rows = None
+    if kw["M"] >= 4096:
+        rows = np.sort(np.random.default_rng(9).choice(kw["M"], 64, replace=False))
+    got, ref = _run(p, rows=rows)
+    assert np.max(np.abs(got - ref)) <= 2e-5 * max(1.0, float(np.max(np.abs(ref))))
