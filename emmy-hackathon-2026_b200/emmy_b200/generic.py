@@ -34,6 +34,8 @@ import struct
 from math import prod
 
 from .analysis import kind, walk
+from .fragments import FragmentLowering
+from .wgmma import WgmmaLowering
 from .ir import dim
 from .ops import LN2, UnsupportedOp, emit_exp, emit_op_f32, identity_f32
 from .ptx import PARAM_TYPES, Kernel, f32_hex, f64_hex
@@ -75,7 +77,7 @@ def _calc_ty(ty: str) -> str:
     return ty
 
 
-class GenericLowering:
+class GenericLowering(FragmentLowering, WgmmaLowering):
     name = "generic"
 
     def __init__(self, ctx):
@@ -194,9 +196,11 @@ class GenericLowering:
             # (a 64-bit divide or remainder is a long emulated sequence)
             cell = k.reg("r")
             k(f"cvt.u32.u64 {cell}, {gid64};")
+        self._wg_begin(tile)
         self.decode(tile, cell, extents)
         self.body(tile.body)
         k.mark(done)
+        self._wg_end()
 
     def decode(self, tile, gid64, extents):
         """Row-major decode of the flat cell id over the Tile axes, with
@@ -956,6 +960,10 @@ class GenericLowering:
 
     def s_Sync(self, s):
         bid = int(s.barrier_id or 0)
+        if self._wg is not None and not s.warp:
+            # threads' shared-memory writes become visible to the tensor
+            # core's async proxy before the barrier orders them
+            self.k("fence.proxy.async.shared::cta;")
         if s.warp:
             self.k("bar.warp.sync 0xffffffff;")
         elif bid:
@@ -1287,6 +1295,13 @@ class GenericLowering:
             k(f"mov.u32 {par}, {int(ph) & 1};")
         else:
             k(f"and.b32 {par}, {ph}, 1;")
+        self.bounded_parity_wait(a, par)
+
+    def bounded_parity_wait(self, a, par):
+        """Wait until the mbarrier at shared address ``a`` completes the phase
+        of parity ``par``, for at most ``WAIT_NS`` of %globaltimer; on expiry
+        record status 8 in ``__emmy_status`` and go on."""
+        k = self.k
         p = k.reg("p")
         top, ok = k.label("MBAR_WAIT"), k.label("MBAR_OK")
         k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{a}], {par};")

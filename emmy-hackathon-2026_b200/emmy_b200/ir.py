@@ -31,6 +31,7 @@ from typing import Any
 _EXPR_MODULE = "emmy.compiler.ir.expr"
 _STMT_MODULE = "emmy.compiler.ir.stmt"
 _TYPE_MODULE = "emmy.compiler.ir.types"
+_FRAG_MODULE = "emmy.compiler.ir.fragment"
 
 # name -> (module, fields).  Field order follows the keyword order Emmy's
 # dataclass reprs print, which is the declaration order.
@@ -83,6 +84,37 @@ _SCHEMA: dict[str, tuple[str, tuple[str, ...]]] = {
     "MbarrierArrive": (_STMT_MODULE, ("mbar", "slot")),
     "MbarrierWait": (_STMT_MODULE, ("mbar", "phase", "slot")),
     "SetMaxNReg": (_STMT_MODULE, ("count", "direction")),
+    # tensor core through register fragments (mma.sync), TASK.md "Tensor core:
+    # register fragments"; Lambda and FragLayout are the helper records those
+    # statements carry
+    "RegFragment": (_STMT_MODULE, ("name", "role", "shape", "dtype", "count", "nregs")),
+    "LdmatrixLoad": (_STMT_MODULE, ("frag", "src_buffer", "src_index", "role", "ldm", "swizzle",
+                                    "staged", "gmem_guard", "k_zero", "b_trans", "pair_frag",
+                                    "byte_slab", "scale_buffer", "scale_index", "scale_ldm",
+                                    "fragment_layout", "fragment_index")),
+    "BlockScaleLoad": (_STMT_MODULE, ("frag", "src_buffer", "src_index", "role", "ldm")),
+    "MmaSyncPtx": (_STMT_MODULE, ("c_frag", "a_frag", "b_frag", "shape", "ab_dtype", "c_dtype",
+                                  "b_row_major", "sfa_frag", "sfb_frag")),
+    "FragmentPromote": (_STMT_MODULE, ("dst", "src")),
+    "FragmentApply": (_STMT_MODULE, ("out", "op", "args", "kinds", "in_place", "layout", "post",
+                                     "row_base", "col_base")),
+    "FragmentRowReduce": (_STMT_MODULE, ("top", "bot", "frags", "op", "layout", "dtype")),
+    "FragmentRepack": (_STMT_MODULE, ("frag", "srcs", "ab_dtype", "fragment_layout", "part")),
+    "RegStore": (_STMT_MODULE, ("dst_buffer", "dst_index", "frag", "shape", "ldm", "epilogue",
+                                "extra_frags", "m_guard", "n_guard", "atomic", "fragment_layout",
+                                "volta_interleaved", "fragment_index", "swizzle", "row_dim",
+                                "col_dim")),
+    "Lambda": (_FRAG_MODULE, ("params", "body", "results")),
+    "FragLayout": (_FRAG_MODULE, ("n_elems", "elem_row", "reduce_xors", "lane_decl", "lane_names",
+                                  "row_off", "col_off")),
+    # tensor core through warpgroups (wgmma), TASK.md "Tensor core: warp groups"
+    "WgmmaDescriptor": (_STMT_MODULE, ("name", "smem", "smem_index", "swizzle", "lbo_bytes",
+                                       "sbo_bytes")),
+    "WgmmaMma": (_STMT_MODULE, ("c_frags", "b_desc", "shape", "ab_dtype", "a_desc", "a_frag",
+                                "scale_d", "trans_a", "trans_b")),
+    "WgmmaFence": (_STMT_MODULE, ()),
+    "WgmmaCommit": (_STMT_MODULE, ()),
+    "WgmmaWait": (_STMT_MODULE, ("group",)),
 }
 
 _DEFAULTS: dict[str, dict[str, Any]] = {
@@ -101,6 +133,27 @@ _DEFAULTS: dict[str, dict[str, Any]] = {
     "CpAsyncCopy": {"swizzle": None, "lane_index": None, "lane_rows": None},
     "CpAsyncWait": {"group": 0},
     "Window": {"base": None, "bound": None, "partition": False},
+    "RegFragment": {"count": 1, "nregs": None},
+    "LdmatrixLoad": {"role": None, "ldm": None, "swizzle": None, "staged": False,
+                     "gmem_guard": None, "k_zero": None, "b_trans": False, "pair_frag": None,
+                     "byte_slab": None, "scale_buffer": None, "scale_index": None,
+                     "scale_ldm": None, "fragment_layout": None, "fragment_index": None},
+    "BlockScaleLoad": {"ldm": None},
+    "MmaSyncPtx": {"shape": None, "ab_dtype": None, "c_dtype": None, "b_row_major": False,
+                   "sfa_frag": None, "sfb_frag": None},
+    "FragmentApply": {"kinds": (), "in_place": True, "layout": None, "post": None,
+                      "row_base": None, "col_base": None},
+    "FragmentRowReduce": {"layout": None, "dtype": None},
+    "FragmentRepack": {"ab_dtype": None, "fragment_layout": None, "part": 0},
+    "RegStore": {"shape": None, "ldm": None, "epilogue": None, "extra_frags": (), "m_guard": None,
+                 "n_guard": None, "atomic": False, "fragment_layout": None,
+                 "volta_interleaved": False, "fragment_index": None, "swizzle": None,
+                 "row_dim": None, "col_dim": None},
+    "FragLayout": {"reduce_xors": (1, 2), "lane_decl": (), "lane_names": ()},
+    "WgmmaDescriptor": {"swizzle": "NONE", "lbo_bytes": 0, "sbo_bytes": 0},
+    "WgmmaMma": {"ab_dtype": None, "a_desc": None, "a_frag": None, "scale_d": 1, "trans_a": 0,
+                 "trans_b": 0},
+    "WgmmaWait": {"group": 0},
 }
 
 

@@ -875,3 +875,331 @@ def zero_prologue(words: int = 100_000, n: int = 4096, block: int = 128) -> Prob
     p.rtol, p.atol = 0, 0
     p.oracle = {"family": "zero_prologue", "args": {"x": "x"}, "output": "acc", "words": words}
     return p
+
+
+# --------------------------------------------------------------------------
+# the register-fragment tensor-core statements (mma.sync), written in the
+# forms emmy_b200.fragments documents
+# --------------------------------------------------------------------------
+
+F16 = I.data_type("f16")
+
+
+def _idiv(a, b):
+    return I.BinaryExpr("/", a, Lit(b))
+
+
+def _imod(a, b):
+    return I.BinaryExpr("%", a, Lit(b))
+
+
+def _and(a, b):
+    return I.BinaryExpr("&&", a, b)
+
+
+def mma_matmul(M: int = 200, N: int = 136, K: int = 80, dtype: str = "bf16",
+               b_kn: bool = True, stage: bool = True, promote: bool = False,
+               epilogue: bool = False, out_dtype: str = "f32", split_k: int = 1) -> Problem:
+    """C = A . B through register fragments: CTAs of 128 threads own 64 x 64
+    tiles of C, each warp a 32 x 32 quarter as 2 x 4 mma.sync atoms.
+
+    ``dtype`` bf16 / f16 (m16n8k16) or tf32 (f32 inputs, m16n8k8); ``b_kn``:
+    B is given [K, N] (fragments loaded transposed) or as Bt [N, K];
+    ``stage``: 64 x 32 slabs of A and B staged in shared memory by the
+    CTA's threads (ldmatrix for 16-bit operands), else fragments loaded
+    straight from global memory with row / column and K guards;
+    ``promote``: f16 products accumulated in f16 fragments, added into the
+    f32 accumulators after every slab; ``epilogue``: C = relu(A.B + bias[col])
+    through the store's Lambda; ``out_dtype`` f32 or bf16; ``split_k`` > 1:
+    that many CTAs per tile, each over a K range, adding atomically into a
+    zeroed C."""
+    wide = dtype in ("bf16", "f16")
+    in_dt = {"bf16": BF16, "f16": F16, "tf32": F32}[dtype]
+    in_name = {"bf16": "bf16", "f16": "f16", "tf32": "f32"}[dtype]
+    shape = "m16n8k16" if wide else "m16n8k8"
+    KK = 16 if wide else 8
+    BK, MI, NJ = 32, 2, 4
+    pad = 8 if wide else 4
+    smem_ty = {"bf16": "bfloat16", "f16": "half", "tf32": "float"}[dtype]
+    kper = -(-K // split_k)
+    nk = -(-kper // BK)
+    p = Problem(f"mma_matmul_{dtype}_{M}x{N}x{K}", "a @ b", "k_mma_matmul", "c")
+    p.add_input("a", (M, K), in_name)
+    p.add_input("b", (K, N) if b_kn else (N, K), in_name)
+    if epilogue:
+        p.add_input("bias", (N,))
+    p.out = ("c", (M, N), out_dtype)
+    t = V("t")
+    body = [I.Let("w", _idiv(t, 32), I.data_type("i32")),
+            I.Let("wm", _idiv(V("w"), 2), I.data_type("i32")),
+            I.Let("wn", _imod(V("w"), 2), I.data_type("i32")),
+            I.Let("rowbase", add(mul(V("bm"), Lit(64)), mul(V("wm"), Lit(32))), I.data_type("i32")),
+            I.Let("colbase", add(mul(V("bn"), Lit(64)), mul(V("wn"), Lit(32))), I.data_type("i32")),
+            I.Let("kend", I.BinaryExpr("min", add(mul(V("ks"), Lit(kper)), Lit(kper)), Lit(K)),
+                  I.data_type("i32")),
+            I.Let("zero", Lit(0.0), F32),
+            I.RegFragment("acc", "c", shape, F32, MI * NJ, 4),
+            I.RegFragment("fa", "a", shape, dtype, MI, 4 if (wide or KK == 8) else 2),
+            I.RegFragment("fb", "b", shape, dtype, NJ, 2)]
+    if promote:
+        body.append(I.RegFragment("acch", "c", shape, F16, MI * NJ, 2))
+    acc = "acch" if promote else "acc"
+    if stage:
+        body += [I.Smem("As", (64, BK + pad), smem_ty, 128),
+                 I.Smem("Bs", (BK, 64 + pad) if b_kn else (64, BK + pad), smem_ty, 128)]
+    slab = [I.Let("k0", add(mul(V("ks"), Lit(kper)), mul(V("kt"), Lit(BK))), I.data_type("i32"))]
+    if stage:
+        def stage_copy(dst, src, rows, cols, src_r, src_c, rbound, cbound):
+            r, c = _idiv(V("e"), cols), _imod(V("e"), cols)
+            ok = _and(I.BinaryExpr("<", src_r(r), rbound), I.BinaryExpr("<", src_c(c), cbound))
+            return strided(axis("e", rows * cols), t, 128, [
+                I.Cond(ok, (load("v", src, src_r(r), src_c(c), dtype=in_dt),
+                            write(dst, (r, c), ("v",))),
+                       (write(dst, (r, c), ("zero",)),))])
+        slab.append(stage_copy("As", "a", 64, BK, lambda r: add(mul(V("bm"), Lit(64)), r),
+                               lambda c: add(V("k0"), c), Lit(M), V("kend")))
+        if b_kn:
+            slab.append(stage_copy("Bs", "b", BK, 64, lambda r: add(V("k0"), r),
+                                   lambda c: add(mul(V("bn"), Lit(64)), c), V("kend"), Lit(N)))
+        else:
+            slab.append(stage_copy("Bs", "b", 64, BK, lambda r: add(mul(V("bn"), Lit(64)), r),
+                                   lambda c: add(V("k0"), c), Lit(N), V("kend")))
+        slab.append(I.Sync(0, None, False))
+    for kk in range(BK // KK):
+        for i in range(MI):
+            if stage:
+                slab.append(I.LdmatrixLoad(f"fa[{i}]", "As", (add(mul(V("wm"), Lit(32)), Lit(16 * i)),
+                                                           Lit(kk * KK)), "a", BK + pad))
+            else:
+                slab.append(I.LdmatrixLoad(f"fa[{i}]", "a", (add(V("rowbase"), Lit(16 * i)),
+                                                          add(V("k0"), Lit(kk * KK))), "a",
+                                           gmem_guard=(Lit(M), None), k_zero=V("kend")))
+        for j in range(NJ):
+            if stage:
+                n_off = add(mul(V("wn"), Lit(32)), Lit(8 * j))
+                idx = (Lit(kk * KK), n_off) if b_kn else (n_off, Lit(kk * KK))
+                slab.append(I.LdmatrixLoad(f"fb[{j}]", "Bs", idx, "b",
+                                           (64 + pad) if b_kn else (BK + pad), b_trans=b_kn))
+            else:
+                n_abs = add(V("colbase"), Lit(8 * j))
+                k_abs = add(V("k0"), Lit(kk * KK))
+                idx = (k_abs, n_abs) if b_kn else (n_abs, k_abs)
+                guard = (None, Lit(N)) if b_kn else (Lit(N), None)
+                slab.append(I.LdmatrixLoad(f"fb[{j}]", "b", idx, "b", gmem_guard=guard,
+                                           k_zero=V("kend"), b_trans=b_kn))
+        for i in range(MI):
+            for j in range(NJ):
+                slab.append(I.MmaSyncPtx(f"{acc}[{i * NJ + j}]", f"fa[{i}]", f"fb[{j}]", shape,
+                                         dtype, "f16" if promote else F32))
+    if stage:
+        slab.append(I.Sync(0, None, False))
+    if promote:
+        slab += [I.FragmentPromote(f"acc[{c}]", f"acch[{c}]") for c in range(MI * NJ)]
+    body.append(I.Loop(axis("kt", nk), tuple(slab), False, False))
+    lam = None
+    if epilogue:
+        lam = I.Lambda(("v",), (load("bv", "bias", V("col")), I.Let("z0", Lit(0.0), F32),
+                                assign("s", "add", "v", "bv"), assign("o", "maximum", "s", "z0")),
+                       ("o",))
+    for i in range(MI):
+        for j in range(NJ):
+            body.append(I.RegStore("c", (add(V("rowbase"), Lit(16 * i)), add(V("colbase"), Lit(8 * j))),
+                                   f"acc[{i * NJ + j}]", shape, None, lam, (), Lit(M), Lit(N),
+                                   split_k > 1))
+    gm, gn = -(-M // 64), -(-N // 64)
+    p.body = I.Tile((axis("ks", split_k), axis("bm", gm), axis("bn", gn), axis("t", 128)),
+                    tuple(body), 128)
+    p.grid, p.block = (split_k * gm * gn, 1, 1), (128, 1, 1)
+    if split_k > 1:
+        p.zero = ["c"]
+    p.rtol = {"bf16": 1e-3, "f16": 2e-2 if promote else 1e-3, "tf32": 5e-3}[dtype]
+    if out_dtype == "bf16":
+        p.rtol = max(p.rtol, 1e-2)
+    p.atol = None
+    p.oracle = {"family": "mma_matmul", "args": {"a": "a", "b": "b", "bias": "bias"},
+                "output": "c", "b_kn": b_kn, "epilogue": epilogue, "tf32": dtype == "tf32",
+                "bf16": {"a": dtype == "bf16", "b": dtype == "bf16"}, "out_bf16": out_dtype == "bf16"}
+    return p
+
+
+def mma_attention(Sq: int = 128, Sk: int = 64, d: int = 32, causal: bool = False,
+                  bias: bool = False, scale: float | None = None) -> Problem:
+    """O = softmax(Q K^T * scale (+ bias) (masked: key <= query)) V for bf16
+    Q [Sq, d], K, V [Sk, d]: each warp owns 16 query rows and all Sk keys
+    in registers -- S by mma.sync from Q fragments read from global memory and
+    K fragments from shared memory, the row max and row sum by
+    FragmentRowReduce, P = 2^(S c - max) by FragmentApply (mask and bias
+    arguments too; the bias row clamped to the last query, so the rows of a
+    ragged last block past Sq read in bounds), P repacked as bf16 A fragments
+    (FragmentRepack), O = P V, O / l by a row argument, stored by RegStore."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    c = scale * 1.4426950408889634
+    nS, nD, nK16 = Sk // 8, d // 8, Sk // 16
+    p = Problem(f"mma_attention_{Sq}x{Sk}x{d}", "softmax(q k^T s) v", "k_mma_attention", "o")
+    p.add_input("q", (Sq, d), "bf16")
+    p.add_input("k", (Sk, d), "bf16")
+    p.add_input("v", (Sk, d), "bf16")
+    if bias:
+        p.add_input("bias", (Sq, Sk))
+    p.out = ("o", (Sq, d), "f32")
+    t = V("t")
+    i32 = I.data_type("i32")
+    body = [I.Let("w", _idiv(t, 32), i32),
+            I.Let("qrow", add(mul(V("qb"), Lit(64)), mul(V("w"), Lit(16))), i32),
+            I.Smem("Ks", (Sk, d + 8), "bfloat16", 128), I.Smem("Vs", (Sk, d + 8), "bfloat16", 128)]
+    for sm, src in (("Ks", "k"), ("Vs", "v")):
+        r, cc = _idiv(V("e"), d), _imod(V("e"), d)
+        body.append(strided(axis("e", Sk * d), t, 128, [load("x", src, r, cc, dtype=BF16),
+                                                          write(sm, (r, cc), ("x",))]))
+    body += [I.Sync(0, None, False),
+             I.RegFragment("fq", "a", "m16n8k16", BF16, d // 16, 4),
+             I.RegFragment("fk", "b", "m16n8k16", BF16, 1, 2),
+             I.RegFragment("s", "c", "m16n8k16", F32, nS, 4),
+             I.RegFragment("fp", "a", "m16n8k16", BF16, nK16, 4),
+             I.RegFragment("fv", "b", "m16n8k16", BF16, 1, 2),
+             I.RegFragment("o", "c", "m16n8k16", F32, nD, 4),
+             I.Let("c", Lit(c), F32), I.Let("ninf", Lit(float("-inf")), F32),
+             I.Let("log2e", Lit(1.4426950408889634), F32)]
+    for kk in range(d // 16):
+        body.append(I.LdmatrixLoad(f"fq[{kk}]", "q", (V("qrow"), Lit(16 * kk)), "a",
+                                   gmem_guard=(Lit(Sq), None)))
+    for j in range(nS):
+        for kk in range(d // 16):
+            body += [I.LdmatrixLoad("fk", "Ks", (Lit(8 * j), Lit(16 * kk)), "b", d + 8, b_trans=False),
+                     I.MmaSyncPtx(f"s[{j}]", f"fq[{kk}]", "fk", "m16n8k16", BF16, F32)]
+    for j in range(nS):
+        body.append(I.FragmentApply(f"s[{j}]", "multiply", (f"s[{j}]", "c"), ("frag", "scalar")))
+        if bias:
+            # s + bias * log2(e): the scores are in base-2 units from here on
+            brow = I.BinaryExpr("min", V("row"), Lit(Sq - 1))
+            body.append(I.FragmentApply(f"s[{j}]", "fma",
+                                        (("bias", (brow, V("col"))), "log2e", f"s[{j}]"),
+                                        ("bias", "scalar", "frag"), True, None, None,
+                                        V("qrow"), Lit(8 * j)))
+        if causal:
+            body.append(I.FragmentApply(f"s[{j}]", "where",
+                                        (I.BinaryExpr("<=", V("col"), V("row")), f"s[{j}]", "ninf"),
+                                        ("mask", "frag", "scalar"), True, None, None,
+                                        V("qrow"), Lit(8 * j)))
+    body.append(I.FragmentRowReduce("mt", "mb", tuple(f"s[{j}]" for j in range(nS)), "max"))
+    for j in range(nS):
+        body.append(I.FragmentApply(f"s[{j}]", "subtract", (f"s[{j}]", ("mt", "mb")),
+                                    ("frag", "row"), True, None, "exp2"))
+    body.append(I.FragmentRowReduce("lt", "lb", tuple(f"s[{j}]" for j in range(nS)), "add"))
+    for i in range(nK16):
+        body.append(I.FragmentRepack(f"fp[{i}]", tuple(f"s[{j}]" for j in range(nS)), BF16, None, i))
+    for i in range(nK16):
+        for j in range(nD):
+            body += [I.LdmatrixLoad("fv", "Vs", (Lit(16 * i), Lit(8 * j)), "b", d + 8, b_trans=True),
+                     I.MmaSyncPtx(f"o[{j}]", f"fp[{i}]", "fv", "m16n8k16", BF16, F32)]
+    for j in range(nD):
+        body += [I.FragmentApply(f"o[{j}]", "divide", (f"o[{j}]", ("lt", "lb")), ("frag", "row")),
+                 I.RegStore("o", (V("qrow"), Lit(8 * j)), f"o[{j}]", "m16n8k16", m_guard=Lit(Sq))]
+    gq = -(-Sq // 64)
+    p.body = I.Tile((axis("qb", gq), axis("t", 128)), tuple(body), 128)
+    p.grid, p.block = (gq, 1, 1), (128, 1, 1)
+    p.rtol, p.atol = 2e-2, None
+    p.oracle = {"family": "mma_attention", "args": {"q": "q", "k": "k", "v": "v", "bias": "bias"},
+                "output": "o", "scale": scale, "causal": causal, "bias_on": bias,
+                "bf16": {"q": True, "k": True, "v": True}}
+    return p
+
+
+def _xor(a, b):
+    return I.BinaryExpr("^", a, b)
+
+
+def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout: str = "sw128",
+                 warpgroups: int = 1, pipelined: bool = False, dtype: str = "bf16") -> Problem:
+    """C = A . B through the warpgroup statements (WgmmaDescriptor, WgmmaFence,
+    WgmmaMma m64nBNk16, WgmmaCommit, WgmmaWait): each warpgroup owns 64 rows
+    of a CTA tile of 64 * ``warpgroups`` x BN, the CTA's threads stage 64-wide
+    K slabs of A and B into shared memory in the canonical layout the
+    descriptors name, and each warp stores its 16 rows of the accumulator with
+    RegStore.  ``layout``: ``sw128`` (both operands K-major, 128-byte
+    swizzle: element (r, k) of a 64-wide slab at r*64 + ((k/8 ^ r%8)*8) +
+    k%8), ``sw128_mn`` (B MN-major, 128-byte swizzle, 64-column blocks of
+    64 k-rows, LBO between blocks) or ``none`` (K-major without swizzle:
+    8x8 core matrices, LBO 128 B between core matrices along K, SBO 1024 B
+    between 8-row groups).  ``pipelined``: two slab buffers, a commit per
+    slab and ``WgmmaWait(1)`` before a buffer is refilled."""
+    dt = {"bf16": BF16, "f16": F16}[dtype]
+    smem_ty = {"bf16": "bfloat16", "f16": "half"}[dtype]
+    BK = 64
+    BM = 64 * warpgroups
+    T = 128 * warpgroups
+    nbuf = 2 if pipelined else 1
+    nk = -(-K // BK)
+    p = Problem(f"wgmma_matmul_{layout}_{M}x{N}x{K}", "a @ b", "k_wgmma_matmul", "c")
+    p.add_input("a", (M, K), dtype)
+    p.add_input("b", (K, N), dtype)
+    p.out = ("c", (M, N), "f32")
+    t = V("t")
+    i32 = I.data_type("i32")
+    a_sz, b_sz = BM * BK, BN * BK
+
+    def pos_kmajor(r, kk):
+        if layout == "none":
+            return add(add(mul(_idiv(r, 8), Lit(512)), mul(_idiv(kk, 8), Lit(64))),
+                       add(mul(_imod(r, 8), Lit(8)), _imod(kk, 8)))
+        return add(mul(r, Lit(64)), add(mul(_xor(_idiv(kk, 8), _imod(r, 8)), Lit(8)), _imod(kk, 8)))
+
+    def pos_mn(kk, n):
+        return add(add(mul(_idiv(n, 64), Lit(64 * BK)), mul(kk, Lit(64))),
+                   add(mul(_xor(_idiv(_imod(n, 64), 8), _imod(kk, 8)), Lit(8)), _imod(n, 8)))
+
+    body = [I.Let("w", _idiv(t, 32), i32), I.Let("wg", _idiv(t, 128), i32),
+            I.Let("zero", Lit(0.0), F32),
+            I.Smem("As", (nbuf * a_sz,), smem_ty, 1024), I.Smem("Bs", (nbuf * b_sz,), smem_ty, 1024),
+            I.RegFragment("acc", "c", "m16n8k16", F32, BN // 8, 4)]
+    slab = [I.Let("k0", mul(V("kt"), Lit(BK)), i32),
+            I.Let("buf", _imod(V("kt"), nbuf) if nbuf > 1 else Lit(0), i32)]
+    if pipelined:
+        slab.append(I.WgmmaWait(1))
+    r, kk = _idiv(V("e"), BK), _imod(V("e"), BK)
+    arow = add(mul(V("bm"), Lit(BM)), r)
+    slab.append(strided(axis("e", BM * BK), t, T, [
+        I.Cond(_and(I.BinaryExpr("<", arow, Lit(M)), I.BinaryExpr("<", add(V("k0"), kk), Lit(K))),
+               (load("v", "a", arow, add(V("k0"), kk), dtype=dt),
+                write("As", (add(mul(V("buf"), Lit(a_sz)), pos_kmajor(r, kk)),), ("v",))),
+               (write("As", (add(mul(V("buf"), Lit(a_sz)), pos_kmajor(r, kk)),), ("zero",)),))]))
+    kr, n = _idiv(V("e"), BN), _imod(V("e"), BN)
+    ncol = add(mul(V("bn"), Lit(BN)), n)
+    bpos = pos_mn(kr, n) if layout == "sw128_mn" else pos_kmajor(n, kr)
+    slab.append(strided(axis("e", BK * BN), t, T, [
+        I.Cond(_and(I.BinaryExpr("<", add(V("k0"), kr), Lit(K)), I.BinaryExpr("<", ncol, Lit(N))),
+               (load("v", "b", add(V("k0"), kr), ncol, dtype=dt),
+                write("Bs", (add(mul(V("buf"), Lit(b_sz)), bpos),), ("v",))),
+               (write("Bs", (add(mul(V("buf"), Lit(b_sz)), bpos),), ("zero",)),))]))
+    slab += [I.Sync(0, None, False), I.WgmmaFence()]
+    swz = "NONE" if layout == "none" else "128B"
+    a_lbo, a_sbo = (128, 1024) if layout == "none" else (16, 1024)
+    b_lbo, b_sbo = ((64 * BK * 2, 1024) if layout == "sw128_mn" else (a_lbo, a_sbo))
+    for s in range(BK // 16):
+        a_step = 128 * s if layout == "none" else 16 * s
+        b_step = 16 * 64 * s if layout == "sw128_mn" else a_step
+        a_idx = add(add(mul(V("buf"), Lit(a_sz)), mul(V("wg"), Lit(64 * BK))), Lit(a_step))
+        b_idx = add(mul(V("buf"), Lit(b_sz)), Lit(b_step))
+        first = I.BinaryExpr("||", I.BinaryExpr(">", V("kt"), Lit(0)), I.BinaryExpr(">", Lit(s), Lit(0)))
+        slab += [I.WgmmaDescriptor("da", "As", (a_idx,), swz, a_lbo, a_sbo),
+                 I.WgmmaDescriptor("db", "Bs", (b_idx,), swz, b_lbo, b_sbo),
+                 I.WgmmaMma("acc", "db", f"m64n{BN}k16", dt, "da", None,
+                            first if s == 0 else Lit(1), 0, int(layout == "sw128_mn"))]
+    slab.append(I.WgmmaCommit())
+    if not pipelined:
+        slab.append(I.WgmmaWait(0))
+    body.append(I.Loop(axis("kt", nk), tuple(slab), False, False))
+    body.append(I.WgmmaWait(0))
+    row0 = add(add(mul(V("bm"), Lit(BM)), mul(V("wg"), Lit(64))), mul(_imod(V("w"), 4), Lit(16)))
+    for j in range(BN // 8):
+        body.append(I.RegStore("c", (row0, add(mul(V("bn"), Lit(BN)), Lit(8 * j))), f"acc[{j}]",
+                               m_guard=Lit(M), n_guard=Lit(N)))
+    gm, gn = -(-M // BM), -(-N // BN)
+    p.body = I.Tile((axis("bm", gm), axis("bn", gn), axis("t", T)), tuple(body), T)
+    p.grid, p.block = (gm * gn, 1, 1), (T, 1, 1)
+    p.rtol, p.atol = 1e-3, None
+    p.oracle = {"family": "mma_matmul", "args": {"a": "a", "b": "b", "bias": "bias"},
+                "output": "c", "b_kn": True, "epilogue": False, "tf32": False,
+                "bf16": {"a": dtype == "bf16", "b": dtype == "bf16"}, "out_bf16": False}
+    return p

@@ -143,6 +143,54 @@ def zero_prologue(x, words):
     return out
 
 
+def mma_matmul(a, b, b_kn=True, bias=None, tf32=False, out_bf16=False):
+    """C = A . B (B given [K, N], or [N, K] when not ``b_kn``) in float64,
+    then relu(C + bias[col]) when a bias is given, as float32 (bf16-rounded
+    when the output buffer is bf16).  tf32 operands: each input rounded to
+    tf32 (10 explicit mantissa bits, round to nearest, ties away) first."""
+    a, b = _d(a), _d(b)
+    if tf32:
+        a, b = _tf32(a), _tf32(b)
+    c = a @ (b if b_kn else b.T)
+    if bias is not None:
+        c = np.maximum(c + _d(bias)[None, :], 0.0)
+    c = c.astype(f32)
+    if out_bf16:
+        c = bf16_to_f32(bf16_bits_rn(c))
+    return c
+
+
+def mma_attention(q, k, v, scale, causal=False, bias=None):
+    """softmax(Q K^T * scale (+ bias), keys after the query masked when
+    causal) V in float64, as float32."""
+    q, k, v = _d(q), _d(k), _d(v)
+    s = (q @ k.T) * scale
+    if bias is not None:
+        s = s + _d(bias) * 1.0
+    if causal:
+        i = np.arange(s.shape[0])[:, None]
+        j = np.arange(s.shape[1])[None, :]
+        s = np.where(j <= i, s, -np.inf)
+    s = s - s.max(-1, keepdims=True)
+    e = np.exp(s)
+    return ((e / e.sum(-1, keepdims=True)) @ v).astype(f32)
+
+
+def _tf32(x):
+    """Round float32 values to tf32: keep the top 10 mantissa bits, round to
+    nearest with ties away from zero (PTX cvt.rna.tf32.f32)."""
+    u = np.asarray(x, f32).view(np.uint32).astype(np.uint64)
+    u = ((u + 0x1000) & 0xFFFFE000).astype(np.uint32)
+    return u.view(f32).astype(np.float64)
+
+
+def bf16_bits_rn(x):
+    """float32 -> bf16 bit patterns, round to nearest even."""
+    u = np.asarray(x, f32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return u.astype(np.uint16)
+
+
 # --------------------------------------------------------------------------
 # the reference's open problems (problems/*/meta.json "code")
 # --------------------------------------------------------------------------
@@ -215,6 +263,13 @@ def evaluate_family(spec: dict, inputs: dict) -> dict:
         r = select_split(v[a["x"]], spec["split"])
     elif fam == "zero_prologue":
         r = zero_prologue(v[a["x"]], spec["words"])
+    elif fam == "mma_matmul":
+        r = mma_matmul(v[a["a"]], v[a["b"]], spec["b_kn"],
+                       v.get(a["bias"]) if spec.get("epilogue") else None,
+                       spec.get("tf32", False), spec.get("out_bf16", False))
+    elif fam == "mma_attention":
+        r = mma_attention(v[a["q"]], v[a["k"]], v[a["v"]], spec["scale"], spec.get("causal"),
+                          v.get(a["bias"]) if spec.get("bias_on") else None)
     else:
         raise KeyError(fam)
     return {out: r}

@@ -56,12 +56,13 @@ def test_cli_usage_and_missing_meta(tmp_path):
 
 
 def test_cli_unsupported_is_exit_1(tmp_path):
-    # a statement kind no lowering handles (wgmma is sm_90a-only) -> exit 1,
-    # "unsupported construct"
+    # a statement sm_100a cannot lower (block-scaled mma.sync is sm_120a-only)
+    # -> exit 1, "unsupported construct"
     g, m = synth.vector_add(n=1024, threads=256).build()
     body = g["nodes"]["add"]["op_fields"]["body"][0]
     g["nodes"]["add"]["op_fields"]["body"][0] = body.replace(
-        "body=(StridedLoop(", "body=(WgmmaFence(), StridedLoop(", 1)
+        "body=(StridedLoop(",
+        "body=(BlockScaleLoad(frag='f', src_buffer='x0', src_index=(), role='a'), StridedLoop(", 1)
     (tmp_path / "k.ir.json").write_text(json.dumps(g))
     (tmp_path / "meta.json").write_text(json.dumps(m))
     r = _cli(str(tmp_path / "k.ir.json"))

@@ -1,0 +1,106 @@
+"""CPU checks of the register-fragment statements: every synthesised IR
+compiles through the generic lowering, assembles for sm_100a and passes
+the static checkers; the forms sm_100a cannot run exit 1."""
+import json
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from emmy_b200 import ir as I
+from emmy_b200 import ptxcheck, synth
+from emmy_b200.compiler import compile_graph
+from oracle import expr
+
+REPO = Path(__file__).resolve().parents[1]
+
+CASES = {
+    "smem": dict(), "smem_nk": dict(b_kn=False), "direct": dict(stage=False),
+    "f16_promote": dict(dtype="f16", promote=True), "tf32": dict(dtype="tf32"),
+    "epilogue_bf16": dict(epilogue=True, out_dtype="bf16"), "split_k": dict(split_k=3, K=200),
+}
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_mma_matmul_compiles(name):
+    g, m = synth.mma_matmul(**CASES[name]).build()
+    c = compile_graph(g, m)
+    assert c.kind == "generic"
+    assert "mma.sync.aligned" in c.ptx
+    assert ptxcheck.check(c.ptx) == []
+    if shutil.which("ptxas"):
+        r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", "-"],
+                           input=c.ptx, capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+
+
+def test_mma_attention_compiles():
+    g, m = synth.mma_attention(Sq=100, causal=True, bias=True).build()
+    c = compile_graph(g, m)
+    for ins in ("ldmatrix.sync.aligned.m8n8.x2.trans", "shfl.sync.bfly",
+                "cvt.rn.bf16x2.f32", "mma.sync.aligned.m16n8k16"):
+        assert ins in c.ptx
+    assert ptxcheck.check(c.ptx) == []
+
+
+def test_round_trip_repr():
+    """The fragment statements serialise and parse back unchanged."""
+    p = synth.mma_attention(causal=True, bias=True)
+    body = p.graph()["nodes"]["o"]["op_fields"]["body"][0]
+    assert I.parse_repr(body) == p.body
+
+
+def _cli(tmp_path, g, m):
+    (tmp_path / "k.ir.json").write_text(json.dumps(g))
+    (tmp_path / "meta.json").write_text(json.dumps(m))
+    return subprocess.run([sys.executable, str(REPO / "compile.py"), str(tmp_path / "k.ir.json")],
+                          capture_output=True, text=True)
+
+
+def test_block_scaled_is_exit_1(tmp_path):
+    """Block-scaled mma.sync is an sm_120a instruction: exit 1, unsupported."""
+    g, m = synth.mma_matmul().build()
+    body = g["nodes"]["c"]["op_fields"]["body"][0]
+    g["nodes"]["c"]["op_fields"]["body"][0] = body.replace(
+        "sfa_frag=None", "sfa_frag='fa[0]'", 1)
+    r = _cli(tmp_path, g, m)
+    assert r.returncode == 1 and r.stderr.startswith("unsupported construct:")
+    assert "sm_120a" in r.stderr
+
+
+def test_oracle_tf32_rounding():
+    """cvt.rna.tf32.f32: 10 mantissa bits kept, ties away from zero."""
+    x = np.array([1.0, 1.0 + 2 ** -11, 1.0 + 2 ** -10 + 2 ** -11, -(1.0 + 2 ** -11)], np.float32)
+    assert list(expr._tf32(x)) == [1.0, 1.0 + 2 ** -10, 1.0 + 2 ** -9, -(1.0 + 2 ** -10)]
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(layout="sw128_mn", BN=128), dict(layout="none"),
+                                dict(pipelined=True), dict(warpgroups=2, BN=128)],
+                         ids=["sw128", "sw128_mn", "none", "pipelined", "wg2"])
+def test_wgmma_compiles(kw):
+    """wgmma on sm_100a: tcgen05.mma M = 64 into tensor memory, 16x256b
+    loads and stores of the C fragments, TMEM freed at the end; the static
+    checkers pass (TMEM pairing, bounded mbarrier waits, definedness)."""
+    g, m = synth.wgmma_matmul(**kw).build()
+    c = compile_graph(g, m)
+    assert c.kind == "generic"
+    for ins in ("tcgen05.mma.cta_group::1.kind::f16", "tcgen05.ld.sync.aligned.16x256b",
+                "tcgen05.st.sync.aligned.16x256b", "tcgen05.dealloc", "fence.proxy.async"):
+        assert ins in c.ptx
+    assert ptxcheck.check(c.ptx) == []
+    if shutil.which("ptxas"):
+        r = subprocess.run(["ptxas", "-arch=sm_100a", "-o", "/dev/null", "-"],
+                           input=c.ptx, capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+
+
+def test_wgmma_register_a_is_exit_1(tmp_path):
+    """An A operand in registers (a_frag) is not lowered: exit 1."""
+    g, m = synth.wgmma_matmul().build()
+    body = g["nodes"]["c"]["op_fields"]["body"][0]
+    g["nodes"]["c"]["op_fields"]["body"][0] = body.replace("a_frag=None", "a_frag='acc'", 1)
+    r = _cli(tmp_path, g, m)
+    assert r.returncode == 1 and "a_frag" in r.stderr
