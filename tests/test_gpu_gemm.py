@@ -138,14 +138,17 @@ F32_PERSISTENT_CASES = [dict(M=256, N=256, K=128), dict(M=1024, N=768, K=256),
 
 @pytest.mark.parametrize("kw", F32_PERSISTENT_CASES,
                          ids=[f"{c['M']}x{c['N']}x{c['K']}" for c in F32_PERSISTENT_CASES])
-def test_gemm_f32_persistent_pairs(kw):
-    """fp32 operands on persistent CTA pairs: each CTA's warps 4-7 split its
-    own landed slice into tf32 hi/lo parts and arrive on the leader's
-    conversion barrier; the leader issues lo*hi, hi*lo, hi*hi as
-    ``kind::tf32`` pair MMAs; the same warps drain the previous tile's
-    accumulator.  Rel 2e-5 of max|C| (BASELINE asks 1e-4); large shapes on
-    sampled rows; the last two shapes run the split 256 x 128 tail."""
+def test_gemm_f32_persistent_pairs(kw, monkeypatch):
+    """fp32 operands on persistent CTA pairs with both operands in shared
+    memory (``TF32_A_TMEM`` off): each CTA's converter warps write the tf32
+    low parts of its landed slice and arrive on the leader's conversion
+    barrier; the leader issues lo*hi, hi*lo, hi*hi as ``kind::tf32`` pair
+    MMAs; warps 4-7 drain the previous tile's accumulator.  Rel 2e-5 of
+    max|C| (BASELINE asks 1e-4); large shapes on sampled rows; the last two
+    shapes run the split 256 x 128 tail."""
     from emmy_b200 import compiler
+    from emmy_b200.templates import gemm_persistent
+    monkeypatch.setattr(gemm_persistent, "TF32_A_TMEM", False)
     p = synth.config("matmul_f32", **kw)
     g, m = p.build()
     assert "persistent CTA pairs" in compiler.compile_graph(g, m).render()
@@ -183,7 +186,8 @@ def test_gemm_f32_3xtf32_error_against_float64():
 @pytest.mark.parametrize("kw", F32_PERSISTENT_CASES,
                          ids=[f"{c['M']}x{c['N']}x{c['K']}" for c in F32_PERSISTENT_CASES])
 def test_gemm_f32_persistent_pairs_a_in_tmem(kw, monkeypatch):
-    """3xTF32 with the A operand in tensor memory (``TF32_A_TMEM``): warps
+    """3xTF32 with the A operand in tensor memory (``TF32_A_TMEM``, the
+    default, set here explicitly): warps
     4-7 store each A row's raw values and low parts into the stage's TMEM
     columns, the MMAs read A there (``[a-tmem]``) and B from shared memory,
     one accumulator (each tile drained before the next one's MMAs).  The
