@@ -37,7 +37,10 @@ fixes the forms below, and the IRs in ``synth`` (``mma_matmul``,
   must keep it so); anything else -- global memory, f32 sources (tf32 or
   converted), ``gmem_guard`` = (row bound, column bound) of the source and
   ``k_zero`` = the bound of the contraction coordinate -- loads element by
-  element, zero where a guard fails;
+  element, zero where a guard fails.  ``swizzle`` (shared memory only) is the
+  vocabulary's chunk swizzle of ``CpAsyncCopy`` (``"B128"`` / ``"B64"`` /
+  ``"B32"``, optional ``@shift``) applied to every flat element index, so a
+  tile copied in swizzled is read back in place;
 * ``FragmentApply`` computes ``out = post(op(args))`` per C element; an
   argument is, by ``kinds``: ``frag`` (a fragment reference), ``row`` (a
   (top, bottom) pair of names from ``FragmentRowReduce``), ``scalar`` (a name
@@ -56,13 +59,14 @@ fixes the forms below, and the IRs in ``synth`` (``mma_matmul``,
   ``row < m_guard`` and ``col < n_guard``; the epilogue ``Lambda`` binds its
   parameters to the element of ``frag`` and of each of ``extra_frags`` and
   ``row`` / ``col`` to the coordinates, runs its body and stores
-  ``results[0]``, converted to the buffer's type (``red.add`` when atomic).
+  ``results[0]``, converted to the buffer's type (``red.add`` when atomic);
+  into shared memory it takes the same ``swizzle``.
 
 Not lowered (exit 1, ``unsupported construct``): ``BlockScaleLoad`` and the
 block-scaled ``MmaSyncPtx`` (``sfa_frag`` / ``sfb_frag``) -- block-scaled
 ``mma.sync`` is an sm_120a instruction, sm_100a scales only through
 ``tcgen05.mma``; the ``byte_slab`` dequantising and ``pair_frag`` loads;
-``volta_interleaved`` stores; swizzled fragment loads and stores.
+``volta_interleaved`` stores; swizzled global accesses.
 """
 from __future__ import annotations
 
@@ -327,12 +331,14 @@ class FragmentLowering:
         for f in ("byte_slab", "scale_buffer", "pair_frag"):
             if getattr(s, f, None):
                 raise NotImplementedError(f"LdmatrixLoad {f}")
-        if getattr(s, "swizzle", None) not in (None, False, "NONE", "none"):
-            raise NotImplementedError(f"LdmatrixLoad swizzle {s.swizzle!r}")
         if getattr(s, "fragment_layout", None) is not None:
             raise NotImplementedError("LdmatrixLoad with a custom fragment layout")
         src = s.src_buffer
         shared = src in self.smem
+        swz = getattr(s, "swizzle", None)
+        swz = None if swz in (None, False, "NONE", "none") else swz
+        if swz is not None and not shared:
+            raise NotImplementedError("LdmatrixLoad swizzle of a global buffer")
         shape = self.shape_of(src)
         sty = self.smem[src]["ty"] if shared else self.ctx.bufs.dtypes.get(src, "f32")
         ldm = int(s.ldm) if s.ldm else int(shape[-1])
@@ -365,7 +371,7 @@ class FragmentLowering:
                 k(f"shr.u32 {c}, {lane}, {col_shift};")
                 k(f"and.b32 {c}, {c}, 1;")
                 k(f"mad.lo.s32 {off}, {c}, 8, {off};")
-            addr = self.saddr(src, self._iadd(base, off))
+            addr = self.saddr(src, self.apply_swizzle(self._iadd(base, off), swz))
             k(f"ldmatrix.sync.aligned.m8n8.x{n}{trans}.shared.b16 "
               f"{{{', '.join(regs)}}}, [{addr}];")
             return
@@ -384,7 +390,7 @@ class FragmentLowering:
                 dr, dc = b, a
             kcoord_is_col = role == "a" or not btrans
             off = self._iadd(self._imul(dr, ldm) if not _imm(dr) else str(int(dr) * ldm), dc)
-            flat = self._iadd(base, off)
+            flat = self.apply_swizzle(self._iadd(base, off), swz)
             p = None
             conds = []
             if guard is not None:
@@ -597,10 +603,12 @@ class FragmentLowering:
             raise NotImplementedError("RegStore stores a C fragment")
         if getattr(s, "volta_interleaved", False):
             raise NotImplementedError("RegStore volta_interleaved")
-        if getattr(s, "swizzle", None) not in (None, False, "NONE", "none"):
-            raise NotImplementedError(f"RegStore swizzle {s.swizzle!r}")
         buf = s.dst_buffer
         shared = buf in self.smem
+        swz = getattr(s, "swizzle", None)
+        swz = None if swz in (None, False, "NONE", "none") else swz
+        if swz is not None and not shared:
+            raise NotImplementedError("RegStore swizzle into a global buffer")
         shape = self.shape_of(buf)
         ty = self.smem[buf]["ty"] if shared else self.ctx.bufs.dtypes.get(buf, "f32")
         index = tuple(s.dst_index)
@@ -643,6 +651,7 @@ class FragmentLowering:
                                   self._iadd(self._imul(ro, int(s.ldm)), co))
             else:
                 flat = self._flat_ops(index, shape, {rd: ro, cd: co})
+            flat = self.apply_swizzle(flat, swz)
             self._store_f32(buf, flat, ty, val, bool(s.atomic), shared)
             k.mark(skip)
 

@@ -1082,27 +1082,36 @@ class GenericLowering(FragmentLowering, WgmmaLowering):
             lf = self._iadd(self._imul(self.ival(s.lane_index[0]), cols),
                             self.ival(s.lane_index[1]))
             flat = self._iadd(flat, lf)
-        if s.swizzle not in (None, "NONE"):
-            sw = str(s.swizzle)
-            mode, shift = (sw.split("@") + ["6"])[:2] if "@" in sw else (sw, "6")
-            mask = {"B128": 7, "B64": 3, "B32": 1}[mode]
-            f = flat
-            if _is_imm(f):
-                e = int(f)
-                flat = str(e ^ (((e >> int(shift)) & mask) << 3))
-            else:
-                t1 = k.reg("r")
-                k(f"shr.u32 {t1}, {f}, {shift};")
-                k(f"and.b32 {t1}, {t1}, {mask};")
-                k(f"shl.b32 {t1}, {t1}, 3;")
-                t2 = k.reg("r")
-                k(f"xor.b32 {t2}, {f}, {t1};")
-                flat = t2
+        flat = self.apply_swizzle(flat, s.swizzle)
         sa = self.saddr(s.smem, flat)
         src_ty = self.ctx.bufs.dtypes.get(s.src, "f32")
         ga = self.gaddr(s.src, self.flat(s.src_index, self.shape_of(s.src)), NBYTES.get(src_ty, 4))
         ins = "cp.async.cg.shared.global" if s.nbytes == 16 else "cp.async.ca.shared.global"
         k(f"{ins} [{sa}], [{ga}], {s.nbytes};")
+
+    def apply_swizzle(self, flat, swizzle):
+        """A shared-memory flat element index under the vocabulary's swizzle
+        (the reference's ``apply_swizzle``, ``compile.py:1706-1730``):
+        ``"B128"`` / ``"B64"`` / ``"B32"`` with an optional ``@shift`` (default
+        6) XOR 8-element chunks by (index >> shift) & 7 / 3 / 1."""
+        if swizzle in (None, "NONE"):
+            return flat
+        k = self.k
+        sw = str(swizzle)
+        mode, shift = (sw.split("@") + ["6"])[:2] if "@" in sw else (sw, "6")
+        mask = {"B128": 7, "B64": 3, "B32": 1}.get(mode)
+        if mask is None:
+            raise NotImplementedError(f"swizzle {swizzle!r}")
+        if _is_imm(flat):
+            e = int(flat)
+            return str(e ^ (((e >> int(shift)) & mask) << 3))
+        t1 = k.reg("r")
+        k(f"shr.u32 {t1}, {flat}, {shift};")
+        k(f"and.b32 {t1}, {t1}, {mask};")
+        k(f"shl.b32 {t1}, {t1}, 3;")
+        t2 = k.reg("r")
+        k(f"xor.b32 {t2}, {flat}, {t1};")
+        return t2
 
     # ------------------------------------------------- TMA and mbarriers
     # The reference defines these nodes without lowering them (TASK.md

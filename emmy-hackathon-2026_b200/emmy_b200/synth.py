@@ -897,9 +897,14 @@ def _and(a, b):
     return I.BinaryExpr("&&", a, b)
 
 
+def _xor(a, b):
+    return I.BinaryExpr("^", a, b)
+
+
 def mma_matmul(M: int = 200, N: int = 136, K: int = 80, dtype: str = "bf16",
                b_kn: bool = True, stage: bool = True, promote: bool = False,
-               epilogue: bool = False, out_dtype: str = "f32", split_k: int = 1) -> Problem:
+               epilogue: bool = False, out_dtype: str = "f32", split_k: int = 1,
+               swizzle: bool = False) -> Problem:
     """C = A . B through register fragments: CTAs of 128 threads own 64 x 64
     tiles of C, each warp a 32 x 32 quarter as 2 x 4 mma.sync atoms.
 
@@ -912,14 +917,17 @@ def mma_matmul(M: int = 200, N: int = 136, K: int = 80, dtype: str = "bf16",
     f32 accumulators after every slab; ``epilogue``: C = relu(A.B + bias[col])
     through the store's Lambda; ``out_dtype`` f32 or bf16; ``split_k`` > 1:
     that many CTAs per tile, each over a K range, adding atomically into a
-    zeroed C."""
+    zeroed C.  ``swizzle`` (16-bit, staged): 64-wide slabs without padding,
+    written with their 16-byte chunks XOR-swizzled by row (chunk c of row r at
+    c ^ (r % 8)) and read back by ldmatrix through the ``"B128"`` swizzle."""
     wide = dtype in ("bf16", "f16")
     in_dt = {"bf16": BF16, "f16": F16, "tf32": F32}[dtype]
     in_name = {"bf16": "bf16", "f16": "f16", "tf32": "f32"}[dtype]
     shape = "m16n8k16" if wide else "m16n8k8"
     KK = 16 if wide else 8
-    BK, MI, NJ = 32, 2, 4
-    pad = 8 if wide else 4
+    BK, MI, NJ = (64 if swizzle else 32), 2, 4
+    pad = 0 if swizzle else (8 if wide else 4)
+    swz = "B128" if swizzle else None
     smem_ty = {"bf16": "bfloat16", "f16": "half", "tf32": "float"}[dtype]
     kper = -(-K // split_k)
     nk = -(-kper // BK)
@@ -952,10 +960,11 @@ def mma_matmul(M: int = 200, N: int = 136, K: int = 80, dtype: str = "bf16",
         def stage_copy(dst, src, rows, cols, src_r, src_c, rbound, cbound):
             r, c = _idiv(V("e"), cols), _imod(V("e"), cols)
             ok = _and(I.BinaryExpr("<", src_r(r), rbound), I.BinaryExpr("<", src_c(c), cbound))
+            dc = _xor(c, mul(_imod(r, 8), Lit(8))) if swizzle else c
             return strided(axis("e", rows * cols), t, 128, [
                 I.Cond(ok, (load("v", src, src_r(r), src_c(c), dtype=in_dt),
-                            write(dst, (r, c), ("v",))),
-                       (write(dst, (r, c), ("zero",)),))])
+                            write(dst, (r, dc), ("v",))),
+                       (write(dst, (r, dc), ("zero",)),))])
         slab.append(stage_copy("As", "a", 64, BK, lambda r: add(mul(V("bm"), Lit(64)), r),
                                lambda c: add(V("k0"), c), Lit(M), V("kend")))
         if b_kn:
@@ -969,7 +978,7 @@ def mma_matmul(M: int = 200, N: int = 136, K: int = 80, dtype: str = "bf16",
         for i in range(MI):
             if stage:
                 slab.append(I.LdmatrixLoad(f"fa[{i}]", "As", (add(mul(V("wm"), Lit(32)), Lit(16 * i)),
-                                                           Lit(kk * KK)), "a", BK + pad))
+                                                           Lit(kk * KK)), "a", BK + pad, swz))
             else:
                 slab.append(I.LdmatrixLoad(f"fa[{i}]", "a", (add(V("rowbase"), Lit(16 * i)),
                                                           add(V("k0"), Lit(kk * KK))), "a",
@@ -979,7 +988,7 @@ def mma_matmul(M: int = 200, N: int = 136, K: int = 80, dtype: str = "bf16",
                 n_off = add(mul(V("wn"), Lit(32)), Lit(8 * j))
                 idx = (Lit(kk * KK), n_off) if b_kn else (n_off, Lit(kk * KK))
                 slab.append(I.LdmatrixLoad(f"fb[{j}]", "Bs", idx, "b",
-                                           (64 + pad) if b_kn else (BK + pad), b_trans=b_kn))
+                                           (64 + pad) if b_kn else (BK + pad), swz, b_trans=b_kn))
             else:
                 n_abs = add(V("colbase"), Lit(8 * j))
                 k_abs = add(V("k0"), Lit(kk * KK))
@@ -1106,12 +1115,9 @@ def mma_attention(Sq: int = 128, Sk: int = 64, d: int = 32, causal: bool = False
     return p
 
 
-def _xor(a, b):
-    return I.BinaryExpr("^", a, b)
-
-
 def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout: str = "sw128",
-                 warpgroups: int = 1, pipelined: bool = False, dtype: str = "bf16") -> Problem:
+                 warpgroups: int = 1, pipelined: bool = False, dtype: str = "bf16",
+                 a_regs: bool = False) -> Problem:
     """C = A . B through the warpgroup statements (WgmmaDescriptor, WgmmaFence,
     WgmmaMma m64nBNk16, WgmmaCommit, WgmmaWait): each warpgroup owns 64 rows
     of a CTA tile of 64 * ``warpgroups`` x BN, the CTA's threads stage 64-wide
@@ -1123,7 +1129,10 @@ def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout:
     64 k-rows, LBO between blocks) or ``none`` (K-major without swizzle:
     8x8 core matrices, LBO 128 B between core matrices along K, SBO 1024 B
     between 8-row groups).  ``pipelined``: two slab buffers, a commit per
-    slab and ``WgmmaWait(1)`` before a buffer is refilled."""
+    slab and ``WgmmaWait(1)`` before a buffer is refilled.  ``a_regs``: the A
+    operand in registers -- each warp loads its 16 rows of every 16-wide K
+    step as an A fragment straight from global memory (guarded) and passes
+    it as ``a_frag``."""
     dt = {"bf16": BF16, "f16": F16}[dtype]
     smem_ty = {"bf16": "bfloat16", "f16": "half"}[dtype]
     BK = 64
@@ -1153,17 +1162,21 @@ def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout:
             I.Let("zero", Lit(0.0), F32),
             I.Smem("As", (nbuf * a_sz,), smem_ty, 1024), I.Smem("Bs", (nbuf * b_sz,), smem_ty, 1024),
             I.RegFragment("acc", "c", "m16n8k16", F32, BN // 8, 4)]
+    if a_regs:
+        body.append(I.RegFragment("fa", "a", "m16n8k16", dt, 1, 4))
     slab = [I.Let("k0", mul(V("kt"), Lit(BK)), i32),
             I.Let("buf", _imod(V("kt"), nbuf) if nbuf > 1 else Lit(0), i32)]
     if pipelined:
         slab.append(I.WgmmaWait(1))
     r, kk = _idiv(V("e"), BK), _imod(V("e"), BK)
     arow = add(mul(V("bm"), Lit(BM)), r)
-    slab.append(strided(axis("e", BM * BK), t, T, [
+    a_stage = strided(axis("e", BM * BK), t, T, [
         I.Cond(_and(I.BinaryExpr("<", arow, Lit(M)), I.BinaryExpr("<", add(V("k0"), kk), Lit(K))),
                (load("v", "a", arow, add(V("k0"), kk), dtype=dt),
                 write("As", (add(mul(V("buf"), Lit(a_sz)), pos_kmajor(r, kk)),), ("v",))),
-               (write("As", (add(mul(V("buf"), Lit(a_sz)), pos_kmajor(r, kk)),), ("zero",)),))]))
+               (write("As", (add(mul(V("buf"), Lit(a_sz)), pos_kmajor(r, kk)),), ("zero",)),))])
+    if not a_regs:
+        slab.append(a_stage)
     kr, n = _idiv(V("e"), BN), _imod(V("e"), BN)
     ncol = add(mul(V("bn"), Lit(BN)), n)
     bpos = pos_mn(kr, n) if layout == "sw128_mn" else pos_kmajor(n, kr)
@@ -1182,10 +1195,19 @@ def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout:
         a_idx = add(add(mul(V("buf"), Lit(a_sz)), mul(V("wg"), Lit(64 * BK))), Lit(a_step))
         b_idx = add(mul(V("buf"), Lit(b_sz)), Lit(b_step))
         first = I.BinaryExpr("||", I.BinaryExpr(">", V("kt"), Lit(0)), I.BinaryExpr(">", Lit(s), Lit(0)))
+        scale = first if s == 0 else Lit(1)
+        if a_regs:
+            wrow = add(add(mul(V("bm"), Lit(BM)), mul(V("wg"), Lit(64))), mul(_imod(V("w"), 4), Lit(16)))
+            slab += [I.LdmatrixLoad("fa", "a", (wrow, add(V("k0"), Lit(16 * s))), "a",
+                                    gmem_guard=(Lit(M), None), k_zero=Lit(K)),
+                     I.WgmmaDescriptor("db", "Bs", (b_idx,), swz, b_lbo, b_sbo),
+                     I.WgmmaMma("acc", "db", f"m64n{BN}k16", dt, None, "fa", scale, 0,
+                                int(layout == "sw128_mn"))]
+            continue
         slab += [I.WgmmaDescriptor("da", "As", (a_idx,), swz, a_lbo, a_sbo),
                  I.WgmmaDescriptor("db", "Bs", (b_idx,), swz, b_lbo, b_sbo),
                  I.WgmmaMma("acc", "db", f"m64n{BN}k16", dt, "da", None,
-                            first if s == 0 else Lit(1), 0, int(layout == "sw128_mn"))]
+                            scale, 0, int(layout == "sw128_mn"))]
     slab.append(I.WgmmaCommit())
     if not pipelined:
         slab.append(I.WgmmaWait(0))

@@ -37,9 +37,17 @@ keeps the statements' meaning on that machine:
   kernel that uses these statements, and ``WgmmaFence`` is that fence plus a
   warpgroup barrier.
 
-Limits (exit 1, ``unsupported construct``): an A operand in registers
-(``a_frag``), a one-dimensional CTA of whole warpgroups with every thread a
-cell, at most 512 tensor-memory columns over all warpgroups' accumulators.
+* an A operand in registers (``a_frag``: the warp's 16 rows of the 64 x 16
+  A tile as an m16n8k16 A fragment, bf16 or f16) is written by the
+  warpgroup into a 2 KiB shared-memory slot in the unswizzled K-major layout
+  (8x8 core matrices, LBO 128 B along K, SBO 256 B along M) and read through
+  a descriptor; the slot is reused only after the product that read it has
+  completed (its own commit and bounded wait), so such products run one at a
+  time.
+
+Limits (exit 1, ``unsupported construct``): a one-dimensional CTA of whole
+warpgroups with every thread a cell; at most 512 tensor-memory columns over
+all warpgroups' accumulators; a register A operand of tf32.
 """
 from __future__ import annotations
 
@@ -115,9 +123,12 @@ class WgmmaLowering:
                                       "with every thread a cell")
         widths: dict = {}
         cfr: dict = {}
+        areg = False
         for s in muls:
             if getattr(s, "a_frag", None):
-                raise NotImplementedError("wgmma with its A operand in registers (a_frag)")
+                areg = True
+                if _wg_shape(s.shape)[2] != 16:
+                    raise NotImplementedError("wgmma register A operand of tf32")
             n = _wg_shape(s.shape)[1]
             key = _key(s.c_frags)
             cfr[key] = s.c_frags
@@ -134,7 +145,9 @@ class WgmmaLowering:
             ncols *= 2
         if ncols > 512:
             raise NotImplementedError(f"wgmma accumulators need {need} tensor-memory columns")
-        k.decl(f".shared .align 8 .b8 __emmy_wg_bar[{8 * RING * nwg}];")
+        k.decl(f".shared .align 8 .b8 __emmy_wg_bar[{8 * (RING + 1) * nwg}];")
+        if areg:
+            k.decl(f".shared .align 128 .b8 __emmy_wg_astage[{2048 * nwg}];")
         k.decl(".shared .align 4 .b8 __emmy_wg_tmem[4];")
         tid, warp = self.tid_x, self.ints["warp"]
         bb = k.reg("r")
@@ -143,7 +156,7 @@ class WgmmaLowering:
         k(f"setp.eq.u32 {p0}, {tid}, 0;")
         skip = k.label("WG_INIT")
         k(f"@!{p0} bra {skip};")
-        for i in range(RING * nwg):
+        for i in range((RING + 1) * nwg):
             k(f"mbarrier.init.shared::cta.b64 [{bb}+{8 * i}], 1;")
         k("fence.mbarrier_init.release.cluster;")
         k.mark(skip)
@@ -169,8 +182,8 @@ class WgmmaLowering:
         k(f"and.b32 {lb}, {warp}, 3;")
         k(f"shl.b32 {lb}, {lb}, 21;")
         k(f"add.s32 {lb}, {lb}, {mytm};")
-        bars = k.reg("r")
-        k(f"mad.lo.s32 {bars}, {wg}, {8 * RING}, {bb};")
+        bars = k.reg("r")                    # RING group barriers, then the A-slot barrier
+        k(f"mad.lo.s32 {bars}, {wg}, {8 * (RING + 1)}, {bb};")
         bid = k.reg("r")
         k(f"add.s32 {bid}, {wg}, 8;")
         el = k.reg("p")
@@ -178,15 +191,21 @@ class WgmmaLowering:
         k(f"and.b32 {t7}, {tid}, 127;")
         k(f"setp.eq.u32 {el}, {t7}, 0;")
         c, w, unc = k.reg("r"), k.reg("r"), k.reg("r")
-        for r in (c, w, unc):
+        abusy, aph = k.reg("r"), k.reg("r")
+        for r in (c, w, unc, abusy, aph):
             k(f"mov.u32 {r}, 0;")
+        astage = None
+        if areg:
+            astage = k.reg("r")
+            k(f"mov.u32 {astage}, __emmy_wg_astage;")
+            k(f"mad.lo.s32 {astage}, {wg}, 2048, {astage};")
         auth = {}
         for key in widths:
             auth[key] = k.reg("r")
             k(f"mov.u32 {auth[key]}, 1;")
         self._wg = {"tm": tm, "mytm": mytm, "lb": lb, "bars": bars, "bid": bid, "el": el,
                     "c": c, "w": w, "unc": unc, "auth": auth, "offs": offs, "ncols": ncols,
-                    "cfr": cfr}
+                    "cfr": cfr, "abusy": abusy, "aph": aph, "astage": astage}
         self.wg_descs = {}
 
     def _wg_end(self):
@@ -195,6 +214,8 @@ class WgmmaLowering:
             return
         k = self.k
         self._wg_wait_all()
+        if wg["astage"] is not None:
+            self._wg_slot_free()
         k("tcgen05.fence::before_thread_sync;")
         k("bar.sync 0;")
         k("tcgen05.fence::after_thread_sync;")
@@ -231,6 +252,48 @@ class WgmmaLowering:
         k(f"and.b32 {par}, {par}, 1;")
         self.bounded_parity_wait(a, par)
         k(f"add.u32 {wg['w']}, {wg['w']}, 1;")
+
+    def _wg_slot_free(self):
+        """Wait (bounded) for the product that last read the A slot."""
+        wg, k = self._wg, self.k
+        pb = k.reg("p")
+        k(f"setp.ne.u32 {pb}, {wg['abusy']}, 0;")
+        skip = k.label("WG_SLOT")
+        k(f"@!{pb} bra {skip};")
+        a = k.reg("r")
+        k(f"add.s32 {a}, {wg['bars']}, {8 * RING};")
+        self.bounded_parity_wait(a, wg["aph"])
+        k(f"xor.b32 {wg['aph']}, {wg['aph']}, 1;")
+        k(f"mov.u32 {wg['abusy']}, 0;")
+        k.mark(skip)
+        k("tcgen05.fence::after_thread_sync;")
+
+    def _wg_stage_a(self, ref):
+        """The warp's A fragment (rows 16 w.., 16 k) into the A slot, K-major
+        without swizzle: element (m, k) at (m/8)*256 + (k/8)*128 + (m%8)*16 +
+        (k%8)*2 bytes.  Returns the slot's descriptor."""
+        wg, k = self._wg, self.k
+        f, regs = self._ref(ref)
+        if f.role != "a" or f.dt not in ("bf16", "f16") or f.shape[2] != 16:
+            raise NotImplementedError("wgmma a_frag must be a 16-bit m16n8k16 A fragment")
+        self._wg_slot_free()
+        g, t = self._lane_gt()
+        w4 = k.reg("r")
+        k(f"and.b32 {w4}, {self.ints['warp']}, 3;")
+        # rows 16 w4 + g (+8), k = 2t (+8): byte = (2 w4 + h) * 256 + kh * 128 + g * 16 + t * 4
+        base = k.reg("r")
+        k(f"mad.lo.s32 {base}, {w4}, 512, {wg['astage']};")
+        k(f"mad.lo.s32 {base}, {g}, 16, {base};")
+        k(f"mad.lo.s32 {base}, {t}, 4, {base};")
+        for r, (dh, kh) in zip(regs, [(0, 0), (1, 0), (0, 1), (1, 1)]):
+            k(f"st.shared.b32 [{base}+{dh * 256 + kh * 128}], {r};")
+        k("fence.proxy.async.shared::cta;")
+        d = k.reg("rd")
+        k(f"cvt.u64.u32 {d}, {wg['astage']};")
+        k(f"shr.u64 {d}, {d}, 4;")
+        k(f"and.b64 {d}, {d}, 16383;")
+        k(f"or.b64 {d}, {d}, {desc_hi(128, 256, 0)};")
+        return d
 
     def _wg_commit(self):
         wg, k = self._wg, self.k
@@ -317,9 +380,13 @@ class WgmmaLowering:
         ab = {"bfloat16": "bf16", "float16": "f16"}.get(str(ab), str(ab))
         if ab not in _FMT or (ab == "tf32") != (K == 8):
             raise NotImplementedError(f"wgmma {ab} k{K}")
-        for nm in (s.a_desc, s.b_desc):
+        areg = bool(getattr(s, "a_frag", None))
+        for nm in ((s.b_desc,) if areg else (s.a_desc, s.b_desc)):
             if nm not in self.wg_descs:
                 raise NotImplementedError(f"wgmma operand descriptor {nm!r} not built")
+        if areg and (s.trans_a or ab == "tf32"):
+            raise NotImplementedError("wgmma register A operand: 16-bit, K-major")
+        adesc = self._wg_stage_a(s.a_frag) if areg else self.wg_descs[s.a_desc]
         auth = wg["auth"][key]
         # the registers are the current accumulator: write them to tensor memory
         pa = k.reg("p")
@@ -349,9 +416,16 @@ class WgmmaLowering:
         skip2 = k.label("WG_ISSUE")
         k(f"@!{wg['el']} bra {skip2};")
         kd = "tf32" if ab == "tf32" else "f16"
-        k(f"tcgen05.mma.cta_group::1.kind::{kd} [{d}], {self.wg_descs[s.a_desc]}, "
+        k(f"tcgen05.mma.cta_group::1.kind::{kd} [{d}], {adesc}, "
           f"{self.wg_descs[s.b_desc]}, {idx}, {ps};")
+        if areg:
+            # the slot is free again once this product completes
+            sa = k.reg("r")
+            k(f"add.s32 {sa}, {wg['bars']}, {8 * RING};")
+            k(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{sa}];")
         k.mark(skip2)
+        if areg:
+            k(f"mov.u32 {wg['abusy']}, 1;")
         k(f"mov.u32 {auth}, 0;")
         k(f"mov.u32 {wg['unc']}, 1;")
 

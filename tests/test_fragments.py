@@ -21,6 +21,7 @@ CASES = {
     "smem": dict(), "smem_nk": dict(b_kn=False), "direct": dict(stage=False),
     "f16_promote": dict(dtype="f16", promote=True), "tf32": dict(dtype="tf32"),
     "epilogue_bf16": dict(epilogue=True, out_dtype="bf16"), "split_k": dict(split_k=3, K=200),
+    "swizzled": dict(swizzle=True),
 }
 
 
@@ -78,8 +79,9 @@ def test_oracle_tf32_rounding():
 
 
 @pytest.mark.parametrize("kw", [dict(), dict(layout="sw128_mn", BN=128), dict(layout="none"),
-                                dict(pipelined=True), dict(warpgroups=2, BN=128)],
-                         ids=["sw128", "sw128_mn", "none", "pipelined", "wg2"])
+                                dict(pipelined=True), dict(warpgroups=2, BN=128),
+                                dict(a_regs=True)],
+                         ids=["sw128", "sw128_mn", "none", "pipelined", "wg2", "a_regs"])
 def test_wgmma_compiles(kw):
     """wgmma on sm_100a: tcgen05.mma M = 64 into tensor memory, 16x256b
     loads and stores of the C fragments, TMEM freed at the end; the static
@@ -97,10 +99,10 @@ def test_wgmma_compiles(kw):
         assert r.returncode == 0, r.stderr
 
 
-def test_wgmma_register_a_is_exit_1(tmp_path):
-    """An A operand in registers (a_frag) is not lowered: exit 1."""
-    g, m = synth.wgmma_matmul().build()
+def test_wgmma_tf32_register_a_is_exit_1(tmp_path):
+    """A register A operand of tf32 has no staged form here: exit 1."""
+    g, m = synth.wgmma_matmul(a_regs=True).build()
     body = g["nodes"]["c"]["op_fields"]["body"][0]
-    g["nodes"]["c"]["op_fields"]["body"][0] = body.replace("a_frag=None", "a_frag='acc'", 1)
+    g["nodes"]["c"]["op_fields"]["body"][0] = body.replace("m64n64k16", "m64n64k8")
     r = _cli(tmp_path, g, m)
-    assert r.returncode == 1 and "a_frag" in r.stderr
+    assert r.returncode == 1 and r.stderr.startswith("unsupported construct:")

@@ -39,11 +39,14 @@ def _run(p):
     dict(M=256, N=192, K=128), dict(M=1, N=5, K=7, stage=False),
     dict(dtype="f16"), dict(dtype="f16", promote=True),
     dict(dtype="tf32"), dict(dtype="tf32", stage=False, b_kn=False),
-    dict(epilogue=True), dict(epilogue=True, out_dtype="bf16"), dict(split_k=3, K=200)],
+    dict(epilogue=True), dict(epilogue=True, out_dtype="bf16"), dict(split_k=3, K=200),
+    dict(swizzle=True), dict(swizzle=True, b_kn=False, K=200)],
     ids=["smem", "smem_nk", "direct", "direct_nk", "aligned", "tiny", "f16", "f16_promote",
-         "tf32", "tf32_direct_nk", "epilogue", "epilogue_bf16", "split_k"])
+         "tf32", "tf32_direct_nk", "epilogue", "epilogue_bf16", "split_k", "swizzled",
+         "swizzled_nk"])
 def test_mma_matmul(kw):
-    """ldmatrix (plain and .trans) and guarded element loads, bf16 / f16 /
+    """ldmatrix (plain and .trans, unswizzled and through the 128-byte chunk
+    swizzle) and guarded element loads, bf16 / f16 /
     tf32 mma.sync, f16 accumulators promoted into f32, the store's Lambda
     epilogue, bf16 stores, atomic split-K stores; ragged 200 x 136 x 80 by
     default (edge tiles cut by the guards)."""
@@ -62,13 +65,15 @@ def test_mma_attention(kw):
 
 @pytest.mark.parametrize("kw", [dict(), dict(layout="sw128_mn", BN=128), dict(layout="none"),
                                 dict(pipelined=True), dict(warpgroups=2, BN=128),
-                                dict(dtype="f16", M=128, N=64, K=64)],
+                                dict(dtype="f16", M=128, N=64, K=64), dict(a_regs=True),
+                                dict(a_regs=True, warpgroups=2, BN=128, layout="sw128_mn")],
                          ids=["sw128", "sw128_mn", "no_swizzle", "pipelined", "two_warpgroups",
-                              "f16_aligned"])
+                              "f16_aligned", "a_in_registers", "a_in_registers_wg2_mn"])
 def test_wgmma_matmul(kw):
     """The warpgroup statements on tcgen05: M = 64 accumulators in tensor
     memory read back into the warps' C fragments, K-major and MN-major
     128-byte-swizzled and unswizzled descriptors, a commit per slab with
     WgmmaWait(1) over two slab buffers, two warpgroups a CTA (their own
-    accumulator columns and barriers), ragged 200 x 136 x 200 by default."""
+    accumulator columns and barriers), the A operand from registers (staged
+    through the unswizzled K-major slot), ragged 200 x 136 x 200 by default."""
     _run(synth.wgmma_matmul(**kw))
