@@ -560,10 +560,12 @@ def emit_pair_persistent(t) -> str:
         k(f"add.u32 {ctl}, {ctl}, {ABASE};")
         chunk = []                                # byte offset of K chunk c in the row
         for c in range(BK * 4 // 16):
-            o = k.reg("r")
-            k(f"xor.b32 {o}, {rsw}, {c};")
-            k(f"shl.b32 {o}, {o}, 4;")
-            k(f"add.u32 {o}, {o}, {roff};")
+            # fresh registers (no in-place update), so the static race
+            # checker resolves the converters' shared-memory addresses
+            x, sh, o = k.reg("r"), k.reg("r"), k.reg("r")
+            k(f"xor.b32 {x}, {rsw}, {c};")
+            k(f"shl.b32 {sh}, {x}, 4;")
+            k(f"add.u32 {o}, {sh}, {roff};")
             chunk.append(o)
         k(f"mov.u32 {st}, 0;")
         k(f"mov.u32 {ph}, 0;")
@@ -629,9 +631,9 @@ def emit_pair_persistent(t) -> str:
         k.mark(bk)
         GemmTemplate._wait(k, bar_addr(0, st), ph, status, 4, teardown)
         sbb = stage_base(st)
-        b0 = k.reg("r")
-        k(f"add.u32 {b0}, {sbb}, {SA};")
-        k(f"add.u32 {b0}, {b0}, {boff};")
+        b1, b0 = k.reg("r"), k.reg("r")
+        k(f"add.u32 {b1}, {sbb}, {SA};")
+        k(f"add.u32 {b0}, {b1}, {boff};")
         for i in range(NVB // CTB):
             x = k.regs("r", 4)
             ad = f"{b0}+{i * 16 * CTB}" if i else b0
