@@ -25,7 +25,8 @@ headline, N=1 times every other category at its BASELINE size (``categories``,
 each with a bounded CPU baseline); N>1 times every configuration as strong
 scaling of the BASELINE problem (``shards``: rows, element chunks, CTA slices
 of the full sum finished by the all-reduce -- and again by ``peer.PeerSum``,
-the same finish over NVLink peer memory without NCCL -- 256-row bands of
+the same finish over NVLink peer memory without NCCL, and by the sum kernel
+itself, whose last CTA runs that exchange (one kernel a rank) -- 256-row bands of
 matmul, (batch, head) pairs of attention).  Inputs smaller than twice the L2
 are flushed between launches (a 512 MiB write whose lines are then discarded
 from L2).
@@ -761,26 +762,34 @@ def run_shards(rank: int, world: int, dev) -> dict:
                                "(output reset, sum kernel and all-reduce replayed as one CUDA graph)")
             if world > 1:
                 d["nvlink_finish"] = peer_finish_shard(kw, world, rank, dev, hbm)
+                d["fused_finish"] = peer_finish_shard(kw, world, rank, dev, hbm, fused=True)
         shards[nm] = d
     return shards
 
 
-def peer_finish_shard(kw: dict, world: int, rank: int, dev, hbm: float) -> dict:
+def peer_finish_shard(kw: dict, world: int, rank: int, dev, hbm: float,
+                      fused: bool = False) -> dict:
     """The strong-scaled full sum with its cross-GPU step done by
     ``peer.PeerSum`` (partials written into every peer's memory over NVLink,
-    no collective library), timed and checked like the NCCL form."""
+    no collective library), timed and checked like the NCCL form; ``fused``:
+    the exchange runs inside the sum kernel (its last CTA), one kernel a
+    rank."""
     from emmy_b200 import dist as D
     from emmy_b200 import synth
     try:
-        r = measure_full_sum_strong(kw, 20, 3, dev, rank, exchange="nvlink")
+        r = measure_full_sum_strong(kw, 20, 3, dev, rank,
+                                    exchange="fused" if fused else "nvlink")
         ms_r, ok_r, err = r["ms_median"], bool(r["check"]["ok"]), None
     except Exception as e:  # every rank still joins the reductions below
         r, ms_r, ok_r, err = None, float("inf"), False, f"{type(e).__name__}: {e}"[:300]
     ms_all = D.max_over_ranks(ms_r, device=dev)
     ok_all = D.max_over_ranks(0.0 if ok_r else 1.0, device=dev) == 0.0
-    d = {"exchange": "peer.PeerSum: each rank's partial stored into every rank's slot over "
-                     "NVLink (CUDA IPC mappings), one polling kernel per rank, summed in rank "
-                     "order; replayed with the sum kernel as one CUDA graph",
+    d = {"exchange": ("the sum kernel's last CTA stores the rank's partial into every rank's "
+                      "slot over NVLink (CUDA IPC mappings), polls its own slots and sums them "
+                      "in rank order: sum and cross-GPU finish in one kernel a rank" if fused else
+                      "peer.PeerSum: each rank's partial stored into every rank's slot over "
+                      "NVLink (CUDA IPC mappings), one polling kernel per rank, summed in rank "
+                      "order; replayed with the sum kernel as one CUDA graph"),
          "ms_max_over_ranks": round(ms_all, 5) if ok_all else None,
          "check": {"checked": True, "ok_all_ranks": ok_all,
                    "status": r["check"]["status"] if r else None}}
@@ -808,15 +817,17 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int,
     from emmy_b200 import dist as D
     from emmy_b200 import harness, native, synth
     p = synth.config("full_sum", **kw)
-    kern = harness.CompiledKernel(*p.build())
+    g, m = p.build()
+    if exchange == "fused":
+        m["kernels"][0]["peer_finish"] = True
+    kern = harness.CompiledKernel(g, m)
     bufs = harness.Buffers.random(kern, seed=rank)
     stream = torch.cuda.current_stream()
     out = bufs.t["sum_1"]
     L = native.lib()
     k = kern.kernel()
-    arr, keep = kern.params(bufs.ptrs())
     ps = None
-    if exchange == "nvlink":
+    if exchange in ("nvlink", "fused"):
         from emmy_b200 import peer
         world = D.from_env().world
         try:
@@ -832,15 +843,19 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int,
             else:
                 D.barrier()
             raise RuntimeError("peer memory could not be mapped on every rank")
+    ptrs = bufs.ptrs()
+    if exchange == "fused":
+        ptrs.update(ps.fused_values())
+    arr, keep = kern.params(ptrs)
 
     def step():
         sh = torch.cuda.current_stream().cuda_stream
         native.check(L.emmy_memset_async(out.data_ptr(), 0, 4, sh))
         native.check(L.emmy_launch(k.h, native.u32x3(kern.grid), native.u32x3(kern.block),
                                    kern.smem, kern._cluster_arg(), arr, sh))
-        if ps is not None:
+        if exchange == "nvlink":
             ps.launch(out.data_ptr(), sh)
-        else:
+        elif exchange == "nccl":
             D.global_sum(out)
 
     for _ in range(warmup):
@@ -867,8 +882,11 @@ def measure_full_sum_strong(kw: dict, steps: int, warmup: int, dev, rank: int,
     del graph
     torch.cuda.synchronize()
     status = None
+    if exchange == "fused":
+        status = read_status(kern)
     if ps is not None:
-        status = ps.status()
+        if exchange == "nvlink":
+            status = ps.status()
         D.barrier()                  # every rank's kernels are done before unmapping
         ps.close(barrier=D.barrier)
     got = float(out.item())

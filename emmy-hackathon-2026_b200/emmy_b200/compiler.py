@@ -80,6 +80,9 @@ class Compiler:
             from .generic import GenericLowering
             self.template = GenericLowering(self.ctx)
             self.ptx = self.template.emit()
+        if self.ctx.info.get("peer_finish") and "// @emmy peer" not in self.ptx:
+            raise NotImplementedError("peer_finish: only the split full sum (rows template) "
+                                      "finishes the global sum in the kernel")
         return self
 
     def render(self) -> str:

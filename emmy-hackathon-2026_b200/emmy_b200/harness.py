@@ -69,6 +69,15 @@ def parse_tmaps(ptx: str) -> list:
     return out
 
 
+def parse_peer(ptx: str) -> list:
+    """The trailing cross-GPU parameters a fused full sum declares
+    (``// @emmy peer <names>``), in order; none for every other kernel."""
+    for line in ptx.splitlines():
+        if line.startswith("// @emmy peer "):
+            return line.split()[3:]
+    return []
+
+
 def parse_cluster(ptx: str):
     m = _CLUSTER_RE.search(ptx)
     return tuple(int(x) for x in m.groups()) if m else None
@@ -88,6 +97,7 @@ class CompiledKernel:
         self.image = native.Image(self.ptx, arch)
         self.tmaps = parse_tmaps(self.ptx)
         self.cluster = parse_cluster(self.ptx)
+        self.peer_params = parse_peer(self.ptx)
         self._module = None
         self._kernel = None
 
@@ -112,6 +122,7 @@ class CompiledKernel:
         self.image = native.Image(ptx, arch)
         self.tmaps = parse_tmaps(ptx)
         self.cluster = parse_cluster(ptx)
+        self.peer_params = parse_peer(ptx)
         self._module = None
         self._kernel = None
         return self
@@ -159,6 +170,12 @@ class CompiledKernel:
                      "u16": ctypes.c_uint16}.get(ty, ctypes.c_uint32)(v)
             else:
                 c = ctypes.c_uint64(int(ptrs[a]))
+            keep.append(c)
+            vals.append(ctypes.cast(ctypes.pointer(c), ctypes.c_void_p))
+        for name in self.peer_params:
+            # the fused full sum's cross-GPU parameters (peer.FUSED_PARAMS)
+            c = (ctypes.c_uint64 if name in ("peer_table", "peer_local") else ctypes.c_uint32)(
+                int(ptrs[name]))
             keep.append(c)
             vals.append(ctypes.cast(ctypes.pointer(c), ctypes.c_void_p))
         for t in self.tmaps:

@@ -27,6 +27,10 @@ single-thread kernel per rank:
   code 9 in the module's ``__emmy_status`` word and returns, leaving the
   partial and the epoch as they were.
 
+The same exchange also runs inside the split full-sum kernel itself
+(:func:`emit_fused_finish`, the kernel's last CTA): one kernel per rank does
+the sum and the cross-GPU finish.
+
 The kernels of different ranks wait on one another, so they must run on
 different GPUs at the same time: one process per GPU, as the benchmark runs.
 """
@@ -119,6 +123,122 @@ DONE:
 """
 
 
+# the fused form: a full-sum kernel compiled with ``"peer_finish": true`` in
+# its meta launch descriptor takes these four parameters after meta
+# arg_order (``// @emmy peer`` in its PTX) and finishes the global sum itself
+FUSED_PARAMS = [("peer_table", "u64"), ("peer_local", "u64"), ("peer_rank", "u32"),
+                ("peer_world", "u32")]
+
+
+def emit_fused_finish(k, sum_addr: str, ncta: int, status: str, done_sym: str) -> None:
+    """The cross-GPU finish inside the split full-sum kernel itself, emitted
+    after thread 0 of a CTA has added the CTA's partial into ``sum_addr`` (a
+    global address register): a release fence and one atomic on the
+    module's completion counter ``done_sym`` find the launch's last CTA,
+    which (after an acquire fence) reads the rank's complete partial, resets
+    the counter for the next launch, and runs the exchange of the
+    single-thread ``emmy_peer_sum`` kernel -- its partial packed with the
+    epoch into every rank's slot (``st.release.sys``), its own slots polled
+    (``ld.acquire.sys``, bounded by ``WAIT_NS``; ``STATUS_TIMEOUT`` into
+    ``status`` on expiry) and summed in rank order over ``sum_addr``.  The
+    other CTAs leave as soon as they have counted themselves, so the partial
+    is final when the exchange starts and no CTA waits on another GPU but
+    the last."""
+    done = k.label("PEER_DONE")
+    old = k.reg("r")
+    k("fence.acq_rel.gpu;")
+    k(f"atom.global.add.u32 {old}, [{done_sym}], 1;")
+    p = k.reg("p")
+    k(f"setp.ne.u32 {p}, {old}, {ncta - 1};")
+    k(f"@{p} bra {done};")
+    k("fence.acq_rel.gpu;")
+    part = k.reg("f")
+    k(f"ld.relaxed.gpu.global.f32 {part}, [{sum_addr}];")
+    k(f"st.relaxed.gpu.global.u32 [{done_sym}], 0;")
+    peers, local = k.reg("rd"), k.reg("rd")
+    rank, world = k.reg("r"), k.reg("r")
+    k(f"ld.param.u64 {peers}, [param_peer_table];")
+    k(f"ld.param.u64 {local}, [param_peer_local];")
+    k(f"ld.param.u32 {rank}, [param_peer_rank];")
+    k(f"ld.param.u32 {world}, [param_peer_world];")
+    # this launch's epoch: the local epoch word (after both slot sets) + 1
+    eoff = k.reg("rd")
+    k(f"mul.wide.u32 {eoff}, {world}, {2 * SLOT};")
+    eaddr = k.reg("rd")
+    k(f"add.s64 {eaddr}, {local}, {eoff};")
+    ep = k.reg("r")
+    k(f"ld.global.u32 {ep}, [{eaddr}];")
+    k(f"add.u32 {ep}, {ep}, 1;")
+    # the epoch's slot set, this rank's word (value low, epoch high)
+    set0 = k.reg("r")
+    k(f"and.b32 {set0}, {ep}, 1;")
+    k(f"mul.lo.u32 {set0}, {set0}, {world};")
+    vb = k.reg("r")
+    k(f"mov.b32 {vb}, {part};")
+    word = k.reg("rd")
+    k(f"mov.b64 {word}, {{{vb}, {ep}}};")
+    mine = k.reg("r")
+    k(f"add.u32 {mine}, {set0}, {rank};")
+    moff = k.reg("rd")
+    k(f"mul.wide.u32 {moff}, {mine}, {SLOT};")
+    i = k.reg("r")
+    k(f"mov.u32 {i}, 0;")
+    put = k.label("PEER_PUT")
+    k.mark(put)
+    pa = k.reg("rd")
+    k(f"mul.wide.u32 {pa}, {i}, 8;")
+    k(f"add.s64 {pa}, {peers}, {pa};")
+    base = k.reg("rd")
+    k(f"ld.global.u64 {base}, [{pa}];")
+    dst = k.reg("rd")
+    k(f"add.s64 {dst}, {base}, {moff};")
+    k(f"st.release.sys.global.u64 [{dst}], {word};")
+    k(f"add.u32 {i}, {i}, 1;")
+    pl = k.reg("p")
+    k(f"setp.lt.u32 {pl}, {i}, {world};")
+    k(f"@{pl} bra {put};")
+    # every rank's word of this epoch, summed in rank order
+    acc = k.reg("f")
+    k(f"mov.f32 {acc}, 0f00000000;")
+    t0 = k.reg("rd")
+    k(f"mov.u64 {t0}, %globaltimer;")
+    k(f"mov.u32 {i}, 0;")
+    get, spin, got = k.label("PEER_GET"), k.label("PEER_SPIN"), k.label("PEER_GOT")
+    k.mark(get)
+    sl = k.reg("r")
+    k(f"add.u32 {sl}, {set0}, {i};")
+    sa = k.reg("rd")
+    k(f"mul.wide.u32 {sa}, {sl}, {SLOT};")
+    k(f"add.s64 {sa}, {local}, {sa};")
+    k.mark(spin)
+    w = k.reg("rd")
+    k(f"ld.acquire.sys.global.u64 {w}, [{sa}];")
+    lo, hi = k.reg("r"), k.reg("r")
+    k(f"mov.b64 {{{lo}, {hi}}}, {w};")
+    pe = k.reg("p")
+    k(f"setp.eq.u32 {pe}, {hi}, {ep};")
+    k(f"@{pe} bra {got};")
+    t1 = k.reg("rd")
+    k(f"mov.u64 {t1}, %globaltimer;")
+    k(f"sub.s64 {t1}, {t1}, {t0};")
+    pt = k.reg("p")
+    k(f"setp.lt.s64 {pt}, {t1}, {WAIT_NS};")
+    k(f"@{pt} bra {spin};")
+    k(f"st.global.u32 [{status}], {STATUS_TIMEOUT};")
+    k(f"bra {done};")
+    k.mark(got)
+    v = k.reg("f")
+    k(f"mov.b32 {v}, {lo};")
+    k(f"add.rn.f32 {acc}, {acc}, {v};")
+    k(f"add.u32 {i}, {i}, 1;")
+    pg = k.reg("p")
+    k(f"setp.lt.u32 {pg}, {i}, {world};")
+    k(f"@{pg} bra {get};")
+    k(f"st.global.f32 [{sum_addr}], {acc};")
+    k(f"st.global.u32 [{eaddr}], {ep};")
+    k.mark(done)
+
+
 def exchange_handles(handle: bytes, world: int) -> list:
     """Every rank's 64-byte handle, in rank order (through the process
     group; a one-process job has only its own)."""
@@ -185,6 +305,13 @@ class PeerSum:
         native.check(L.emmy_memcpy_dtoh_async(ctypes.addressof(v), addr, 4, None))
         native.check(L.emmy_stream_sync(None))
         return v.value
+
+    def fused_values(self) -> dict:
+        """The values of ``FUSED_PARAMS`` for a fused full-sum kernel's launch
+        (keyed by parameter name, as ``harness.CompiledKernel.params`` takes
+        them beside the meta arguments)."""
+        return {"peer_table": self.peer_table, "peer_local": self.local,
+                "peer_rank": self.rank, "peer_world": self.world}
 
     def launch(self, sum_ptr: int, stream) -> None:
         L = native.lib()

@@ -40,6 +40,10 @@ WORKERS = 74                 # clusters of 2 CTAs: the 148 SMs of a B200
 PERSISTENT_MIN_STAGES = 4    # 4 x 32 KiB ring: one CTA per SM
 EPI_CHUNK = 16               # accumulator columns per tcgen05.ld in the epilogue
 GROUP_M = 16                 # 256-row bands per raster group (tiles run down a group's bands)
+# 3xTF32 operands are twice as wide: 8 bands a group read 1.12 GB from DRAM at
+# M=N=8192, K=4096 against 1.27 GB with 16 and 1.45 GB with 4 (ncu, same
+# call), at 278.7 / 278.4 / 274.4 TFLOP/s on the BASELINE shape
+GROUP_M_TF32 = 8
 TAIL_SPLIT = True            # leftover pair tiles of a partial last round run as 256 x 128 halves
 # 3xTF32: the A operand's raw (high) and low parts in tensor memory instead of
 # shared memory (tcgen05.mma's [a-tmem] form), one accumulator instead of two.
@@ -278,7 +282,7 @@ def emit_pair_persistent(t) -> str:
         """(m0 of this CTA, n0 of the pair tile, this CTA's B columns, the
         half-tile predicate) for this cluster's tile iteration ``idx``."""
         tt, ph_, hoff = tile_index(k, idx, clus, W, NF, HALF)
-        mp, nbk = raster(k, tt, MB, NB)
+        mp, nbk = raster(k, tt, MB, NB, GROUP_M_TF32 if tf32 else None)
         m0 = k.reg("r")
         k(f"mad.lo.u32 {m0}, {mp}, 2, {rank};")
         k(f"mul.lo.u32 {m0}, {m0}, {BM};")

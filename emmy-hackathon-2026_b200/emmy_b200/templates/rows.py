@@ -37,6 +37,8 @@ columns); reductions are checked at the problems' relative tolerance.
 """
 from __future__ import annotations
 
+from math import prod
+
 from ..analysis import NotAffine, affine, cond_var_eq, flat_index, kind
 from ..ir import dim
 from ..ops import emit_op_f32
@@ -330,7 +332,23 @@ class RowsTemplate:
     # ------------------------------------------------------------------- emit
     def emit(self) -> str:
         ctx = self.ctx
-        k = self.k = Kernel(ctx.entry, ctx.params())
+        # a full-sum kernel that also finishes the global sum across GPUs
+        # (meta "peer_finish": true; the multi-GPU path's own launch
+        # descriptor): four parameters after meta arg_order
+        self.peer = bool(ctx.info.get("peer_finish"))
+        params = ctx.params()
+        if self.peer:
+            from ..peer import FUSED_PARAMS
+            w = self.red_write[0] if self.reduce_tail is not None else None
+            if w is None or not w.atomic or self.red_write[1].as_dict():
+                raise NotImplementedError("peer_finish: only the split full sum (one atomic "
+                                          "add of a scalar per CTA)")
+            params = params + FUSED_PARAMS
+        k = self.k = Kernel(ctx.entry, params)
+        if self.peer:
+            k.directive("peer " + " ".join(n for n, _ in FUSED_PARAMS))
+            k.decl(".global .align 4 .u32 __emmy_done;")
+            k.decl(".global .align 4 .u32 __emmy_status;")
         k.comment(f"emmy-b200 template: rows R={self.R} L={self.L} B={self.B} "
                   f"V={self.V} J={self.J} {'fused' if self.loop2 else 'reduce'}")
         self.base = {a: k.param_ptr(a) for a in ctx.arg_order}
@@ -614,6 +632,11 @@ class RowsTemplate:
             k(f"red.global.add.f32 [{a}], {v};")
         else:
             k(f"st.global.f32 [{a}], {v};")
+        if self.peer:
+            from ..peer import emit_fused_finish
+            st = k.reg("rd")
+            k(f"mov.u64 {st}, __emmy_status;")
+            emit_fused_finish(k, a, prod(self.ctx.grid), st, "__emmy_done")
         k.mark(done)
 
     def _pass2(self, chain, env, kept):

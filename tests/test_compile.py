@@ -489,3 +489,25 @@ def test_vocabulary_nodes_lower(native_lib):
                                                            ("v",))])
     with pytest.raises(NotImplementedError):
         compile_graph(*p.build()).render()
+
+
+def test_fused_full_sum_variant():
+    """``peer_finish`` in the launch descriptor: the split full sum takes the
+    four cross-GPU parameters after meta arg_order, declares them in its
+    ``// @emmy peer`` line, and passes the static checks; any other kernel
+    refuses the request (exit 1) instead of ignoring it."""
+    from emmy_b200 import peer, ptxcheck
+    from emmy_b200.harness import parse_peer
+    g, m = synth.config("full_sum", n=1 << 20, ctas=64).build()
+    m["kernels"][0]["peer_finish"] = True
+    c = compile_graph(g, m)
+    assert c.kind == "rows"
+    assert parse_peer(c.ptx) == [n for n, _ in peer.FUSED_PARAMS]
+    for n, ty in peer.FUSED_PARAMS:
+        assert f".param .{ty} param_{n}" in c.ptx
+    assert "st.release.sys.global.u64" in c.ptx and "ld.acquire.sys.global.u64" in c.ptx
+    assert ptxcheck.check(c.ptx) == []
+    g, m = synth.config("row_sum", rows=64, cols=2048).build()
+    m["kernels"][0]["peer_finish"] = True
+    with pytest.raises(NotImplementedError):
+        compile_graph(g, m)
