@@ -106,3 +106,25 @@ def test_wgmma_tf32_register_a_is_exit_1(tmp_path):
     g["nodes"]["c"]["op_fields"]["body"][0] = body.replace("m64n64k16", "m64n64k8")
     r = _cli(tmp_path, g, m)
     assert r.returncode == 1 and r.stderr.startswith("unsupported construct:")
+
+
+@pytest.mark.parametrize("role,kk,cls,rows,cols", [
+    ("a", 16, "wide", 16, 16), ("a", 8, "wide", 16, 8), ("a", 8, "tf32", 16, 8),
+    ("b", 16, "wide", 16, 8), ("b", 8, "wide", 8, 8), ("b", 8, "tf32", 8, 8),
+    ("c", 16, "f32", 16, 8), ("c", 16, "f16", 16, 8)])
+def test_fragment_layouts_cover_the_tile_once(role, kk, cls, rows, cols):
+    """Every element of an operand tile (A m x k, B k x n, C m x n) is held by
+    exactly one (lane, register, half) of the warp under the mma.sync layouts
+    the fragment statements use."""
+    from emmy_b200.fragments import _LAYOUTS
+    lay = _LAYOUTS[(role, kk, cls)]
+    seen = {}
+    for lane in range(32):
+        g, t = lane >> 2, lane & 3
+        for (reg, half, r, c) in lay:
+            row = r[0] * g + r[1] * t + r[2]
+            col = c[0] * g + c[1] * t + c[2]
+            assert 0 <= row < rows and 0 <= col < cols
+            assert (row, col) not in seen, ((row, col), seen.get((row, col)), (lane, reg, half))
+            seen[(row, col)] = (lane, reg, half)
+    assert len(seen) == rows * cols
