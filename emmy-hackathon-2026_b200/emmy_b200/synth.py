@@ -1133,16 +1133,21 @@ def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout:
     operand in registers -- each warp loads its 16 rows of every 16-wide K
     step as an A fragment straight from global memory (guarded) and passes
     it as ``a_frag``."""
-    dt = {"bf16": BF16, "f16": F16}[dtype]
-    smem_ty = {"bf16": "bfloat16", "f16": "half"}[dtype]
-    BK = 64
+    dt = {"bf16": BF16, "f16": F16, "tf32": F32}[dtype]
+    smem_ty = {"bf16": "bfloat16", "f16": "half", "tf32": "float"}[dtype]
+    es = 4 if dtype == "tf32" else 2           # bytes an element
+    ce = 16 // es                              # elements a 16-byte chunk
+    BK = 128 // es                             # a 128-byte row of K a slab
+    KS = 8 if dtype == "tf32" else 16          # K of one product
+    if dtype == "tf32" and (layout == "sw128_mn" or a_regs):
+        raise ValueError("tf32 operands: K-major shared memory only")
     BM = 64 * warpgroups
     T = 128 * warpgroups
     nbuf = 2 if pipelined else 1
     nk = -(-K // BK)
     p = Problem(f"wgmma_matmul_{layout}_{M}x{N}x{K}", "a @ b", "k_wgmma_matmul", "c")
-    p.add_input("a", (M, K), dtype)
-    p.add_input("b", (K, N), dtype)
+    p.add_input("a", (M, K), "f32" if dtype == "tf32" else dtype)
+    p.add_input("b", (K, N), "f32" if dtype == "tf32" else dtype)
     p.out = ("c", (M, N), "f32")
     t = V("t")
     i32 = I.data_type("i32")
@@ -1150,9 +1155,10 @@ def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout:
 
     def pos_kmajor(r, kk):
         if layout == "none":
-            return add(add(mul(_idiv(r, 8), Lit(512)), mul(_idiv(kk, 8), Lit(64))),
-                       add(mul(_imod(r, 8), Lit(8)), _imod(kk, 8)))
-        return add(mul(r, Lit(64)), add(mul(_xor(_idiv(kk, 8), _imod(r, 8)), Lit(8)), _imod(kk, 8)))
+            return add(add(mul(_idiv(r, 8), Lit(1024 // es)), mul(_idiv(kk, ce), Lit(128 // es))),
+                       add(mul(_imod(r, 8), Lit(ce)), _imod(kk, ce)))
+        return add(mul(r, Lit(BK)), add(mul(_xor(_idiv(kk, ce), _imod(r, 8)), Lit(ce)),
+                                        _imod(kk, ce)))
 
     def pos_mn(kk, n):
         return add(add(mul(_idiv(n, 64), Lit(64 * BK)), mul(kk, Lit(64))),
@@ -1189,8 +1195,8 @@ def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout:
     swz = "NONE" if layout == "none" else "128B"
     a_lbo, a_sbo = (128, 1024) if layout == "none" else (16, 1024)
     b_lbo, b_sbo = ((64 * BK * 2, 1024) if layout == "sw128_mn" else (a_lbo, a_sbo))
-    for s in range(BK // 16):
-        a_step = 128 * s if layout == "none" else 16 * s
+    for s in range(BK // KS):
+        a_step = (KS // ce) * (128 // es) * s if layout == "none" else KS * s
         b_step = 16 * 64 * s if layout == "sw128_mn" else a_step
         a_idx = add(add(mul(V("buf"), Lit(a_sz)), mul(V("wg"), Lit(64 * BK))), Lit(a_step))
         b_idx = add(mul(V("buf"), Lit(b_sz)), Lit(b_step))
@@ -1201,12 +1207,13 @@ def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout:
             slab += [I.LdmatrixLoad("fa", "a", (wrow, add(V("k0"), Lit(16 * s))), "a",
                                     gmem_guard=(Lit(M), None), k_zero=Lit(K)),
                      I.WgmmaDescriptor("db", "Bs", (b_idx,), swz, b_lbo, b_sbo),
-                     I.WgmmaMma("acc", "db", f"m64n{BN}k16", dt, None, "fa", scale, 0,
+                     I.WgmmaMma("acc", "db", f"m64n{BN}k{KS}", dt, None, "fa", scale, 0,
                                 int(layout == "sw128_mn"))]
             continue
         slab += [I.WgmmaDescriptor("da", "As", (a_idx,), swz, a_lbo, a_sbo),
                  I.WgmmaDescriptor("db", "Bs", (b_idx,), swz, b_lbo, b_sbo),
-                 I.WgmmaMma("acc", "db", f"m64n{BN}k16", dt, "da", None,
+                 I.WgmmaMma("acc", "db", f"m64n{BN}k{KS}",
+                            I.data_type("tf32") if dtype == "tf32" else dt, "da", None,
                             scale, 0, int(layout == "sw128_mn"))]
     slab.append(I.WgmmaCommit())
     if not pipelined:
@@ -1220,8 +1227,9 @@ def wgmma_matmul(M: int = 200, N: int = 136, K: int = 200, BN: int = 64, layout:
     gm, gn = -(-M // BM), -(-N // BN)
     p.body = I.Tile((axis("bm", gm), axis("bn", gn), axis("t", T)), tuple(body), T)
     p.grid, p.block = (gm * gn, 1, 1), (T, 1, 1)
-    p.rtol, p.atol = 1e-3, None
+    p.rtol, p.atol = (5e-3 if dtype == "tf32" else 1e-3), None
     p.oracle = {"family": "mma_matmul", "args": {"a": "a", "b": "b", "bias": "bias"},
-                "output": "c", "b_kn": True, "epilogue": False, "tf32": False,
+                "output": "c", "b_kn": True, "epilogue": False,
+                "tf32": "trunc" if dtype == "tf32" else False,
                 "bf16": {"a": dtype == "bf16", "b": dtype == "bf16"}, "out_bf16": False}
     return p

@@ -147,10 +147,11 @@ def mma_matmul(a, b, b_kn=True, bias=None, tf32=False, out_bf16=False):
     """C = A . B (B given [K, N], or [N, K] when not ``b_kn``) in float64,
     then relu(C + bias[col]) when a bias is given, as float32 (bf16-rounded
     when the output buffer is bf16).  tf32 operands: each input rounded to
-    tf32 (10 explicit mantissa bits, round to nearest, ties away) first."""
+    tf32 (10 explicit mantissa bits, round to nearest, ties away; or
+    truncated when ``tf32 == "trunc"``) first."""
     a, b = _d(a), _d(b)
     if tf32:
-        a, b = _tf32(a), _tf32(b)
+        a, b = _tf32(a, tf32 == "trunc"), _tf32(b, tf32 == "trunc")
     c = a @ (b if b_kn else b.T)
     if bias is not None:
         c = np.maximum(c + _d(bias)[None, :], 0.0)
@@ -176,11 +177,13 @@ def mma_attention(q, k, v, scale, causal=False, bias=None):
     return ((e / e.sum(-1, keepdims=True)) @ v).astype(f32)
 
 
-def _tf32(x):
+def _tf32(x, trunc=False):
     """Round float32 values to tf32: keep the top 10 mantissa bits, round to
-    nearest with ties away from zero (PTX cvt.rna.tf32.f32)."""
+    nearest with ties away from zero (PTX cvt.rna.tf32.f32); ``trunc``: drop
+    the low 13 bits instead (a tensor core reading raw float32 operands as
+    tf32 takes their top 19 bits)."""
     u = np.asarray(x, f32).view(np.uint32).astype(np.uint64)
-    u = ((u + 0x1000) & 0xFFFFE000).astype(np.uint32)
+    u = ((u if trunc else u + 0x1000) & 0xFFFFE000).astype(np.uint32)
     return u.view(f32).astype(np.float64)
 
 

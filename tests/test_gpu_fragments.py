@@ -66,14 +66,18 @@ def test_mma_attention(kw):
 @pytest.mark.parametrize("kw", [dict(), dict(layout="sw128_mn", BN=128), dict(layout="none"),
                                 dict(pipelined=True), dict(warpgroups=2, BN=128),
                                 dict(dtype="f16", M=128, N=64, K=64), dict(a_regs=True),
-                                dict(a_regs=True, warpgroups=2, BN=128, layout="sw128_mn")],
+                                dict(a_regs=True, warpgroups=2, BN=128, layout="sw128_mn"),
+                                dict(dtype="tf32"), dict(dtype="tf32", layout="none")],
                          ids=["sw128", "sw128_mn", "no_swizzle", "pipelined", "two_warpgroups",
-                              "f16_aligned", "a_in_registers", "a_in_registers_wg2_mn"])
+                              "f16_aligned", "a_in_registers", "a_in_registers_wg2_mn",
+                              "tf32_sw128", "tf32_no_swizzle"])
 def test_wgmma_matmul(kw):
     """The warpgroup statements on tcgen05: M = 64 accumulators in tensor
     memory read back into the warps' C fragments, K-major and MN-major
     128-byte-swizzled and unswizzled descriptors, a commit per slab with
     WgmmaWait(1) over two slab buffers, two warpgroups a CTA (their own
     accumulator columns and barriers), the A operand from registers (staged
-    through the unswizzled K-major slot), ragged 200 x 136 x 200 by default."""
+    through the unswizzled K-major slot), tf32 operands (m64nNk8: raw float32
+    read as tf32, against an oracle that truncates them the same way),
+    ragged 200 x 136 x 200 by default."""
     _run(synth.wgmma_matmul(**kw))
