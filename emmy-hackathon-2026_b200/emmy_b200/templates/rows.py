@@ -48,6 +48,13 @@ from .common import (Chain, TemplateMismatch, accum_identity, addr_of, dtype_nam
 
 RESIDENT_MAX = 64      # values per thread kept in registers across passes
 BATCH = 4              # vectors per buffer in flight in the streaming loop
+# a launch of fewer CTAs than the B200 has SMs (the open problems' one-CTA
+# sums and means) is bound by DRAM round trips per thread, not by bandwidth;
+# ptxas keeps only a few register loads of a batch in flight (it places each
+# load next to its use), so these launches stage each batch through shared
+# memory with cp.async instead -- every copy of a batch in flight at once --
+# in at most this many bytes of static shared memory
+SMALL_LAUNCH_STAGE = 32 * 1024
 
 
 def _lit(e, v=None):
@@ -504,7 +511,17 @@ class RowsTemplate:
         of BATCH vectors per buffer, all loads of a batch issued first."""
         k = self.k
         J = self.J
-        nb, rem = divmod(J, BATCH)
+        batch = BATCH
+        self.stage = None
+        if prod(self.ctx.grid) < 148 and len(elem1) + len(col1) == 1:
+            per = self.B * self.V * 4                  # bytes a vector of every thread
+            batch = max(1, min(J, SMALL_LAUNCH_STAGE // per))
+            if batch > BATCH and self.V * 4 % 16 == 0:
+                k.decl(f".shared .align 16 .b8 __emmy_stage[{batch * per}];")
+                self.stage = batch
+            else:
+                batch = BATCH
+        nb, rem = divmod(J, batch)
         jreg = k.reg("r")
         k(f"mov.u32 {jreg}, {self.col0};")
         step = self.B * self.V
@@ -513,8 +530,8 @@ class RowsTemplate:
             k(f"mov.u32 {cnt}, 0;")
             top = k.label("ROWS_BATCH")
             k.mark(top)
-            self._batch(chain, env, elem1, col1, jreg, BATCH, step)
-            k(f"add.s32 {jreg}, {jreg}, {BATCH * step};")
+            self._batch(chain, env, elem1, col1, jreg, batch, step)
+            k(f"add.s32 {jreg}, {jreg}, {batch * step};")
             k(f"add.s32 {cnt}, {cnt}, 1;")
             p = k.reg("p")
             k(f"setp.lt.s32 {p}, {cnt}, {nb};")
@@ -532,13 +549,45 @@ class RowsTemplate:
                 c = k.reg("r")
                 k(f"add.s32 {c}, {jreg}, {u * step};")
                 cols.append(c)
-        vecs = {b: [ld_global_f32(k, self._vec_addr(b, c, "elem"), self.V, hint=".L1::no_allocate")
-                    for c in cols] for b in elem1}
-        cvecs = {b: [ld_global_f32(k, self._vec_addr(b, c, "col"), self.V) for c in cols]
-                 for b in col1}
+        if self.stage is not None:
+            vecs = {b: self._staged_vectors(b, cols, "elem") for b in elem1}
+            cvecs = {b: self._staged_vectors(b, cols, "col") for b in col1}
+        else:
+            vecs = {b: [ld_global_f32(k, self._vec_addr(b, c, "elem"), self.V,
+                                      hint=".L1::no_allocate") for c in cols] for b in elem1}
+            cvecs = {b: [ld_global_f32(k, self._vec_addr(b, c, "col"), self.V) for c in cols]
+                     for b in col1}
         for u in range(n):
             for ln in range(self.V):
                 self._run_elem(chain, env, self.loop1.body, vecs, cvecs, u, ln)
+
+    def _staged_vectors(self, buf, cols, what):
+        """The batch's vectors of ``buf`` through shared memory: 16-byte
+        ``cp.async`` copies of every vector issued first (this thread's own
+        slots: vector u at u * B * V * 4 + tid * V * 4 bytes), one commit and
+        wait, then the vectors read back -- each thread reads only what it
+        copied, so no barrier is needed; the next batch's copies are issued
+        after these reads."""
+        k = self.k
+        base = k.reg("r")
+        k(f"mov.u32 {base}, __emmy_stage;")
+        mine = k.reg("r")
+        k(f"mad.lo.u32 {mine}, {self.tid}, {self.V * 4}, {base};")
+        per = self.B * self.V * 4
+        for u, c in enumerate(cols):
+            ga = self._vec_addr(buf, c, what)
+            for h in range(self.V * 4 // 16):
+                k(f"cp.async.cg.shared.global [{mine}+{u * per + 16 * h}], [{ga}+{16 * h}], 16;")
+        k("cp.async.commit_group;")
+        k("cp.async.wait_group 0;")
+        out = []
+        for u in range(len(cols)):
+            regs = k.regs("f", self.V)
+            for h in range(self.V // 4):
+                k(f"ld.shared.v4.f32 {{{', '.join(regs[4 * h:4 * h + 4])}}}, "
+                  f"[{mine}+{u * per + 16 * h}];")
+            out.append(regs)
+        return out
 
     def _combine(self, chain, env):
         """Warp butterfly with the IR's combine statements, then the per-warp
