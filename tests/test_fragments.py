@@ -128,3 +128,31 @@ def test_fragment_layouts_cover_the_tile_once(role, kk, cls, rows, cols):
             assert (row, col) not in seen, ((row, col), seen.get((row, col)), (lane, reg, half))
             seen[(row, col)] = (lane, reg, half)
     assert len(seen) == rows * cols
+
+
+def _body_edit(g, old, new):
+    node = next(n for n in g["nodes"].values() if n["op"] == "KernelOp")
+    body = node["op_fields"]["body"][0]
+    assert old in body, old
+    node["op_fields"]["body"][0] = body.replace(old, new, 1)
+
+
+@pytest.mark.parametrize("old,new,msg", [
+    ("RegFragment(name='fa', role='a', shape='m16n8k16'",
+     "RegFragment(name='fa', role='a', shape='m16n8k32'", "shape"),
+    ("count=2, nregs=4)", "count=2, nregs=3)", "registers"),
+    ("MmaSyncPtx(c_frag='acc[0]', a_frag='fa[0]', b_frag='fb[0]'",
+     "MmaSyncPtx(c_frag='acc[0]', a_frag='fb[0]', b_frag='fa[0]'", "operands"),
+    ("LdmatrixLoad(frag='fa[0]'", "LdmatrixLoad(frag='nope[0]'", "before its RegFragment"),
+    ("volta_interleaved=False", "volta_interleaved=True", "volta_interleaved"),
+], ids=["shape", "nregs", "roles", "undeclared", "volta"])
+def test_fragment_misuse_is_exit_1(tmp_path, old, new, msg):
+    """Fragment statements this lowering cannot honour -- an mma shape it
+    has no layout for, a register count that contradicts the shape, A and B
+    swapped, a fragment used before its declaration, Volta-interleaved
+    stores -- exit 1 with ``unsupported construct`` and the reason."""
+    g, m = synth.mma_matmul().build()
+    _body_edit(g, old, new)
+    r = _cli(tmp_path, g, m)
+    assert r.returncode == 1 and r.stderr.startswith("unsupported construct:"), r.stderr
+    assert msg in r.stderr, r.stderr
