@@ -207,8 +207,50 @@ def _make_class(name: str, module: str, fields: tuple[str, ...]):
     return cls
 
 
-NODE_CLASSES: dict[str, type] = {n: _make_class(n, m, f) for n, (m, f) in _SCHEMA.items()}
-globals().update(NODE_CLASSES)
+class _NodeClasses(dict):
+    """name -> IR class, each made the first time it is asked for (an IR
+    names only a few of the vocabulary's classes; making all of them costs
+    a one-kernel ``compile.py`` run tens of milliseconds).  ``in`` and
+    iteration see the whole vocabulary."""
+
+    def __missing__(self, name):
+        if name not in _SCHEMA:
+            raise KeyError(name)
+        m, f = _SCHEMA[name]
+        cls = self[name] = _make_class(name, m, f)
+        return cls
+
+    def get(self, name, default=None):
+        return self[name] if name in _SCHEMA else default
+
+    def __contains__(self, name):
+        return name in _SCHEMA
+
+    def __iter__(self):
+        return iter(_SCHEMA)
+
+    def keys(self):
+        return list(_SCHEMA)
+
+    def items(self):
+        return [(n, self[n]) for n in _SCHEMA]
+
+    def values(self):
+        return [self[n] for n in _SCHEMA]
+
+    def __len__(self):
+        return len(_SCHEMA)
+
+
+NODE_CLASSES: dict[str, type] = _NodeClasses()
+
+
+def __getattr__(name):
+    """``ir.Tile``, ``from .ir import Var`` and the like: the class, made on
+    first use."""
+    if name in _SCHEMA:
+        return NODE_CLASSES[name]
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
 
 STMT_KINDS = frozenset(n for n, (m, _) in _SCHEMA.items() if m == _STMT_MODULE)
 EXPR_KINDS = frozenset(n for n, (m, _) in _SCHEMA.items() if m == _EXPR_MODULE)
