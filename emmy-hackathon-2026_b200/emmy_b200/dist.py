@@ -76,10 +76,11 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
 # 256-row bands of A and C for matmul (B replicated), (batch, head) pairs for
 # attention -- none of them exchanges data -- and for the full sum whole CTA
 # slices (131,072 elements each, one CTA of the one-GPU launch; a shard of
-# fewer than 1024 slices runs each on 2, 4, ... CTAs), whose per-rank
-# partial sums are finished by one all-reduce.
+# fewer than 4096 slices runs each on 2, 4, ... CTAs), whose per-rank
+# partial sums are finished by one all-reduce.  (The 8-GPU shard, 2^25
+# elements: 25.0 us a step at 1024 CTAs, 23.0 at 4096, one GPU, graph replays.)
 SUM_SLICE = 268_435_456 // 2048
-SUM_MIN_CTAS = 1024
+SUM_MIN_CTAS = 4096
 SHARDED = {
     "vector_add": ("elements", 1_048_576 // 2048, 2048),
     "full_sum": ("slices", 2048, SUM_SLICE),
@@ -104,8 +105,8 @@ def shard_kwargs(name: str, rank: int, world: int) -> dict:
         return {"n": k * unit}
     if dim == "slices":
         # a shard of few slices splits each over several CTAs (a power of
-        # two, so the slice divides evenly), keeping at least 1024 CTAs in
-        # the launch: 256 one-slice CTAs on 148 SMs leave HBM idle
+        # two, so the slice divides evenly), keeping at least SUM_MIN_CTAS
+        # CTAs in the launch: 256 one-slice CTAs on 148 SMs leave HBM idle
         split = 1 << max(0, (SUM_MIN_CTAS // max(k, 1)).bit_length() - 1)
         return {"n": k * unit, "ctas": k * split}
     if dim == "M":

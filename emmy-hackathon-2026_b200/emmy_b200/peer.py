@@ -133,9 +133,9 @@ FUSED_PARAMS = [("peer_table", "u64"), ("peer_local", "u64"), ("peer_rank", "u32
 def emit_fused_finish(k, sum_addr: str, ncta: int, status: str, done_sym: str) -> None:
     """The cross-GPU finish inside the split full-sum kernel itself, emitted
     after thread 0 of a CTA has added the CTA's partial into ``sum_addr`` (a
-    global address register): a release fence and one atomic on the
-    module's completion counter ``done_sym`` find the launch's last CTA,
-    which (after an acquire fence) reads the rank's complete partial, resets
+    global address register): one acquire-release atomic on the module's
+    completion counter ``done_sym`` finds the launch's last CTA, which reads
+    the rank's complete partial, resets
     the counter for the next launch, and runs the exchange of the
     single-thread ``emmy_peer_sum`` kernel -- its partial packed with the
     epoch into every rank's slot (``st.release.sys``), its own slots polled
@@ -146,12 +146,12 @@ def emit_fused_finish(k, sum_addr: str, ncta: int, status: str, done_sym: str) -
     the last."""
     done = k.label("PEER_DONE")
     old = k.reg("r")
-    k("fence.acq_rel.gpu;")
-    k(f"atom.global.add.u32 {old}, [{done_sym}], 1;")
+    # the count is an acquire-release RMW: it publishes this CTA's partial
+    # (added just before) and, in the last CTA, sees every other CTA's
+    k(f"atom.acq_rel.gpu.global.add.u32 {old}, [{done_sym}], 1;")
     p = k.reg("p")
     k(f"setp.ne.u32 {p}, {old}, {ncta - 1};")
     k(f"@{p} bra {done};")
-    k("fence.acq_rel.gpu;")
     part = k.reg("f")
     k(f"ld.relaxed.gpu.global.f32 {part}, [{sum_addr}];")
     k(f"st.relaxed.gpu.global.u32 [{done_sym}], 0;")
