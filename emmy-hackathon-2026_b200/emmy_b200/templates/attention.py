@@ -160,7 +160,10 @@ class AttentionTemplate:
     # K/V shared-memory traffic halve.  Correct, and slower at D = 128 (933
     # against 1178 TFLOP/s): a trace shows each tile's MMA chain shorter
     # but the two tiles' softmax passes in phase, contending for the MUFU
-    # (3,200 cycles a pass instead of 1,750), a 4,570-cycle block period
+    # (3,200 cycles a pass instead of 1,750), a 4,570-cycle block period.
+    # At D = 64 pairs run the split-P form (each CTA 32 columns of every V
+    # block in 64-byte swizzled boxes; S_FREE and P_READY count both CTAs'
+    # softmax warps): correct, and slower too (557 against 743 TFLOP/s)
     PAIR = {64: False, 128: False}
     # two-tile CTAs run persistent: the first WORKERS CTAs loop over the
     # (batch, head, 256-row) units and every other CTA returns at once; with
@@ -264,8 +267,8 @@ class AttentionTemplate:
         self.SK, self.SV = (n + 1) // 2, n // 2
         self.split_p = bool(cls.SPLIT_P.get(D, False)) and self.NT * (128 + 64 + D) <= 512
         # (a CTA's half of a V block is D/2 columns: whole 64-column boxes)
-        self.pair = (bool(cls.PAIR.get(D, False)) and not self.split_p and self.NT == 2
-                     and D % 128 == 0 and (S // 256) % 2 == 0 and tuple(ctx.grid[1:]) == (1, 1))
+        self.pair = (bool(cls.PAIR.get(D, False)) and self.NT == 2
+                     and D % 64 == 0 and (S // 256) % 2 == 0 and tuple(ctx.grid[1:]) == (1, 1))
         if self.pair:
             # K and V stages hold half a block each: twice as many fit
             n = min(12, avail // (TB // 2))
@@ -310,10 +313,15 @@ class AttentionTemplate:
             k.decl(f".global .align 32 .b8 __emmy_part[{2 * RU_ * 256 * (D + 2) * 4}];")
             k.decl(f".global .align 4 .u32 __emmy_pairs[{RU_}];")
         rows = self.B * self.H * S
+        # a pair's V half is D/2 columns: 64-column boxes (128-byte rows,
+        # 128-byte swizzle), or at D = 64 one 32-column box (64-byte rows,
+        # 64-byte swizzle)
+        VBOX = min(64, D // 2) if pair else 64
         for nm, buf in (("tmapQ", self.q), ("tmapK", self.k), ("tmapV", self.v)):
             bk = 64 if pair and nm == "tmapK" else 128
+            bw, sw = (VBOX, 3 if VBOX == 64 else 2) if nm == "tmapV" else (64, 3)
             k.directive(f"tmap {nm} buf={buf} dtype=9 dims={D},{rows} strides={D * 2} "
-                        f"box=64,{bk} swizzle=3")
+                        f"box={bw},{bk} swizzle={sw}")
         k.comment(f"emmy-b200 template: tcgen05 flash attention B={self.B} H={self.H} S={S} "
                   f"D={D}, {NT} query tile(s) per CTA")
         obase = k.param_ptr(self.out)
@@ -413,7 +421,8 @@ class AttentionTemplate:
         k(f"@!{p0} bra {skip};")
         for slot in range(NSLOT):
             if split:
-                cnt = 4 * NT if slot in (P_READY, S_FREE) else 1
+                # pair: the leader's counts both CTAs' softmax warps
+                cnt = (8 if pair else 4) * NT if slot in (P_READY, S_FREE) else 1
             else:
                 # pair: the leader's P_READY counts both CTAs' softmax warps
                 cnt = (8 if pair else 4) if P_READY <= slot < P_READY + NT else 1
@@ -486,6 +495,8 @@ class AttentionTemplate:
             k(f"and.b32 {ph_}, {ph_}, 1;")
             return st_, ph_
 
+        # the leader's waits on barriers the peer CTA's warps arrive on
+        csem = ".acquire.cluster" if pair else ""
         if pair:
             cmask = k.reg("h")
             k(f"mov.b16 {cmask}, 3;")
@@ -599,10 +610,10 @@ class AttentionTemplate:
                 # all 128 keys of the block, this CTA's D/2 columns
                 c0 = k.reg("r")
                 k(f"mul.lo.u32 {c0}, {rank}, {D // 2};")
-                for i in range(NBX // 2):
+                for i in range((D // 2) // VBOX):
                     ci = k.reg("r")
-                    k(f"add.u32 {ci}, {c0}, {64 * i};")
-                    k(f"{cpy} [{dst}+{i * 16384}], [{tmap}, {{{ci}, {kr}}}], [{fbt}];")
+                    k(f"add.u32 {ci}, {c0}, {VBOX * i};")
+                    k(f"{cpy} [{dst}+{i * 128 * VBOX * 2}], [{tmap}, {{{ci}, {kr}}}], [{fbt}];")
             else:
                 for i in range(NBX):
                     k(f"{cpy} [{dst}+{i * 16384}], [{tmap}, {{{64 * i}, {kr}}}], [{fbt}];")
@@ -634,7 +645,10 @@ class AttentionTemplate:
         ipv = k.reg("r")
         k(f"mov.u32 {ipv}, {idesc_mma(MM, D, True)};")
         hiK = _desc_hi(16, 1024)
-        hiV = _desc_hi(16384, 1024)
+        # V: MN-major, 128 keys x VBOX columns a box; 16 key rows a K step
+        VROW = VBOX * 2                               # bytes of a V box row
+        hiV = (_desc_hi(16384, 1024) if VROW == 128 else
+               _desc_hi(128 * VROW, 8 * VROW, 4))     # 64-byte swizzle (layout 4)
         ptrue = k.reg("p")
         k(f"setp.eq.u32 {ptrue}, 0, 0;")
         pfalse = k.reg("p")
@@ -678,7 +692,7 @@ class AttentionTemplate:
                 a = k.reg("r")
                 k(f"add.u32 {a}, {p_tm[t]}, {8 * kk};")  # 16 bf16 = 8 TMEM columns
                 bd = k.reg("rd")
-                k(f"add.s64 {bd}, {dv}, {kk * 128};")   # +16 key rows * 128 B
+                k(f"add.s64 {bd}, {dv}, {kk * VROW};")  # +16 key rows (16-byte units)
                 k(f"tcgen05.mma.{cg}.kind::f16 [{o_tm[t]}], [{a}], {bd}, {ipv}, "
                   f"{pacc if kk == 0 else ptrue};")
 
@@ -717,7 +731,7 @@ class AttentionTemplate:
             spar0 = k.reg("r")
             k(f"sub.u32 {spar0}, {j}, 1;")
             k(f"and.b32 {spar0}, {spar0}, 1;")
-            wait(k, bar(S_FREE), spar0, status, 2, end_mma)
+            wait(k, bar(S_FREE), spar0, status, 2, end_mma, csem)
             k("tcgen05.fence::after_thread_sync;")
             k.mark(sfirst)
         for t in range(NT):
@@ -778,7 +792,7 @@ class AttentionTemplate:
                 k(f"add.u32 {jn}, {j}, 1;")
                 dk, kst = k_ready(jn)
                 k.comment(f"@trace 9 {jn}")
-                wait(k, bar(S_FREE), par, status, 2, end_mma)
+                wait(k, bar(S_FREE), par, status, 2, end_mma, csem)
                 k("tcgen05.fence::after_thread_sync;")
                 for t in range(NT):
                     issue_qk(t, dk, jn, False)
@@ -791,7 +805,7 @@ class AttentionTemplate:
             k(f"mad.lo.u32 {vad}, {vst}, {TBV}, {vring};")
             dv = GemmTemplate._desc(k, vad, hiV)
             k(f"setp.ne.u32 {pacc}, {j}, {g0};")
-            wait(k, bar(P_READY), par, status, 2, end_mma)
+            wait(k, bar(P_READY), par, status, 2, end_mma, csem)
             k.comment(f"@trace 1 {j}")
             k("tcgen05.fence::after_thread_sync;")
             for t in range(NT):
@@ -949,10 +963,15 @@ class AttentionTemplate:
                 k(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{orow_tm}+{32 * c}], "
                   f"{{{', '.join(ov)}}};")
 
+        lsfree = None
         if pair:
-            # the P_READY the leader's issuing thread waits on
+            # the P_READY (and, with split P, S_FREE) the leader's issuing
+            # thread waits on
             lpready = k.reg("r")
             k(f"mapa.shared::cluster.u32 {lpready}, {pready}, 0;")
+            if split:
+                lsfree = k.reg("r")
+                k(f"mapa.shared::cluster.u32 {lsfree}, {sfree}, 0;")
 
         def p_ready_arrive():
             """This warp's P (and O) stores are complete: one arrival per warp
@@ -981,6 +1000,7 @@ class AttentionTemplate:
                 ld32=ld32, wait_ld=wait_ld, st16=st16, rescale_o=rescale_o,
                 p_ready_arrive=p_ready_arrive, row_sum=row_sum, max_into=max_into, sc=sc,
                 sc2=sc2, cst=cst, poly=poly, m=m, lsum=lsum, j=j, top3=top3, sfree=sfree,
+                lsfree=lsfree,
                 fin=fin, pl0=pl0, g0=g0, gend=gend, R=R, status=status, fail=soft_teardown,
                 wait=wait))
         else:
@@ -1212,7 +1232,12 @@ class AttentionTemplate:
         e["wait_ld"]()
         k("tcgen05.fence::before_thread_sync;")
         k("bar.warp.sync 0xffffffff;")
-        k(f"@{e['pl0']} mbarrier.arrive.shared::cta.b64 _, [{e['sfree']}];")
+        if e.get("lsfree"):
+            # a pair: on the leader's S_FREE, released to the cluster
+            k(f"@{e['pl0']} mbarrier.arrive.release.cluster.shared::cluster.b64 _, "
+              f"[{e['lsfree']}];")
+        else:
+            k(f"@{e['pl0']} mbarrier.arrive.shared::cta.b64 _, [{e['sfree']}];")
         k.comment(f"@trace 12 {j}")
         # row max: eight partial maxima (3-input max), then folded
         mx = [k.reg("f") for _ in range(8)]

@@ -112,6 +112,25 @@ def test_attention_cta_pairs(kw, ramp, monkeypatch):
     _run(p, transform=_key_ramp if ramp else None)
 
 
+@pytest.mark.parametrize("kw", [dict(B=1, H=2, S=512, D=64), dict(B=2, H=1, S=1024, D=64)],
+                         ids=["d64_s512", "d64_s1024"])
+@pytest.mark.parametrize("ramp", [False, True], ids=["plain", "growing"])
+def test_attention_cta_pairs_split_p(kw, ramp, monkeypatch):
+    """d=64 with split P on CTA pairs: the leader issues the M=256 products
+    of both CTAs' tiles, each CTA holds 64 keys of every K block and 32
+    columns of every V block (64-byte swizzled boxes), S_FREE and P_READY
+    count both CTAs' softmax warps (the follower's arriving remotely) and
+    S_FULL / DONE are committed to both CTAs: the same oracle bounds."""
+    from emmy_b200.compiler import compile_graph
+    from emmy_b200.templates import attention
+    monkeypatch.setattr(attention.AttentionTemplate, "PAIR", {64: True, 128: False})
+    p = synth.attention(**kw)
+    g, m = p.build()
+    t = compile_graph(g, m).template
+    assert t.pair and t.split_p
+    _run(p, transform=_key_ramp if ramp else None)
+
+
 # persistent launches: 148 worker CTAs loop over (batch, head, 256-row) units
 UNIT_CASES = [dict(B=1, H=40, S=1024, D=128), dict(B=1, H=40, S=1024, D=64),
               dict(B=1, H=80, S=1024, D=128), dict(B=1, H=80, S=1024, D=64),
