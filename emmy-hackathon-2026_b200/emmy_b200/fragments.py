@@ -62,6 +62,10 @@ fixes the forms below, and the IRs in ``synth`` (``mma_matmul``,
   ``results[0]``, converted to the buffer's type (``red.add`` when atomic);
   into shared memory it takes the same ``swizzle``.
 
+``LdmatrixLoad.staged`` and ``FragmentApply.in_place`` are accepted and change
+nothing: the source buffer's memory space decides how a fragment is loaded,
+and an applied fragment's registers are always updated where they are.
+
 Not lowered (exit 1, ``unsupported construct``): ``BlockScaleLoad`` and the
 block-scaled ``MmaSyncPtx`` (``sfa_frag`` / ``sfb_frag``) -- block-scaled
 ``mma.sync`` is an sm_120a instruction, sm_100a scales only through
