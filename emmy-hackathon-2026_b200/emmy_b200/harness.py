@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import ctypes
 import json
+import os
 import re
 from pathlib import Path
 
@@ -247,11 +248,22 @@ def from_device(t, dt: str) -> np.ndarray:
     return a
 
 
+GUARD_BYTE = 0xA5      # fill of the guard regions around guarded buffers
+
+
 class Buffers:
-    """Device buffers for every meta argument of a kernel (torch-allocated)."""
+    """Device buffers for every meta argument of a kernel (torch-allocated).
+
+    With ``guard`` > 0 (bytes, a multiple of 512 so the data keeps torch's
+    alignment) every buffer sits between two guard regions of that size
+    filled with ``GUARD_BYTE``, and a copy of every input is kept:
+    ``check_guards`` then reports any byte a launch wrote outside an output's
+    extent or into an input -- the memory-safety check that stands in for
+    compute-sanitizer, which is closed on the GPU pool (the reference runs
+    its fixtures under memcheck, ``tools/harness/sanitizer.py:9-30``)."""
 
     def __init__(self, kern: CompiledKernel, inputs: dict | None = None, folder=None,
-                 device="cuda"):
+                 device="cuda", guard: int = 0):
         import torch
         self.kern = kern
         self.t = {}
@@ -267,6 +279,39 @@ class Buffers:
             else:
                 host = inputs[name] if name in inputs else materialize(a, folder)
                 self.t[name] = to_device(np.asarray(host).reshape(-1), dt, device)
+        self.guard = int(guard)
+        self._raw, self._inputs0 = {}, {}
+        if self.guard:
+            assert self.guard % 512 == 0, "guard regions keep 512-byte alignment"
+            for name, t in list(self.t.items()):
+                nb = t.numel() * t.element_size()
+                raw = torch.full((2 * self.guard + nb,), GUARD_BYTE, dtype=torch.uint8,
+                                 device=t.device)
+                raw[self.guard:self.guard + nb].copy_(t.view(torch.uint8))
+                self._raw[name] = raw
+                self.t[name] = raw[self.guard:self.guard + nb].view(t.dtype)
+                if not self.args[name].get("output"):
+                    self._inputs0[name] = raw[self.guard:self.guard + nb].clone()
+
+    def check_guards(self) -> list:
+        """Every violation of a guarded buffer as (argument, where, first
+        offending byte offset, bytes changed): ``where`` is "before" or
+        "after" for a guard region (offset counted from the region's start)
+        and "input" for a changed input byte.  Empty when nothing was
+        written out of place."""
+        out = []
+        g = self.guard
+        for name, raw in self._raw.items():
+            nb = raw.numel() - 2 * g
+            for where, region in (("before", raw[:g]), ("after", raw[g + nb:])):
+                bad = (region != GUARD_BYTE).nonzero()
+                if bad.numel():
+                    out.append((name, where, int(bad[0, 0]), int(bad.shape[0])))
+            if name in self._inputs0:
+                bad = (raw[g:g + nb] != self._inputs0[name]).nonzero()
+                if bad.numel():
+                    out.append((name, "input", int(bad[0, 0]), int(bad.shape[0])))
+        return out
 
     @classmethod
     def random(cls, kern: CompiledKernel, seed: int = 0, device="cuda") -> "Buffers":
@@ -321,18 +366,48 @@ class Buffers:
         return res
 
 
+class GuardViolation(RuntimeError):
+    """A launch wrote outside its outputs' extents or into an input."""
+
+
+def guard_bytes() -> int:
+    """Guard-region size for ``run`` from ``EMMY_GUARD_BYTES`` (0: none).
+    The test suite sets it, so every launch it makes through ``run`` is
+    checked for out-of-place writes (the role of the reference's
+    ``EMMY_SANITIZER``, ``tools/harness/sanitizer.py:19``, which runs the
+    launch under compute-sanitizer's memcheck)."""
+    v = os.environ.get("EMMY_GUARD_BYTES", "").strip()
+    return int(v) if v else 0
+
+
 def run(graph_dict: dict, meta: dict, inputs: dict | None = None, folder=None,
         device="cuda", kern: CompiledKernel | None = None):
-    """Compile + launch once; returns ({output: ndarray}, CompiledKernel)."""
+    """Compile + launch once; returns ({output: ndarray}, CompiledKernel).
+    Under ``EMMY_GUARD_BYTES`` the buffers are guarded and a launch that
+    wrote out of place raises ``GuardViolation``."""
+    kern = kern or CompiledKernel(graph_dict, meta)
+    outs, kern, bad = run_guarded(graph_dict, meta, inputs, folder, guard_bytes(), kern, device)
+    if bad:
+        raise GuardViolation(f"{kern.ctx.entry}: bytes written out of place "
+                             f"(argument, where, first offset, count): {bad}")
+    return outs, kern
+
+
+def run_guarded(graph_dict: dict, meta: dict, inputs: dict | None = None, folder=None,
+                guard: int = 1 << 16, kern: CompiledKernel | None = None, device="cuda"):
+    """Compile + launch once with every buffer between guard regions of
+    ``guard`` bytes (0: plain buffers): returns ({output: ndarray},
+    CompiledKernel, violations) -- the violations as
+    ``Buffers.check_guards`` lists them, read after the launch."""
     import torch
     kern = kern or CompiledKernel(graph_dict, meta)
-    bufs = Buffers(kern, inputs, folder, device)
+    bufs = Buffers(kern, inputs, folder, device, guard=guard)
     stream = torch.cuda.current_stream().cuda_stream
     for z, nb in bufs.zero_list():
         native.check(native.lib().emmy_memset_async(z, 0, nb, stream))
     kern.launch(bufs.ptrs(), stream)
     torch.cuda.synchronize()
-    return bufs.outputs(), kern
+    return bufs.outputs(), kern, bufs.check_guards()
 
 
 def load_problem(folder) -> tuple[dict, dict]:

@@ -15,6 +15,11 @@ FIXTURES = sorted(p for p in (GOLDEN / "fixtures").iterdir() if p.is_dir())
 # the reference checkout (only the tests that regenerate or compare against it
 # use it): EMMY_REFERENCE_ROOT, else a "reference" folder beside this repository
 REFERENCE = Path(os.environ.get("EMMY_REFERENCE_ROOT") or REPO.parent / "reference")
+# every launch the tests make through harness.run gets 64 KiB guard regions
+# around each buffer and fails on a byte written out of place (an output's
+# neighbourhood or an input): the memory-safety check in place of
+# compute-sanitizer, which is closed on the GPU pool
+os.environ.setdefault("EMMY_GUARD_BYTES", str(64 * 1024))
 
 
 def pytest_configure(config):
