@@ -293,6 +293,13 @@ class GemmSmallTemplate:
     # 8.7 / 6.7, mm_rect2 64: 8.6 / 6.7, mm128 1536: 10.8 / 8.7, m01 and
     # mm512 2048: 21.0 / 98.8
     MIN_MACS_PER_THREAD = 2048
+    # by operand mode: CTAs of two or more warps issue the MMAs from a warp
+    # of their own (the others only stage), else thread 0 stages and issues.
+    # Measured on one B200 (same process, alternating, outputs checked):
+    # 3xTF32, whose slab holds three products a k step, m01 21.0-21.8 ->
+    # 18.8 us and the meta-only BASELINE fp32 matmul 7.76 -> 7.48 ms; bf16,
+    # bound by staging, 4.97 -> 5.17 ms with one warp fewer staging
+    DEDICATED_ISSUER = {"tf32x3": True, "bf16": False}
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -567,8 +574,15 @@ class GemmSmallTemplate:
         k(f"setp.eq.u32 {p0}, {tid}, 0;")
         skip = k.label("SKIP_INIT")
         k(f"@!{p0} bra {skip};")
+        # a CTA of two or more warps gives its last warp to the MMA issue:
+        # the others stage slabs and arrive on the buffer's STAGED barrier
+        # (one arrival a thread), so no staging thread waits for an issue
+        dedicated = self.DEDICATED_ISSUER.get(self.mode, False) and T >= 64
+        T_st = T - 32 if dedicated else T
         for b in range(self.nbuf):
             k(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * b}], 1;")
+            if dedicated:
+                k(f"mbarrier.init.shared::cta.b64 [{bars}+{32 + 8 * b}], {T_st};")
         k("fence.mbarrier_init.release.cluster;")
         k.mark(skip)
         pw0 = k.reg("p")
@@ -592,7 +606,7 @@ class GemmSmallTemplate:
         k(f"setp.eq.u32 {ptrue}, 0, 0;")
         wait = GemmTemplate._wait
 
-        st = Stager(k, tid, T, es, tf32)
+        st = Stager(k, tid, T_st, es, tf32)
 
         vec_a = K % CE == 0 and KC % CE == 0            # a chunk is all in or all out
 
@@ -600,7 +614,7 @@ class GemmSmallTemplate:
             """This thread's A and B chunks of slab ``slab`` (k from k0 + slab*KB)."""
             kb = k.reg("r")
             k(f"mad.lo.u32 {kb}, {slab}, {KB}, {k0};")
-            na = -(-BM * 8 // T)
+            na = -(-BM * 8 // T_st)              # A chunks a staging thread holds
             a = st.fetch("K", kb, r0, BM, M, abase, K, kend, vec_a, into and into[:na])
             b = st.fetch("T", kb, n0, BN, N, bbase, N, kend, False, into and into[na:])
             return a + b, na
@@ -616,10 +630,10 @@ class GemmSmallTemplate:
             st.put(chunks[na:], bb, self.sb)
             k("fence.proxy.async.shared::cta;")
 
-        def mma(slab, buf, nsteps):
-            """Thread 0: the MMAs of one staged slab, then a commit."""
+        def mma(slab, buf, nsteps, issuer=p0):
+            """Thread ``issuer``: the MMAs of one staged slab, then a commit."""
             sk = k.label("NO_MMA")
-            k(f"@!{p0} bra {sk};")
+            k(f"@!{issuer} bra {sk};")
             k("tcgen05.fence::after_thread_sync;")
             base = k.reg("r")
             k(f"mad.lo.u32 {base}, {buf}, {self.buf}, {sm};")
@@ -668,35 +682,100 @@ class GemmSmallTemplate:
         nslab = -(-KC // KB)
         s = k.reg("r")
         bufr = k.reg("r")
-        k(f"mov.u32 {s}, 0;")
-        chunks = fetch(s)
-        top = k.label("SLAB")
-        k.mark(top)
-        k(f"rem.u32 {bufr}, {s}, {self.nbuf};")
-        pw = k.reg("p")
-        k(f"setp.ge.u32 {pw}, {s}, {self.nbuf};")
-        skw = k.label("NO_WAIT")
-        k(f"@!{pw} bra {skw};")
-        prev = k.reg("r")
-        k(f"sub.u32 {prev}, {s}, {self.nbuf};")
-        wait_slab(prev)                       # the buffer's previous MMAs are done
-        k.mark(skw)
-        put(chunks, bufr)
-        k("bar.sync 0;")
-        nxt = k.reg("r")
-        k(f"add.u32 {nxt}, {s}, 1;")
-        pn = k.reg("p")
-        k(f"setp.lt.u32 {pn}, {nxt}, {nslab};")
-        skf = k.label("NO_FETCH")
-        k(f"@!{pn} bra {skf};")
-        fetch(nxt, chunks[0])                 # in flight while the MMAs run
-        k.mark(skf)
-        mma(s, bufr, KB // KMMA)
-        k(f"mov.u32 {s}, {nxt};")
-        k(f"@{pn} bra {top};")
-        last = k.reg("r")
-        k(f"mov.u32 {last}, {nslab - 1};")
-        wait_slab(last)                       # MMAs complete in order: all done
+        if dedicated:
+            after = k.label("STAGED_ALL")
+            pmw = k.reg("p")                      # the MMA warp
+            k(f"setp.eq.u32 {pmw}, {warp}, {T // 32 - 1};")
+            mloop = k.label("MMA_WARP")
+            k(f"@{pmw} bra {mloop};")
+            # staging warps: slab s into buffer s % nbuf once the MMAs that
+            # read the buffer's previous slab are done, then one arrival a
+            # thread on the buffer's STAGED barrier; the next slab's loads
+            # are in flight in registers meanwhile
+            k(f"mov.u32 {s}, 0;")
+            chunks = fetch(s)
+            top = k.label("SLAB")
+            k.mark(top)
+            k(f"rem.u32 {bufr}, {s}, {self.nbuf};")
+            pw = k.reg("p")
+            k(f"setp.ge.u32 {pw}, {s}, {self.nbuf};")
+            skw = k.label("NO_WAIT")
+            k(f"@!{pw} bra {skw};")
+            prev = k.reg("r")
+            k(f"sub.u32 {prev}, {s}, {self.nbuf};")
+            wait_slab(prev)                       # the buffer's previous MMAs are done
+            k.mark(skw)
+            put(chunks, bufr)                     # ends with the async-proxy fence
+            sbar = k.reg("r")
+            k(f"mad.lo.u32 {sbar}, {bufr}, 8, {bars};")
+            k(f"mbarrier.arrive.shared::cta.b64 _, [{sbar}+32];")
+            nxt = k.reg("r")
+            k(f"add.u32 {nxt}, {s}, 1;")
+            pn = k.reg("p")
+            k(f"setp.lt.u32 {pn}, {nxt}, {nslab};")
+            skf = k.label("NO_FETCH")
+            k(f"@!{pn} bra {skf};")
+            fetch(nxt, chunks[0])
+            k.mark(skf)
+            k(f"mov.u32 {s}, {nxt};")
+            k(f"@{pn} bra {top};")
+            k(f"bra {after};")
+            # the MMA warp's lane 0: slab s once its buffer is staged
+            k.mark(mloop)
+            pl0 = k.reg("p")
+            k(f"setp.eq.u32 {pl0}, {lane}, 0;")
+            k(f"@!{pl0} bra {after};")
+            k(f"mov.u32 {s}, 0;")
+            mtop = k.label("MMA_SLAB")
+            k.mark(mtop)
+            k(f"rem.u32 {bufr}, {s}, {self.nbuf};")
+            sbar2 = k.reg("r")
+            k(f"mad.lo.u32 {sbar2}, {bufr}, 8, {bars};")
+            k(f"add.u32 {sbar2}, {sbar2}, 32;")
+            sph = k.reg("r")
+            k(f"div.u32 {sph}, {s}, {self.nbuf};")
+            k(f"and.b32 {sph}, {sph}, 1;")
+            wait(k, sbar2, sph, status, 2, teardown)
+            mma(s, bufr, KB // KMMA, issuer=ptrue)
+            k(f"add.u32 {s}, {s}, 1;")
+            pm = k.reg("p")
+            k(f"setp.lt.u32 {pm}, {s}, {nslab};")
+            k(f"@{pm} bra {mtop};")
+            k.mark(after)
+            last = k.reg("r")
+            k(f"mov.u32 {last}, {nslab - 1};")
+            wait_slab(last)                       # MMAs complete in order: all done
+            k("bar.warp.sync 0xffffffff;")
+        else:
+            k(f"mov.u32 {s}, 0;")
+            chunks = fetch(s)
+            top = k.label("SLAB")
+            k.mark(top)
+            k(f"rem.u32 {bufr}, {s}, {self.nbuf};")
+            pw = k.reg("p")
+            k(f"setp.ge.u32 {pw}, {s}, {self.nbuf};")
+            skw = k.label("NO_WAIT")
+            k(f"@!{pw} bra {skw};")
+            prev = k.reg("r")
+            k(f"sub.u32 {prev}, {s}, {self.nbuf};")
+            wait_slab(prev)                       # the buffer's previous MMAs are done
+            k.mark(skw)
+            put(chunks, bufr)
+            k("bar.sync 0;")
+            nxt = k.reg("r")
+            k(f"add.u32 {nxt}, {s}, 1;")
+            pn = k.reg("p")
+            k(f"setp.lt.u32 {pn}, {nxt}, {nslab};")
+            skf = k.label("NO_FETCH")
+            k(f"@!{pn} bra {skf};")
+            fetch(nxt, chunks[0])                 # in flight while the MMAs run
+            k.mark(skf)
+            mma(s, bufr, KB // KMMA)
+            k(f"mov.u32 {s}, {nxt};")
+            k(f"@{pn} bra {top};")
+            last = k.reg("r")
+            k(f"mov.u32 {last}, {nslab - 1};")
+            wait_slab(last)                       # MMAs complete in order: all done
         k("tcgen05.fence::after_thread_sync;")
         # ---------------- epilogue ----------------
         warps = T // 32
