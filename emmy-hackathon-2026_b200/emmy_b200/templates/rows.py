@@ -55,6 +55,16 @@ BATCH = 4              # vectors per buffer in flight in the streaming loop
 # memory with cp.async instead -- every copy of a batch in flight at once --
 # in at most this many bytes of static shared memory
 SMALL_LAUNCH_STAGE = 32 * 1024
+# ... or, for a single row-contiguous input, through a ring of this many
+# shared-memory stages of at most BULK_STAGE bytes each, each filled by one
+# 1-D bulk copy (``cp.async.bulk``, the copy engine: no tensor map, no
+# multicast) that one thread issues as soon as every thread has read the
+# stage's previous batch: several batches stream in while the threads
+# reduce an earlier one (0 stages: the cp.async form).  Measured on one B200
+# (same process, alternating, outputs checked): r02 (256 KiB, one CTA)
+# 10.6 -> 8.75 us; r03 (128 KiB) 8.58 -> 8.54 us
+BULK_STAGES = 3
+BULK_STAGE = 15 * 1024
 
 
 def _lit(e, v=None):
@@ -513,6 +523,14 @@ class RowsTemplate:
         J = self.J
         batch = BATCH
         self.stage = None
+        per = self.B * self.V * 4
+        if (prod(self.ctx.grid) < 148 and len(elem1) + len(col1) == 1 and BULK_STAGES
+                and self.V * 4 % 16 == 0 and self.L * 4 % 16 == 0
+                and J > max(1, BULK_STAGE // per)):
+            what = "elem" if elem1 else "col"
+            self._stream_bulk(chain, env, list(elem1 or col1)[0], what,
+                              max(1, BULK_STAGE // per))
+            return
         if prod(self.ctx.grid) < 148 and len(elem1) + len(col1) == 1:
             per = self.B * self.V * 4                  # bytes a vector of every thread
             batch = max(1, min(J, SMALL_LAUNCH_STAGE // per))
@@ -538,6 +556,119 @@ class RowsTemplate:
             k(f"@{p} bra.uni {top};")
         if rem:
             self._batch(chain, env, elem1, col1, jreg, rem, step)
+
+    def _status(self):
+        """Register holding the address of ``__emmy_status`` (declared once)."""
+        k = self.k
+        if not getattr(self, "_status_declared", False) and not self.peer:
+            k.decl(".global .align 4 .u32 __emmy_status;")
+        self._status_declared = True
+        st = k.reg("rd")
+        k(f"mov.u64 {st}, __emmy_status;")
+        return st
+
+    def _wait_through(self, bar, parity, status, code):
+        """Wait for phase ``parity`` of mbarrier ``bar`` for at most WAIT_NS of
+        %globaltimer; on expiry record ``code`` in ``__emmy_status`` and go on
+        (the CTA barriers after the wait are then still reached by every
+        thread: no thread leaves the batch loop on its own)."""
+        from .gemm import WAIT_NS
+        k = self.k
+        p = k.reg("p")
+        top, ok = k.label("BW"), k.label("BW_OK")
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar}], {parity};")
+        k(f"@{p} bra {ok};")
+        t0 = k.reg("rd")
+        k(f"mov.u64 {t0}, %globaltimer;")
+        k.mark(top)
+        k(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar}], {parity};")
+        k(f"@{p} bra {ok};")
+        t1 = k.reg("rd")
+        k(f"mov.u64 {t1}, %globaltimer;")
+        k(f"sub.s64 {t1}, {t1}, {t0};")
+        q = k.reg("p")
+        k(f"setp.lt.s64 {q}, {t1}, {WAIT_NS};")
+        k(f"@{q} bra {top};")
+        k(f"st.global.u32 [{status}], {code};")
+        k.mark(ok)
+
+    def _stream_bulk(self, chain, env, buf, what, batch):
+        """Pass 1 of a small launch over one row-contiguous input (``what``:
+        "elem", the CTA's row of it, or "col", a vector every row reads): batch i
+        (``batch`` vectors of every thread, contiguous in the row) lands in
+        stage i % NST by one ``cp.async.bulk`` issued by thread 0 on the
+        stage's mbarrier (expect-tx of its bytes); every thread waits for it,
+        reads its own vectors (vector u of thread t at u * B * V * 4 +
+        t * V * 4: the row's layout, so one copy serves all threads), runs
+        the IR's element statements, and after a CTA barrier thread 0 refills
+        the stage with batch i + NST.  Batches are unrolled (a few dozen at
+        most for these launches), so stage and parity are constants."""
+        k = self.k
+        J, B, V = self.J, self.B, self.V
+        per = B * V * 4
+        sb = batch * per
+        nbt = -(-J // batch)
+        NST = min(BULK_STAGES, nbt)
+        k.decl(f".shared .align 128 .b8 __emmy_bulk[{NST * sb}];")
+        k.decl(f".shared .align 8 .b64 __emmy_bulk_full[{NST}];")
+        status = self._status()
+        stg = k.reg("r")
+        k(f"mov.u32 {stg}, __emmy_bulk;")
+        full = k.reg("r")
+        k(f"mov.u32 {full}, __emmy_bulk_full;")
+        mine = k.reg("r")
+        k(f"mad.lo.u32 {mine}, {self.tid}, {V * 4}, {stg};")
+        gb = self.base[buf]
+        if what == "elem" and self.row_off is not None:
+            g2 = k.reg("rd")
+            k(f"add.s64 {g2}, {gb}, {self.row_off};")
+            gb = g2
+        p0 = k.reg("p")
+        k(f"setp.eq.u32 {p0}, {self.tid}, 0;")
+
+        def nvec(i):
+            return min(batch, J - i * batch)
+
+        def issue(i):
+            """Thread 0: batch i into its stage (the stage's reads are done)."""
+            st_, nb_ = i % NST, nvec(i) * per
+            sk = k.label("NO_BULK")
+            k(f"@!{p0} bra {sk};")
+            k("fence.proxy.async.shared::cta;")
+            k(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{full}+{8 * st_}], {nb_};")
+            src = k.reg("rd")
+            k(f"add.s64 {src}, {gb}, {i * sb};")
+            k(f"cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+              f"[{stg}+{st_ * sb}], [{src}], {nb_}, [{full}+{8 * st_}];")
+            k.mark(sk)
+
+        sk0 = k.label("NO_INIT")
+        k(f"@!{p0} bra {sk0};")
+        for st_ in range(NST):
+            k(f"mbarrier.init.shared::cta.b64 [{full}+{8 * st_}], 1;")
+        k("fence.mbarrier_init.release.cluster;")
+        k.mark(sk0)
+        k("bar.sync 0;")
+        for i in range(NST):
+            issue(i)
+        for i in range(nbt):
+            st_ = i % NST
+            self._wait_through(f"{full}+{8 * st_}", (i // NST) & 1, status, 10)
+            vecs = []
+            for u in range(nvec(i)):
+                regs = k.regs("f", V)
+                for h in range(V // 4):
+                    k(f"ld.shared.v4.f32 {{{', '.join(regs[4 * h:4 * h + 4])}}}, "
+                      f"[{mine}+{st_ * sb + u * per + 16 * h}];")
+                vecs.append(regs)
+            if i + NST < nbt:
+                k("bar.sync 0;")              # every thread has read the stage
+                issue(i + NST)
+            for u in range(nvec(i)):
+                for ln in range(V):
+                    self._run_elem(chain, env, self.loop1.body,
+                                   {buf: vecs} if what == "elem" else {},
+                                   {buf: vecs} if what == "col" else {}, u, ln)
 
     def _batch(self, chain, env, elem1, col1, jreg, n, step):
         k = self.k
