@@ -674,7 +674,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                 categories[nm] = {kk: r[kk] for kk in (
                     "template", "ms_median", "GB/s", "TFLOP/s", "frac", "peak_basis",
                     "reference_ptx_ms", "speedup_vs_reference_ptx", "reference_ptx_check",
-                    "check", "back_to_back", "wide_launch") if kk in r}
+                    "check", "back_to_back", "rotated", "wide_launch") if kk in r}
         cat_clocks = cclk.summary()
         if rank == 0:
             for nm in CATEGORY_CASES:
