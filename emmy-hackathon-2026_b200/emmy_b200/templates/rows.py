@@ -526,7 +526,7 @@ class RowsTemplate:
         per = self.B * self.V * 4
         if (prod(self.ctx.grid) < 148 and len(elem1) + len(col1) == 1 and BULK_STAGES
                 and self.V * 4 % 16 == 0 and self.L * 4 % 16 == 0
-                and J > max(1, BULK_STAGE // per)):
+                and per <= BULK_STAGE and J > BULK_STAGE // per):
             what = "elem" if elem1 else "col"
             self._stream_bulk(chain, env, list(elem1 or col1)[0], what,
                               max(1, BULK_STAGE // per))
