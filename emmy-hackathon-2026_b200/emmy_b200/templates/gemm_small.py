@@ -273,13 +273,62 @@ class Stager:
             out.append((row, ch, live, w))
         return out
 
+    def fetch_mn(self, kb, n0, cols, bound, ptr, ld, kend, into=None):
+        """This thread's 16-byte chunks of one slab of a [k][n] operand kept
+        MN-major (bf16 only): a chunk is 8 consecutive n of one k row, one
+        vector load, coalesced across the threads; in shared memory, 64-column
+        blocks of ``KB`` k rows x 128 bytes (block b at b * KB * 128), the
+        chunk cc of k row r of an 8-row atom at chunk cc ^ (r % 8) -- the
+        128-byte-swizzle MN-major layout.  ``bound`` (the matrix width) is a
+        multiple of 8, so a chunk is all in or all out.  Returns chunks as
+        (byte offset, None, live, words)."""
+        k, T = self.k, self.T
+        per_row = cols // 8
+        out = []
+        slots = iter(into or [])
+        for c in range(-(-self.KB * per_row // T)):
+            prev = next(slots, None)
+            idx = k.reg("r")
+            k(f"add.u32 {idx}, {self.tid}, {c * T};")
+            live = prev[2] if prev else k.reg("p")
+            k(f"setp.lt.u32 {live}, {idx}, {self.KB * per_row};")
+            kr, nc = k.reg("r"), k.reg("r")
+            k(f"div.u32 {kr}, {idx}, {per_row};")
+            k(f"rem.u32 {nc}, {idx}, {per_row};")
+            off = prev[0] if prev else k.reg("r")
+            blk = k.reg("r")
+            k(f"shr.u32 {blk}, {nc}, 3;")              # 64-column block
+            cc = k.reg("r")
+            k(f"and.b32 {cc}, {nc}, 7;")
+            k(f"mul.lo.u32 {off}, {blk}, {self.KB * 128};")
+            x = self.swz(kr, cc)
+            k(f"add.u32 {off}, {off}, {x};")
+            gk = k.reg("r")
+            k(f"add.u32 {gk}, {kb}, {kr};")
+            gn = k.reg("r")
+            k(f"mad.lo.u32 {gn}, {nc}, 8, {n0};")
+            ok = k.reg("p")
+            k(f"setp.lt.and.u32 {ok}, {gk}, {kend}, {live};")
+            k(f"setp.lt.and.u32 {ok}, {gn}, {bound}, {ok};")
+            w = prev[3] if prev else k.regs("r", 4)
+            for r_ in w:
+                k(f"mov.b32 {r_}, 0;")
+            ei = k.reg("r")
+            k(f"mad.lo.u32 {ei}, {gk}, {ld}, {gn};")
+            a = k.reg("rd")
+            k(f"mul.wide.u32 {a}, {ei}, {self.es};")
+            k(f"add.s64 {a}, {a}, {ptr};")
+            k(f"@{ok} ld.global.nc.v4.b32 {{{', '.join(w)}}}, [{a}];")
+            out.append((off, None, live, w))
+        return out
+
     def put(self, chunks, dst, lo_off):
         """Store fetched chunks at buffer ``dst`` (a register)."""
         k = self.k
         for row, ch, live, w in chunks:
             sk = k.label("NO_CHUNK")
             k(f"@!{live} bra {sk};")
-            self.store_chunk(dst, self.swz(row, ch), w, lo_off)
+            self.store_chunk(dst, row if ch is None else self.swz(row, ch), w, lo_off)
             k.mark(sk)
 
 
@@ -300,6 +349,11 @@ class GemmSmallTemplate:
     # 18.8 us and the meta-only BASELINE fp32 matmul 7.76 -> 7.48 ms; bf16,
     # bound by staging, 4.97 -> 5.17 ms with one warp fewer staging
     DEDICATED_ISSUER = {"tf32x3": True, "bf16": False}
+    # bf16 B staged MN-major (16-byte loads along N, no transposition).
+    # Measured on one B200 (same process, alternating, outputs checked): the
+    # meta-only BASELINE bf16 matmul 4.96-4.98 -> 2.89-2.90 ms (221 -> 380
+    # TFLOP/s)
+    BF16_B_MN = True
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -492,6 +546,10 @@ class GemmSmallTemplate:
         self.CE = 16 // self.es                 # elements per 16-byte chunk
         self.KB = 128 // self.es                # k per 128-byte swizzle row (one slab)
         self.BNp = -(-BN // 16) * 16
+        # bf16 B kept MN-major (as stored: 16-byte loads along N, no
+        # transposition) when the tile is whole 64-column blocks and N a
+        # multiple of 8; otherwise transposed into K-major chunks
+        self.b_mn = (cls.BF16_B_MN and mode == "bf16" and self.BNp % 64 == 0 and N % 8 == 0)
         half = 2 if mode == "tf32x3" else 1     # raw + low parts
         # per slab buffer: A (the tile's rows, in whole 8-row atoms) | A_lo |
         # B (BNp rows) | B_lo, 128 bytes a row.  The MMA's A descriptor spans
@@ -600,8 +658,10 @@ class GemmSmallTemplate:
         k(f"ld.shared.u32 {tmem}, [{tslot}];")
         teardown = k.label("TEARDOWN")
         idesc = k.reg("r")
-        k(f"mov.u32 {idesc}, {idesc_mma(128, BNp, False, tf32)};")
+        bmn = self.b_mn
+        k(f"mov.u32 {idesc}, {idesc_mma(128, BNp, bmn, tf32)};")
         hi = _desc_hi(16, 1024)
+        hiB = _desc_hi(KB * 128, 1024) if bmn else hi
         ptrue = k.reg("p")
         k(f"setp.eq.u32 {ptrue}, 0, 0;")
         wait = GemmTemplate._wait
@@ -616,7 +676,10 @@ class GemmSmallTemplate:
             k(f"mad.lo.u32 {kb}, {slab}, {KB}, {k0};")
             na = -(-BM * 8 // T_st)              # A chunks a staging thread holds
             a = st.fetch("K", kb, r0, BM, M, abase, K, kend, vec_a, into and into[:na])
-            b = st.fetch("T", kb, n0, BN, N, bbase, N, kend, False, into and into[na:])
+            if bmn:
+                b = st.fetch_mn(kb, n0, BNp, N, bbase, N, kend, into and into[na:])
+            else:
+                b = st.fetch("T", kb, n0, BN, N, bbase, N, kend, False, into and into[na:])
             return a + b, na
 
         def put(fetched, buf):
@@ -640,7 +703,8 @@ class GemmSmallTemplate:
             da = GemmTemplate._desc(k, base, hi)
             bb = k.reg("r")
             k(f"add.u32 {bb}, {base}, {self.sa * (2 if tf32 else 1)};")
-            db = GemmTemplate._desc(k, bb, hi)
+            db = GemmTemplate._desc(k, bb, hiB)
+            bstep = 128 if bmn else 2               # a K step: 16 k rows MN-major, 32 bytes K-major
             if tf32:
                 la = k.reg("r")
                 k(f"add.u32 {la}, {base}, {self.sa};")
@@ -657,7 +721,7 @@ class GemmSmallTemplate:
                     ax = k.reg("rd")
                     k(f"add.s64 {ax}, {x}, {2 * st};")
                     by = k.reg("rd")
-                    k(f"add.s64 {by}, {y}, {2 * st};")
+                    k(f"add.s64 {by}, {y}, {bstep * st};")
                     kind_ = "tf32" if tf32 else "f16"
                     k(f"tcgen05.mma.cta_group::1.kind::{kind_} [{tmem}], {ax}, {by}, {idesc}, "
                       f"{pacc if first else ptrue};")
