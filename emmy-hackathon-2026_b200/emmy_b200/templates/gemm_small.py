@@ -275,15 +275,18 @@ class Stager:
 
     def fetch_mn(self, kb, n0, cols, bound, ptr, ld, kend, into=None):
         """This thread's 16-byte chunks of one slab of a [k][n] operand kept
-        MN-major (bf16 only): a chunk is 8 consecutive n of one k row, one
-        vector load, coalesced across the threads; in shared memory, 64-column
-        blocks of ``KB`` k rows x 128 bytes (block b at b * KB * 128), the
-        chunk cc of k row r of an 8-row atom at chunk cc ^ (r % 8) -- the
-        128-byte-swizzle MN-major layout.  ``bound`` (the matrix width) is a
-        multiple of 8, so a chunk is all in or all out.  Returns chunks as
-        (byte offset, None, live, words)."""
+        MN-major: a chunk is ``CE`` consecutive n of one k row, one vector
+        load, coalesced across the threads; in shared memory, blocks of 128
+        bytes of n (64 bf16 or 32 fp32 columns) x ``KB`` k rows (block b at
+        b * KB * 128, k row r at r * 128 in it) -- the 128-byte-swizzle
+        MN-major layouts: bf16 with 16-byte atoms (chunk cc of row r at
+        chunk cc ^ (r % 8)), fp32 (tf32) with 32-byte atoms (the 32-byte
+        atom cc / 2 of row r at atom (cc / 2) ^ (r % 4), its half cc % 2
+        kept).  ``bound`` (the matrix width) is a multiple of ``CE``, so a
+        chunk is all in or all out.  Returns chunks as (byte offset, None,
+        live, words)."""
         k, T = self.k, self.T
-        per_row = cols // 8
+        per_row = cols // self.CE
         out = []
         slots = iter(into or [])
         for c in range(-(-self.KB * per_row // T)):
@@ -301,12 +304,24 @@ class Stager:
             cc = k.reg("r")
             k(f"and.b32 {cc}, {nc}, 7;")
             k(f"mul.lo.u32 {off}, {blk}, {self.KB * 128};")
-            x = self.swz(kr, cc)
+            if self.es == 2:
+                x = self.swz(kr, cc)
+            else:
+                x = k.reg("r")                      # 32-byte atoms, 4-row pattern
+                r4 = k.reg("r")
+                k(f"and.b32 {r4}, {kr}, 3;")
+                k(f"shr.u32 {x}, {cc}, 1;")
+                k(f"xor.b32 {x}, {x}, {r4};")
+                k(f"shl.b32 {x}, {x}, 5;")
+                h = k.reg("r")
+                k(f"and.b32 {h}, {cc}, 1;")
+                k(f"mad.lo.u32 {x}, {h}, 16, {x};")
+                k(f"mad.lo.u32 {x}, {kr}, 128, {x};")
             k(f"add.u32 {off}, {off}, {x};")
             gk = k.reg("r")
             k(f"add.u32 {gk}, {kb}, {kr};")
             gn = k.reg("r")
-            k(f"mad.lo.u32 {gn}, {nc}, 8, {n0};")
+            k(f"mad.lo.u32 {gn}, {nc}, {self.CE}, {n0};")
             ok = k.reg("p")
             k(f"setp.lt.and.u32 {ok}, {gk}, {kend}, {live};")
             k(f"setp.lt.and.u32 {ok}, {gn}, {bound}, {ok};")
@@ -354,6 +369,10 @@ class GemmSmallTemplate:
     # meta-only BASELINE bf16 matmul 4.96-4.98 -> 2.89-2.90 ms (221 -> 380
     # TFLOP/s)
     BF16_B_MN = True
+    # fp32 B staged MN-major too (the tf32 MN-major layout: 32-byte atoms).
+    # Measured the same way: the meta-only BASELINE fp32 matmul 7.46 ->
+    # 6.16 ms (147 -> 178 TFLOP/s); m01 18.9 us either way (issue-bound)
+    TF32_B_MN = True
 
     # ------------------------------------------------------------------ match
     @classmethod
@@ -549,7 +568,8 @@ class GemmSmallTemplate:
         # bf16 B kept MN-major (as stored: 16-byte loads along N, no
         # transposition) when the tile is whole 64-column blocks and N a
         # multiple of 8; otherwise transposed into K-major chunks
-        self.b_mn = (cls.BF16_B_MN and mode == "bf16" and self.BNp % 64 == 0 and N % 8 == 0)
+        self.b_mn = ((cls.BF16_B_MN and mode == "bf16" and self.BNp % 64 == 0 and N % 8 == 0) or
+                     (cls.TF32_B_MN and mode == "tf32x3" and self.BNp % 32 == 0 and N % 4 == 0))
         half = 2 if mode == "tf32x3" else 1     # raw + low parts
         # per slab buffer: A (the tile's rows, in whole 8-row atoms) | A_lo |
         # B (BNp rows) | B_lo, 128 bytes a row.  The MMA's A descriptor spans
@@ -661,7 +681,8 @@ class GemmSmallTemplate:
         bmn = self.b_mn
         k(f"mov.u32 {idesc}, {idesc_mma(128, BNp, bmn, tf32)};")
         hi = _desc_hi(16, 1024)
-        hiB = _desc_hi(KB * 128, 1024) if bmn else hi
+        hiB = (hi if not bmn else _desc_hi(KB * 128, 512, 1) if tf32
+               else _desc_hi(KB * 128, 1024))
         ptrue = k.reg("p")
         k(f"setp.eq.u32 {ptrue}, 0, 0;")
         wait = GemmTemplate._wait
@@ -704,14 +725,14 @@ class GemmSmallTemplate:
             bb = k.reg("r")
             k(f"add.u32 {bb}, {base}, {self.sa * (2 if tf32 else 1)};")
             db = GemmTemplate._desc(k, bb, hiB)
-            bstep = 128 if bmn else 2               # a K step: 16 k rows MN-major, 32 bytes K-major
+            bstep = KMMA * 8 if bmn else 2          # a K step: KMMA k rows MN-major, 32 bytes K-major
             if tf32:
                 la = k.reg("r")
                 k(f"add.u32 {la}, {base}, {self.sa};")
                 dla = GemmTemplate._desc(k, la, hi)
                 lb = k.reg("r")
                 k(f"add.u32 {lb}, {base}, {2 * self.sa + self.sb};")
-                dlb = GemmTemplate._desc(k, lb, hi)
+                dlb = GemmTemplate._desc(k, lb, hiB)
             pacc = k.reg("p")
             k(f"setp.ne.u32 {pacc}, {slab}, 0;")
             first = True
