@@ -369,6 +369,12 @@ class GemmSmallTemplate:
     # meta-only BASELINE bf16 matmul 4.96-4.98 -> 2.89-2.90 ms (221 -> 380
     # TFLOP/s)
     BF16_B_MN = True
+    # bf16 operands copied global -> shared by cp.async (16-byte chunks,
+    # zero-filled past the matrix) into a ring of 3-4 buffers, up to two
+    # slabs in flight beyond the one being multiplied, no register staging.
+    # Measured the same way: the meta-only BASELINE bf16 matmul 2.885-2.888
+    # -> 2.042-2.044 ms (381 -> 538 TFLOP/s)
+    ASYNC_BF16 = True
     # fp32 B staged MN-major too (the tf32 MN-major layout: 32-byte atoms).
     # Measured the same way: the meta-only BASELINE fp32 matmul 7.46 ->
     # 6.16 ms (147 -> 178 TFLOP/s); m01 18.9 us either way (issue-bound)
@@ -587,7 +593,19 @@ class GemmSmallTemplate:
         # static shared memory adds to the launch's dynamic bytes: a launcher
         # raises the per-CTA limit above 48 KiB only for dynamic sizes above it
         cap = SMEM_LIMIT if avail > 48 * 1024 else 48 * 1024
-        for nbuf in (2, 1):
+        # bf16 with both operands in 16-byte chunks (A rows along K, B MN-major)
+        # copies global -> shared with cp.async, so a slab needs no registers
+        # and up to three slabs are in flight (four buffers)
+        self.async_ = bool(cls.ASYNC_BF16 and mode == "bf16" and self.b_mn
+                           and K % 8 == 0 and KC % 8 == 0)
+        if self.async_:
+            # the ring needs three buffers or more (a buffer is refilled one
+            # slab after its MMAs are issued), all in dynamic shared memory
+            fit = [n for n in (4, 3) if avail >= need(n)]
+            self.async_ = bool(fit)
+            if fit:
+                self.nbuf, self.dynamic = fit[0], True
+        for nbuf in (() if self.async_ else (2, 1)):
             if avail >= need(nbuf):
                 self.nbuf, self.dynamic = nbuf, True
                 break
@@ -595,7 +613,8 @@ class GemmSmallTemplate:
                 self.nbuf, self.dynamic = nbuf, False
                 break
         else:
-            raise TemplateMismatch("shared memory for one slab")
+            if not self.async_:
+                raise TemplateMismatch("shared memory for one slab")
         self.smem_need = need(self.nbuf)
         return self
 
@@ -645,7 +664,7 @@ class GemmSmallTemplate:
         bars = k.reg("r")
         k(f"add.u32 {bars}, {sm}, {self.smem_need - 1024 - 64};")
         tslot = k.reg("r")
-        k(f"add.u32 {tslot}, {bars}, 16;")
+        k(f"add.u32 {tslot}, {bars}, 48;")
         status = k.reg("rd")
         k(f"mov.u64 {status}, __emmy_status;")
         p0 = k.reg("p")
@@ -767,7 +786,119 @@ class GemmSmallTemplate:
         nslab = -(-KC // KB)
         s = k.reg("r")
         bufr = k.reg("r")
-        if dedicated:
+
+        def copy_async(slab, buf):
+            """cp.async of slab ``slab`` (a register) into buffer ``buf`` (a
+            register): this thread's 16-byte chunks of A (rows along K) and of
+            B (MN-major), zero-filled outside the matrix and the K range."""
+            base = k.reg("r")
+            k(f"mad.lo.u32 {base}, {buf}, {self.buf}, {sm};")
+            kb = k.reg("r")
+            k(f"mad.lo.u32 {kb}, {slab}, {KB}, {k0};")
+
+            def chunk(live, ok, dst, gidx, ptr):
+                src = k.reg("rd")
+                k(f"mul.wide.u32 {src}, {gidx}, {es};")
+                k(f"add.s64 {src}, {src}, {ptr};")
+                k(f"selp.b64 {src}, {src}, {ptr}, {ok};")      # no read when zero-filled
+                sz = k.reg("r")
+                k(f"selp.u32 {sz}, 16, 0, {ok};")
+                k(f"@{live} cp.async.cg.shared.global [{dst}], [{src}], 16, {sz};")
+            for c in range(-(-BM * 8 // T)):
+                idx = k.reg("r")
+                k(f"add.u32 {idx}, {tid}, {c * T};")
+                live = k.reg("p")
+                k(f"setp.lt.u32 {live}, {idx}, {BM * 8};")
+                row, ch = k.reg("r"), k.reg("r")
+                k(f"shr.u32 {row}, {idx}, 3;")
+                k(f"and.b32 {ch}, {idx}, 7;")
+                g = k.reg("r")
+                k(f"add.u32 {g}, {r0}, {row};")
+                kk = k.reg("r")
+                k(f"mad.lo.u32 {kk}, {ch}, {CE}, {kb};")
+                ok = k.reg("p")
+                k(f"setp.lt.and.u32 {ok}, {g}, {M}, {live};")
+                k(f"setp.lt.and.u32 {ok}, {kk}, {kend}, {ok};")
+                dst = k.reg("r")
+                k(f"add.u32 {dst}, {base}, {st.swz(row, ch)};")
+                gi = k.reg("r")
+                k(f"mad.lo.u32 {gi}, {g}, {K}, {kk};")
+                chunk(live, ok, dst, gi, abase)
+            per_row = BNp // CE
+            for c in range(-(-KB * per_row // T)):
+                idx = k.reg("r")
+                k(f"add.u32 {idx}, {tid}, {c * T};")
+                live = k.reg("p")
+                k(f"setp.lt.u32 {live}, {idx}, {KB * per_row};")
+                kr, nc = k.reg("r"), k.reg("r")
+                k(f"div.u32 {kr}, {idx}, {per_row};")
+                k(f"rem.u32 {nc}, {idx}, {per_row};")
+                blk, cc = k.reg("r"), k.reg("r")
+                k(f"shr.u32 {blk}, {nc}, 3;")
+                k(f"and.b32 {cc}, {nc}, 7;")
+                dst = k.reg("r")
+                k(f"mad.lo.u32 {dst}, {blk}, {KB * 128}, {base};")
+                k(f"add.u32 {dst}, {dst}, {st.swz(kr, cc)};")
+                k(f"add.u32 {dst}, {dst}, {self.sa};")
+                gk, gn = k.reg("r"), k.reg("r")
+                k(f"add.u32 {gk}, {kb}, {kr};")
+                k(f"mad.lo.u32 {gn}, {nc}, {CE}, {n0};")
+                ok = k.reg("p")
+                k(f"setp.lt.and.u32 {ok}, {gk}, {kend}, {live};")
+                k(f"setp.lt.and.u32 {ok}, {gn}, {N}, {ok};")
+                gi = k.reg("r")
+                k(f"mad.lo.u32 {gi}, {gk}, {N}, {gn};")
+                chunk(live, ok, dst, gi, bbase)
+
+        if self.async_:
+            # one commit group per prologue slab and one per iteration (empty
+            # when nothing is refilled): slab t >= D is copied in iteration
+            # t - D + 1, so when iteration s waits for slab s, at most D - 2
+            # newer groups may still be pending (D - 1 for the prologue's
+            # slabs: waiting for D - 2 is stricter, never wrong)
+            D = self.nbuf
+            for i in range(D):
+                if i < nslab:
+                    ri = k.reg("r")
+                    k(f"mov.u32 {ri}, {i};")
+                    copy_async(ri, ri)
+                k("cp.async.commit_group;")
+            k(f"mov.u32 {s}, 0;")
+            top = k.label("SLAB")
+            k.mark(top)
+            k(f"cp.async.wait_group {D - 2};")
+            k("fence.proxy.async.shared::cta;")
+            k("bar.sync 0;")
+            k(f"rem.u32 {bufr}, {s}, {D};")
+            mma(s, bufr, KB // KMMA)
+            # refill the buffer of slab s-1 (its MMAs were issued a slab ago)
+            # with slab s-1+D
+            skr = k.label("NO_REFILL")
+            pr = k.reg("p")
+            k(f"setp.eq.u32 {pr}, {s}, 0;")
+            k(f"@{pr} bra {skr};")
+            prv = k.reg("r")
+            k(f"sub.u32 {prv}, {s}, 1;")
+            nx = k.reg("r")
+            k(f"add.u32 {nx}, {prv}, {D};")
+            pn2 = k.reg("p")
+            k(f"setp.ge.u32 {pn2}, {nx}, {nslab};")
+            k(f"@{pn2} bra {skr};")
+            wait_slab(prv)
+            pb = k.reg("r")
+            k(f"rem.u32 {pb}, {prv}, {D};")
+            copy_async(nx, pb)
+            k.mark(skr)
+            k("cp.async.commit_group;")
+            k(f"add.u32 {s}, {s}, 1;")
+            pl = k.reg("p")
+            k(f"setp.lt.u32 {pl}, {s}, {nslab};")
+            k(f"@{pl} bra {top};")
+            last = k.reg("r")
+            k(f"mov.u32 {last}, {nslab - 1};")
+            wait_slab(last)                       # MMAs complete in order: all done
+            k("cp.async.wait_group 0;")
+        elif dedicated:
             after = k.label("STAGED_ALL")
             pmw = k.reg("p")                      # the MMA warp
             k(f"setp.eq.u32 {pmw}, {warp}, {T // 32 - 1};")
